@@ -1,0 +1,348 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 weight path of RRR (K-quant GEMV HBM GB/s; Phi-4-mini-shape
+decode tok/s). Prints ONE JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the metric's config): the four per-layer GEMVs of
+Phi-4-mini at batch 1 (QKV Q5_K 5120x3072, O Q4_K 3072x3072, gate_up Q4_K 16384x3072,
+down Q6_K 3072x8192). One step = that GEMV set over all 32 layers' weights (seeded
+synthetic blocks resident in HBM, 2.08 GB per pass, larger than the 126 MB L2, so no
+flush is needed between steps). `value` = algorithmic bytes (weights + x + y) of all
+ranks / device time (max over ranks). Under torchrun each rank runs its own copy of the
+layer stack (independent weights, no data-path collective): scaling "weak".
+Also reported: per-GEMV GB/s, the full decode step tok/s with its CUDA
+graph, the end-to-end number through the C ABI with host buffers, the roofline of the
+dominant kernel and a CPU baseline (the oracle's restatement of the reference's
+dequant + f32 dot on the host cores).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from ctypes import c_void_p
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+METRIC = "K-quant GEMV HBM GB/s (% of peak) per B200; Phi-4-mini-shape decode tok/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+            os.unlink(self.path)
+        except Exception:
+            return None
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(oracle, cfg, seconds: float = 10.0, layer_seed: int = 0):
+    """The reference path on the host cores: dequantise each weight matrix to f32 (the
+    reference's dequant_*) then a row-parallel f32 dot, over all host threads. Sample:
+    the four GEMVs of one layer, repeated for about `seconds`."""
+    import numpy as np
+    from importlib import import_module
+    phi4 = import_module("recursive-routing-racer-rs_b200.phi4")
+    threads = os.cpu_count() or 1
+    mats = []
+    for name, qt, K, N in cfg.layer_gemvs():
+        raw = oracle.fill_kquant_random(qt, N * (K // 256), phi4.tensor_seed(layer_seed, 0, name))
+        x = np.random.default_rng(1).standard_normal(K).astype(np.float32)
+        mats.append((qt, raw, x, K, N, np.empty(N * K, np.float32)))
+    nbytes = sum(raw.nbytes + 4 * K + 4 * N for _, raw, _, K, N, _ in mats)
+    t_deq = t_dot = 0.0
+    reps = 0
+    t0 = time.time()
+    while reps < 1 or (time.time() - t0 < seconds and reps < 50):
+        for qt, raw, x, K, N, scratch in mats:
+            _, td, tt = oracle.gemv_kq_baseline(qt, raw, x, K, N, threads, scratch)
+            t_deq += td
+            t_dot += tt
+        reps += 1
+    total = t_deq + t_dot
+    return {"value": round(nbytes * reps / total / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"one layer's 4 GEMVs (QKV Q5_K, O Q4_K, gate_up Q4_K, down Q6_K; "
+                      f"{nbytes / 1e6:.1f} MB algorithmic) x {reps} reps; dequant {t_deq:.2f}s + dot {t_dot:.2f}s",
+            "dequant_s": round(t_deq, 3), "dot_s": round(t_dot, 3)}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path (oracle port; the Rust reference cannot be
+    built in this image) on the host cores, same metric/config."""
+    if rank != 0:
+        return
+    import oracle
+    oracle.build()
+    from importlib import import_module
+    phi4 = import_module("recursive-routing-racer-rs_b200.phi4")
+    cfg = phi4.ModelConfig()
+    per_step = max(1.0, 60.0 / max(1, args.steps + args.warmup))
+    for _ in range(args.warmup):
+        cpu_baseline(oracle, cfg, seconds=0.0)
+    t0 = time.time()
+    vals = []
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(oracle, cfg, seconds=min(per_step, 10.0)))
+    el = time.time() - t0
+    v = round(statistics.mean(x["value"] for x in vals), 3)
+    cb = dict(vals[-1])
+    cb["value"] = v
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * el / max(1, args.steps), 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "configs[1] per-layer GEMV set, batch 1 (CPU sample: one layer)",
+                                            "threads": cb["cores"]},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    rrr = importlib.import_module("recursive-routing-racer-rs_b200")
+    importlib.import_module("recursive-routing-racer-rs_b200.build").build()
+    phi4 = importlib.import_module("recursive-routing-racer-rs_b200.phi4")
+    ffi = rrr.ffi
+    L = ffi.lib()
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    ctx = ffi.Context(local_rank)
+    stream = torch.cuda.current_stream()
+    sp = c_void_p(stream.cuda_stream)
+    cfg = phi4.ModelConfig()
+    model = phi4.SyntheticPhi4(ctx, cfg, seed=1000 + rank, stream=sp)
+    gemvs = cfg.layer_gemvs()
+    xs = {name: torch.randn(K * (2 if name == "down" else 1), device="cuda") for name, _, K, _ in gemvs}
+    ys = {name: torch.empty(N, device="cuda") for name, _, _, N in gemvs}
+    bytes_layer = sum(cfg.weight_bytes(q, K, N) + 4 * K + 4 * N for _, q, K, N in gemvs)
+    bytes_step = bytes_layer * cfg.n_layers
+    launches_step = 4 * cfg.n_layers
+
+    def gemv(layer, name):
+        p, qt, K, N = model.layers[layer][name]
+        return L.rrr_gemv_kq(ctx.h, qt, c_void_p(p), c_void_p(xs[name].data_ptr()),
+                             c_void_p(ys[name].data_ptr()), K, N, None, sp)
+
+    def step():
+        for l in range(cfg.n_layers):
+            for name, _, _, _ in gemvs:
+                rc = gemv(l, name)
+                if rc:
+                    ctx.check(rc)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if not dist:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------- headline: per-layer GEMV set over 32 layers
+    for _ in range(max(3, args.warmup)):
+        step()
+    clocks = Clocks(local_rank)
+    barrier()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    # ---------------- per-GEMV (same kernel, one shape at a time over 32 layers)
+    per = {}
+    for name, qt, K, N in gemvs:
+        for l in range(cfg.n_layers):
+            gemv(l, name)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(2, args.steps)
+        a.record(stream)
+        for _ in range(reps):
+            for l in range(cfg.n_layers):
+                gemv(l, name)
+        b.record(stream)
+        torch.cuda.synchronize()
+        us = 1e3 * a.elapsed_time(b) / (reps * cfg.n_layers)
+        nb = cfg.weight_bytes(qt, K, N) + 4 * K + 4 * N
+        per[name] = {"qtype": {12: "Q4_K", 13: "Q5_K", 14: "Q6_K"}[qt], "K": K, "N": N, "bytes": nb,
+                     "us_per_launch": round(us, 3), "GBps": round(nb / us / 1e3, 1)}
+    clk = clocks.stop()
+    peak, peak_src = peaks()
+    # ---------------- decode step through the CUDA graph
+    dec = phi4.Phi4Decoder(ctx, model)
+    hidden = torch.randn(cfg.d_model, device="cuda")
+    logits = torch.empty(cfg.vocab_size, device="cuda")
+    am = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for _ in range(max(3, args.warmup)):
+        dec.forward(hidden.data_ptr(), logits.data_ptr(), am.data_ptr(), True, stream)
+    barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dsteps = max(args.steps, 10)
+    d0.record(stream)
+    for _ in range(dsteps):
+        dec.forward(hidden.data_ptr(), logits.data_ptr(), am.data_ptr(), True, stream)
+    d1.record(stream)
+    barrier()
+    dms = max_over_ranks(d0.elapsed_time(d1) / dsteps)
+    dec_bytes = cfg.step_bytes()
+    decode = {"tok_s": round(1e3 / dms, 2), "ms_per_token": round(dms, 4),
+              "GBps": round(dec_bytes / dms / 1e6, 1), "bytes_per_token": dec_bytes,
+              "frac_of_peak": round(dec_bytes / dms / 1e6 / peak, 4),
+              "launches_per_token": dec.launches_per_step() + 1, "graph": True}
+    dec.close()
+    # ---------------- end to end through the C ABI with host buffers (pinned)
+    hx = {n: torch.randn(K * (2 if n == "down" else 1)).pin_memory() for n, _, K, _ in gemvs}
+    hy = {n: torch.empty(N).pin_memory() for n, _, _, N in gemvs}
+    h2d = sum(hx[n].numel() * 4 for n, _, _, _ in gemvs) * cfg.n_layers
+    d2h = sum(hy[n].numel() * 4 for n, _, _, _ in gemvs) * cfg.n_layers
+
+    def e2e_step():
+        for l in range(cfg.n_layers):
+            for name, _, _, _ in gemvs:
+                ctx.check(L.rrr_h2d(ctx.h, c_void_p(xs[name].data_ptr()), c_void_p(hx[name].data_ptr()),
+                                    hx[name].numel() * 4, sp))
+                ctx.check(gemv(l, name))
+                ctx.check(L.rrr_d2h(ctx.h, c_void_p(hy[name].data_ptr()), c_void_p(ys[name].data_ptr()),
+                                    hy[name].numel() * 4, sp))
+        ctx.check(L.rrr_sync(ctx.h, sp))
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_ms = max_over_ranks(1e3 * (time.perf_counter() - t0) / args.steps)
+    code = ctx.device_error()
+    if code:
+        raise SystemExit(f"device error flag {code}")
+    # ---------------- CPU baseline (rank 0, N = 1 only)
+    cb = None
+    if rank == 0 and world == 1:
+        import oracle
+        oracle.build()
+        cb = cpu_baseline(oracle, cfg, seconds=10.0)
+    if rank == 0:
+        gbs = bytes_step * world / ms / 1e6
+        dom = per["gate_up"]
+        line = {
+            "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 (K-quant) x f32",
+            "data": "synthetic",
+            "config": {"workload": "configs[1]: per-layer GEMV set at batch 1 (QKV Q5_K 5120x3072, O Q4_K "
+                                   "3072x3072, gate_up Q4_K 16384x3072, down Q6_K 3072x8192) over 32 layers' "
+                                   "weights per step", "bytes_per_step_per_gpu": bytes_step,
+                       "l2": "inputs larger than L2 (2.08 GB rotation per step), no flush",
+                       "parallelism": f"independent layer stacks per GPU (x{world})"},
+            "frac_of_peak": round(gbs / world / peak, 4),
+            "per_gemv": per,
+            "roofline": {"bound": "hbm", "kernel": "gemv_kq_kernel<Q4_K> (gate_up)",
+                         "achieved": dom["GBps"], "peak": peak, "unit": "GB/s",
+                         "frac": round(dom["GBps"] / peak, 4), "peak_source": peak_src,
+                         "traffic": None},
+            "decode": decode,
+            "e2e": {"value": round(bytes_step / e2e_ms / 1e6, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "rrr_h2d + rrr_gemv_kq + rrr_d2h per GEMV (pinned host buffers), one sync per step"},
+            "gpu_launches": launches_step * args.steps,
+            "clocks": clk,
+            "cpu_baseline": cb,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

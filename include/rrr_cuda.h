@@ -1,0 +1,262 @@
+/*
+ * rrr_cuda.h — C ABI of the B200 (sm_100a) weight-path kernels for Recursive Routing
+ * Racer (RRR, Peterc3-dev/recursive-routing-racer-rs).
+ *
+ * This header replaces RRR's Vulkan `ComputeEngine` (src/gpu/engine.rs:15-29) and the
+ * weight-path dispatch helpers built on it (src/model/phi4.rs:631-697, 1081-1096,
+ * src/gpu/ops.rs:65-84). A Rust host binds it with a thin `extern "C"` block; Python
+ * binds it with ctypes. Every citation below is a file:line in the reference project.
+ *
+ * Conventions (all entry points):
+ *   - Return 0 (RRR_OK) on success and a negative rrr_status on failure. Nothing panics
+ *     or throws across the ABI. rrr_last_error(ctx) returns a message for the last
+ *     failure on that context (thread-local per context use; one host thread at a time).
+ *   - Weight, activation and output pointers are DEVICE pointers unless a name says
+ *     "host". K-quant weights are raw GGUF super-blocks (Q4_K 144 B, Q5_K 176 B,
+ *     Q6_K 210 B per 256 elements), row-major: row n's K/256 blocks are contiguous at
+ *     byte offset n*(K/256)*block_bytes. No repacking (the reference's repack_q*k,
+ *     src/model/phi4.rs:278-436, is not needed).
+ *   - Kernels are asynchronous on the given `stream` (a cudaStream_t passed as void*;
+ *     NULL = the legacy default stream). The caller synchronises (rrr_sync).
+ *   - qtype uses GGUF type ids: 12 = Q4_K, 13 = Q5_K, 14 = Q6_K (phi4.rs:154-156).
+ */
+#ifndef RRR_CUDA_H
+#define RRR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RRR_ABI_VERSION 1
+
+typedef enum rrr_status {
+  RRR_OK = 0,
+  RRR_ERR_INVALID_ARG = -1,  /* null pointer, bad count, unknown name */
+  RRR_ERR_BAD_QTYPE = -2,    /* qtype not 12/13/14 */
+  RRR_ERR_BAD_SHAPE = -3,    /* K % 256 != 0, K or N out of the supported range */
+  RRR_ERR_MISALIGNED = -4,   /* pointer alignment rule violated */
+  RRR_ERR_CUDA = -5,         /* a CUDA runtime call failed */
+  RRR_ERR_NCCL = -6,         /* an NCCL call failed or NCCL is unavailable */
+  RRR_ERR_TIMEOUT = -7,      /* a bounded device-side wait gave up (kernel error flag) */
+  RRR_ERR_OOM = -8,          /* device allocation failed */
+  RRR_ERR_UNSUPPORTED = -9,  /* known operation that this build does not implement */
+  RRR_ERR_IO = -10,          /* file open / mmap / parse failure (GGUF) */
+  RRR_ERR_BUFFER_TOO_SMALL = -11 /* a buffer size given to a dispatch is too small */
+} rrr_status;
+
+enum { RRR_Q4_K = 12, RRR_Q5_K = 13, RRR_Q6_K = 14 };
+
+typedef struct rrr_ctx rrr_ctx;
+
+/* ---- context, memory, streams (replaces ComputeEngine::new / alloc_buffer /
+ *      upload / download: engine.rs:49-128, 200-229; phi4.rs:616-626) ---------------- */
+
+/* Create a context on CUDA device `device`. Fails with RRR_ERR_CUDA if no device. */
+int rrr_init(int device, rrr_ctx** out);
+/* Destroy a context (frees its internal buffers; user allocations must be freed first). */
+int rrr_destroy(rrr_ctx* ctx);
+/* Message of the last failure on this context ("" if none). ctx may be NULL: then the
+ * message of the last failure of a call that had no context (e.g. rrr_init). */
+const char* rrr_last_error(rrr_ctx* ctx);
+/* Name of a status code. */
+const char* rrr_status_string(int status);
+int rrr_abi_version(void);
+
+int rrr_alloc(rrr_ctx* ctx, size_t bytes, void** dptr);  /* 256-B aligned device memory */
+int rrr_free(rrr_ctx* ctx, void* dptr);
+int rrr_alloc_host(rrr_ctx* ctx, size_t bytes, void** hptr);  /* pinned host memory */
+int rrr_free_host(rrr_ctx* ctx, void* hptr);
+int rrr_h2d(rrr_ctx* ctx, void* dst_dev, const void* src_host, size_t bytes, void* stream);
+int rrr_d2h(rrr_ctx* ctx, void* dst_host, const void* src_dev, size_t bytes, void* stream);
+int rrr_d2d(rrr_ctx* ctx, void* dst_dev, const void* src_dev, size_t bytes, void* stream);
+int rrr_memset(rrr_ctx* ctx, void* dst_dev, int value, size_t bytes, void* stream);
+int rrr_sync(rrr_ctx* ctx, void* stream);
+/* Reads and clears the context's device error flag, which kernels set when a bounded
+ * wait gives up. Synchronises the device. *code = 0 if no kernel reported an error. */
+int rrr_check_device_error(rrr_ctx* ctx, int* code);
+/* Number of streaming multiprocessors of the context's device. */
+int rrr_device_sm_count(rrr_ctx* ctx, int* sms);
+/* Diagnostic: runs the integer tensor-core fragment-layout check the GEMV relies on
+ * (one warp, known operands); *ok = 1 when the device result is exact. No reference
+ * counterpart (the reference has no GPU self-tests). */
+int rrr_selftest_mma(rrr_ctx* ctx, int* ok);
+
+/* ---- kernel (1): fused raw-block K-quant GEMV, y = W x (+ residual) ------------------
+ * Replaces gpu_matmul_kquant / kquant_dispatch (phi4.rs:631-658, 1081-1096) and the
+ * `matmul_q{4,5,6}k` / `matmul_gpuq{4,5,6}` shaders they dispatch (push [K, N],
+ * workgroups [N,1,1]). W: N rows x K (raw blocks, 16-B aligned base), x: f32[K]
+ * (16-B aligned), y: f32[N]. residual: NULL or f32[N]; when given, y = residual + W x
+ * (the residual_add shader, phi4.rs:1028,1033, fused). y may alias residual.
+ * Supported: K % 256 == 0, 256 <= K <= 16384, N >= 1. */
+int rrr_gemv_kq(rrr_ctx* ctx, int qtype, const void* w_raw, const float* x, float* y,
+                int K, int N, const float* residual, void* stream);
+
+/* Same GEMV with the input produced in the prologue (fusions of the decode step,
+ * phi4.rs:1006-1033):
+ *   RRR_X_RMSNORM : x_in f32[K], gamma f32[K]; the GEMV input is rms_norm(x_in)*gamma
+ *                   (phi4.rs:593-599, `rmsnorm` shader slot before QKV / FFN-up).
+ *   RRR_X_SILU_GATE: x_in f32[2K] = [gate; up]; input = silu(gate) * up
+ *                   (phi4.rs:601-606, 1359-1378, `silu_gate` shader).
+ *   RRR_X_GQA_V   : x_in = qkv f32[n_q*hd + 2*n_kv*hd]; input[h*hd + d] =
+ *                   V[(h / (n_q/n_kv))*hd + d] — attention output at position 0
+ *                   (seq_len 1: softmax = 1, output = V of the head's KV group;
+ *                   `attention` push [seq_len, n_kv, heads_per_kv, head_dim],
+ *                   phi4.rs:1120). K must equal n_q*hd. */
+enum { RRR_X_PLAIN = 0, RRR_X_RMSNORM = 1, RRR_X_SILU_GATE = 2, RRR_X_GQA_V = 3 };
+typedef struct rrr_gemv_prologue {
+  int mode;            /* RRR_X_* */
+  const float* gamma;  /* RRR_X_RMSNORM */
+  float eps;           /* RRR_X_RMSNORM */
+  int n_q_heads, n_kv_heads, head_dim; /* RRR_X_GQA_V */
+} rrr_gemv_prologue;
+int rrr_gemv_kq_ex(rrr_ctx* ctx, int qtype, const void* w_raw, const float* x_in,
+                   float* y, int K, int N, const float* residual,
+                   const rrr_gemv_prologue* pro, void* stream);
+
+/* Bit-exact dequantisation of n_blocks raw blocks to f32 (n_blocks*256 values), the
+ * reference's CPU dequant_q4_k / dequant_q5_k / dequant_q6_k (phi4.rs:481-542, 444-479)
+ * on the GPU, with no FMA contraction. */
+int rrr_dequant_kq(rrr_ctx* ctx, int qtype, const void* w_raw, float* out,
+                   int64_t n_blocks, void* stream);
+
+/* ---- kernel (2): batched-token K-quant GEMM, Y[M,N] = X[M,K] W^T (f32 out) ----------
+ * Replaces the `matmul_gpuq{4,5,6}_batch` dispatches (push [K, N, M], workgroups
+ * [N, M, 1], phi4.rs:1257-1268, 1346-1357, 1380-1391). X is bf16 [M,K] row-major
+ * (uint16 bit patterns). Tensor-core path (tcgen05) for M >= 16; smaller M is routed
+ * to the GEMV kernel per token. */
+int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16_t* x_bf16,
+                        float* y, int M, int K, int N, void* stream);
+
+/* ---- kernel (3): RMSNorm, y = gamma * x / sqrt(mean(x^2) + eps), `rows` rows of d ---
+ * Replaces gpu_rmsnorm / the `rmsnorm` shader (phi4.rs:680-697, push [num_rows, d]). */
+int rrr_rmsnorm(rrr_ctx* ctx, const float* x, const float* gamma, float* y, int rows,
+                int d, float eps, void* stream);
+
+/* ---- kernel (4): F32 logits GEMV over the vocab, y[v] = sum_k W[v,k] x[k] ----------
+ * Replaces the logits `matmul_tiled` chunks (phi4.rs:866-893, 1049-1064). W is
+ * row-major [V, K] f32 (16-B aligned); the vocab is processed in chunks of chunk_rows
+ * (0 = one launch). gamma != NULL fuses the output RMSNorm (phi4.rs:1043-1047):
+ * the GEMV input is rms_norm(x)*gamma with eps. K % 4 == 0, K <= 16384. */
+int rrr_logits_f32(rrr_ctx* ctx, const float* W, const float* x, float* y, int V, int K,
+                   int chunk_rows, const float* gamma, float eps, void* stream);
+
+/* Decode glue (phi4.rs:601-610, shaders silu_gate / residual_add, phi4.rs:736-737). */
+int rrr_silu_gate(rrr_ctx* ctx, const float* gate_up, float* out, int F, void* stream);
+int rrr_residual_add(rrr_ctx* ctx, const float* a, const float* b, float* out, int n,
+                     void* stream);
+/* Greedy argmax over f32[n] (replaces the CPU scan, phi4.rs:1172-1183). First index
+ * wins on ties, NaN is never selected. out_index: device int32[1]. */
+int rrr_argmax_f32(rrr_ctx* ctx, const float* x, int n, int* out_index, void* stream);
+
+/* f32 GEMM C[M,N] = A[M,K] B[K,N] with B in the reference's transposed chunk layout
+ * ([K, N] row-major, phi4.rs:874-893); the `matmul_tiled` / `matmul_reg_tiled`
+ * shaders (push [M, K, N], ops.rs:65-84). */
+int rrr_matmul_f32(rrr_ctx* ctx, const float* A, const float* B, float* C, int M, int K,
+                   int N, void* stream);
+
+/* ---- named dispatch (replaces ComputeEngine::dispatch_by_name, engine.rs:476-554) ---
+ * `name` is a reference shader name; buffers/sizes follow its bindings and push
+ * constants its push layout:
+ *   matmul_q4k | matmul_q5k | matmul_q6k   bufs [x, W, y]            push u32[K, N]
+ *   matmul_q4k_batch | _q5k_ | _q6k_batch  bufs [X(bf16), W, Y]      push u32[K, N, M]
+ *   rmsnorm                                 bufs [x, gamma, y]        push u32[rows, d]
+ *   matmul_tiled | matmul_reg_tiled         bufs [A, B, C]            push u32[M, K, N]
+ *   silu_gate                               bufs [gate_up, out]       push u32[F]
+ *   residual_add                            bufs [a, b, out]          push u32[n]
+ * Sizes are byte sizes of each binding (checked: RRR_ERR_BUFFER_TOO_SMALL). Names of
+ * the reference's repacked-layout shaders (matmul_gpuq*) return RRR_ERR_UNSUPPORTED,
+ * as do attention / rope / rope_kv_store / kv_store (outside the weight path).
+ * The rmsnorm eps is 1e-5 (phi4.rs:111). */
+int rrr_dispatch_by_name(rrr_ctx* ctx, const char* name, void* const* buffers,
+                         const uint64_t* sizes, int n_buffers, const void* push,
+                         int push_bytes, void* stream);
+
+/* ---- prebuilt dispatch table as a CUDA graph (replaces pre_allocate_desc_set +
+ *      dispatch_batch_persistent_v2, engine.rs:244-268, 317-370; phi4.rs:969-1064) ---- */
+typedef struct rrr_batch rrr_batch;
+int rrr_batch_create(rrr_ctx* ctx, rrr_batch** out);
+/* Append one named dispatch (same arguments as rrr_dispatch_by_name, validated now). */
+int rrr_batch_add(rrr_batch* b, const char* name, void* const* buffers,
+                  const uint64_t* sizes, int n_buffers, const void* push, int push_bytes);
+/* Launch all dispatches in order on `stream` (captured into a CUDA graph on first use). */
+int rrr_batch_launch(rrr_batch* b, void* stream);
+int rrr_batch_size(rrr_batch* b, int* n);
+int rrr_batch_destroy(rrr_batch* b);
+
+/* ---- GGUF loader (replaces GGUFModel, src/model/gguf.rs:125-195) -------------------- */
+typedef struct rrr_gguf rrr_gguf;
+typedef struct rrr_gguf_tensor {
+  const char* name;
+  int n_dims;
+  uint64_t shape[4];   /* ne0 (contiguous) first */
+  uint32_t type;       /* GGML type id */
+  uint64_t offset;     /* relative to the data section */
+  uint64_t n_bytes;    /* byte size by type (gguf.rs:173-195) */
+  const void* data;    /* zero-copy pointer into the mapping */
+} rrr_gguf_tensor;
+int rrr_gguf_open(const char* path, rrr_gguf** out);
+int rrr_gguf_close(rrr_gguf* g);
+int rrr_gguf_n_tensors(rrr_gguf* g, int64_t* n);
+int rrr_gguf_tensor_at(rrr_gguf* g, int64_t index, rrr_gguf_tensor* out);
+int rrr_gguf_find_tensor(rrr_gguf* g, const char* name, rrr_gguf_tensor* out);
+/* Metadata readers (MetaValue::as_u64 / as_f32 / as_str, gguf.rs:41-62). */
+int rrr_gguf_meta_u64(rrr_gguf* g, const char* key, uint64_t* out);
+int rrr_gguf_meta_f32(rrr_gguf* g, const char* key, float* out);
+int rrr_gguf_meta_str(rrr_gguf* g, const char* key, const char** out);
+int rrr_gguf_version(rrr_gguf* g, uint32_t* version);
+int rrr_gguf_data_offset(rrr_gguf* g, uint64_t* off);
+/* Copy one tensor's raw bytes from the mapping to a new device buffer (raw, no repack;
+ * the weight upload of load_weight_gpu, phi4.rs:744-771, without repack_q*k). */
+int rrr_gguf_upload(rrr_ctx* ctx, rrr_gguf* g, const char* name, void** dptr,
+                    uint64_t* n_bytes);
+
+/* ---- Phi-4-mini-shape decode step (replaces forward_gpu, phi4.rs:1099-1196) --------
+ * One token at position 0 (attention output = V, see RRR_X_GQA_V): per layer
+ *   h += Wo . expand(V(Wqkv . rms(h)*g_attn)); h += Wdown . (silu(g) * u),
+ *   [g; u] = Wgate_up . rms(h)*g_ffn; then logits = Wout . rms(h)*g_out.
+ * All pointers are device pointers that the caller owns and keeps alive. */
+typedef struct rrr_phi4_layer {
+  const void* w_qkv;      int qkv_type;      /* [n_q*hd + 2*n_kv*hd, d] */
+  const void* w_o;        int o_type;        /* [d, n_q*hd] */
+  const void* w_gate_up;  int gate_up_type;  /* [2*ffn, d] */
+  const void* w_down;     int down_type;     /* [d, ffn] */
+  const float* attn_norm; /* f32[d] */
+  const float* ffn_norm;  /* f32[d] */
+} rrr_phi4_layer;
+typedef struct rrr_phi4_desc {
+  int d_model, n_heads, n_kv_heads, head_dim, ffn_dim, n_layers, vocab;
+  float rms_eps;
+  int logits_chunk_rows;        /* 0 = whole vocab per launch */
+  const rrr_phi4_layer* layers; /* n_layers entries (copied) */
+  const float* output_norm;     /* f32[d] */
+  const float* w_out;           /* f32 [vocab, d] row-major */
+} rrr_phi4_desc;
+typedef struct rrr_phi4 rrr_phi4;
+int rrr_phi4_create(rrr_ctx* ctx, const rrr_phi4_desc* desc, rrr_phi4** out);
+/* hidden: device f32[d], updated in place (the residual stream); logits: device
+ * f32[vocab]; argmax_out: NULL or device int32[1]. use_graph != 0 replays a CUDA graph
+ * of the step (captured on the first call for this stream and these pointers). */
+int rrr_phi4_forward(rrr_phi4* m, float* hidden, float* logits, int* argmax_out,
+                     int use_graph, void* stream);
+/* Number of kernel launches one forward issues. */
+int rrr_phi4_launches_per_step(rrr_phi4* m, int* n);
+int rrr_phi4_destroy(rrr_phi4* m);
+
+/* ---- seeded synthetic data on the device (bench / tests) --------------------------
+ * Blocks follow the distributions of the benchmark configs: d, dmin f16 ~ U[1e-4,1e-2];
+ * Q6_K scales int8 ~ U[-32,31]; all other bytes uniform. Block i depends only on
+ * (seed, i) through splitmix64, so any row range can be regenerated on the host. */
+int rrr_fill_kquant_random(rrr_ctx* ctx, int qtype, void* dst, int64_t n_blocks,
+                           uint64_t seed, void* stream);
+int rrr_fill_f32_normal(rrr_ctx* ctx, float* dst, int64_t n, float mean, float std,
+                        uint64_t seed, void* stream);
+int rrr_fill_f32_uniform(rrr_ctx* ctx, float* dst, int64_t n, float lo, float hi,
+                         uint64_t seed, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RRR_CUDA_H */

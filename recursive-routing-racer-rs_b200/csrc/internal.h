@@ -1,0 +1,53 @@
+// internal.h — host-side launch functions shared between the kernel translation units
+// and the C ABI (capi.cpp). Not part of the public interface.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/rrr_cuda.h"
+
+namespace rrr {
+
+struct LaunchEnv {
+  cudaStream_t stream;
+  int sm_count;
+  int* d_err;  // device error flag of the context
+  bool pdl;    // launch with programmatic stream serialisation
+};
+
+// Shape limits of the K-quant GEMV (checked by the C ABI before launching).
+constexpr int kGemvMaxK = 16384;
+
+cudaError_t launch_gemv_kq(const LaunchEnv& env, int qtype, const void* w, const float* x,
+                           float* y, int K, int N, const float* residual,
+                           const rrr_gemv_prologue* pro);
+// GEMV with a bf16 input vector (one token of the batched path when M < 16).
+cudaError_t launch_gemv_kq_bf16(const LaunchEnv& env, int qtype, const void* w,
+                                const uint16_t* x, float* y, int K, int N);
+cudaError_t launch_dequant_kq(const LaunchEnv& env, int qtype, const void* w, float* out,
+                              int64_t n_blocks);
+cudaError_t launch_rmsnorm(const LaunchEnv& env, const float* x, const float* gamma, float* y,
+                           int rows, int d, float eps);
+cudaError_t launch_logits_f32(const LaunchEnv& env, const float* W, const float* x, float* y,
+                              int V, int K, const float* gamma, float eps);
+cudaError_t launch_silu_gate(const LaunchEnv& env, const float* gu, float* out, int F);
+cudaError_t launch_residual_add(const LaunchEnv& env, const float* a, const float* b,
+                                float* out, int n);
+cudaError_t launch_argmax(const LaunchEnv& env, const float* x, int n, int* out_index);
+cudaError_t launch_matmul_f32(const LaunchEnv& env, const float* A, const float* B, float* C,
+                              int M, int K, int N);
+cudaError_t launch_fill_kquant(const LaunchEnv& env, int qtype, void* dst, int64_t n_blocks,
+                               uint64_t seed);
+cudaError_t launch_fill_f32(const LaunchEnv& env, float* dst, int64_t n, int normal, float a,
+                            float b, uint64_t seed);
+cudaError_t launch_bf16_to_f32_rows(const LaunchEnv& env, const uint16_t* x, float* out,
+                                    int64_t n);
+// Batched-token GEMM (tensor cores). Returns cudaErrorNotSupported when the shape is not
+// handled by the tensor-core path.
+cudaError_t launch_gemm_kq_tc(const LaunchEnv& env, int qtype, const void* w,
+                              const uint16_t* x_bf16, float* y, int M, int K, int N);
+// Self-test of the integer tensor-core fragment layout used by the GEMV (writes 1 to
+// *d_ok when the device result matches the expected product).
+cudaError_t launch_mma_selftest(const LaunchEnv& env, int* d_ok);
+
+}  // namespace rrr

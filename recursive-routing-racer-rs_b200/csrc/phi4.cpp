@@ -1,0 +1,169 @@
+// phi4.cpp — Phi-4-mini-shape decode step on the weight-path kernels (replaces
+// Phi4Model::forward_gpu, src/model/phi4.rs:1099-1196, and its 378-dispatch table,
+// phi4.rs:969-1064).
+//
+// Per layer the reference issues 11 dispatches (rmsnorm, qkv, rope_kv_store, attention,
+// o-proj, residual_add, rmsnorm, ffn_up, silu_gate, ffn_down, residual_add). Here the
+// norms, the SiLU gate, the attention output at position 0 and both residual adds are
+// fused into the four GEMVs (prologues / epilogues of rrr_gemv_kq_ex), so a layer is 4
+// launches and the step is 4*L + logits chunks (+ argmax). The whole step can be
+// captured once into a CUDA graph and replayed.
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "capi_internal.h"
+
+using namespace rrr;
+
+struct rrr_phi4 {
+  rrr_ctx* ctx = nullptr;
+  rrr_phi4_desc d{};
+  std::vector<rrr_phi4_layer> layers;
+  float* qkv = nullptr;      // f32[n_q*hd + 2*n_kv*hd]
+  float* gate_up = nullptr;  // f32[2*ffn]
+  // graph cache
+  cudaGraphExec_t exec = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaStream_t cap_stream = nullptr;
+  float* g_hidden = nullptr;
+  float* g_logits = nullptr;
+  int* g_argmax = nullptr;
+};
+
+static int phi4_issue(rrr_phi4* m, float* hidden, float* logits, int* argmax, void* stream) {
+  const rrr_phi4_desc& d = m->d;
+  rrr_ctx* ctx = m->ctx;
+  const int qkv_dim = (d.n_heads + 2 * d.n_kv_heads) * d.head_dim;
+  int rc;
+  for (int l = 0; l < d.n_layers; ++l) {
+    const rrr_phi4_layer& L = m->layers[l];
+    rrr_gemv_prologue pn{RRR_X_RMSNORM, L.attn_norm, d.rms_eps, 0, 0, 0};
+    if ((rc = rrr_gemv_kq_ex(ctx, L.qkv_type, L.w_qkv, hidden, m->qkv, d.d_model, qkv_dim, nullptr,
+                             &pn, stream)))
+      return rc;
+    rrr_gemv_prologue pv{RRR_X_GQA_V, nullptr, 0.f, d.n_heads, d.n_kv_heads, d.head_dim};
+    if ((rc = rrr_gemv_kq_ex(ctx, L.o_type, L.w_o, m->qkv, hidden, d.n_heads * d.head_dim,
+                             d.d_model, hidden, &pv, stream)))
+      return rc;
+    rrr_gemv_prologue pf{RRR_X_RMSNORM, L.ffn_norm, d.rms_eps, 0, 0, 0};
+    if ((rc = rrr_gemv_kq_ex(ctx, L.gate_up_type, L.w_gate_up, hidden, m->gate_up, d.d_model,
+                             2 * d.ffn_dim, nullptr, &pf, stream)))
+      return rc;
+    rrr_gemv_prologue ps{RRR_X_SILU_GATE, nullptr, 0.f, 0, 0, 0};
+    if ((rc = rrr_gemv_kq_ex(ctx, L.down_type, L.w_down, m->gate_up, hidden, d.ffn_dim, d.d_model,
+                             hidden, &ps, stream)))
+      return rc;
+  }
+  if ((rc = rrr_logits_f32(ctx, d.w_out, hidden, logits, d.vocab, d.d_model, d.logits_chunk_rows,
+                           d.output_norm, d.rms_eps, stream)))
+    return rc;
+  if (argmax && (rc = rrr_argmax_f32(ctx, logits, d.vocab, argmax, stream))) return rc;
+  return RRR_OK;
+}
+
+static void phi4_drop_graph(rrr_phi4* m) {
+  if (m->exec) cudaGraphExecDestroy(m->exec);
+  if (m->graph) cudaGraphDestroy(m->graph);
+  m->exec = nullptr;
+  m->graph = nullptr;
+}
+
+extern "C" {
+
+int rrr_phi4_create(rrr_ctx* ctx, const rrr_phi4_desc* desc, rrr_phi4** out) {
+  if (!ctx) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null context");
+  if (!desc || !out) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_phi4_create: null argument");
+  *out = nullptr;
+  const rrr_phi4_desc& d = *desc;
+  if (d.d_model <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.head_dim <= 0 || d.ffn_dim <= 0 ||
+      d.n_layers < 0 || d.vocab <= 0 || d.n_heads % d.n_kv_heads != 0 ||
+      d.n_heads * d.head_dim != d.d_model || d.d_model % 256 != 0 || d.ffn_dim % 256 != 0 ||
+      d.head_dim % 8 != 0)
+    return set_error(ctx, RRR_ERR_BAD_SHAPE,
+                     "rrr_phi4_create: need n_heads*head_dim == d_model, d_model and ffn_dim "
+                     "multiples of 256, head_dim %% 8 == 0, n_heads %% n_kv_heads == 0");
+  if ((d.n_layers > 0 && !d.layers) || !d.output_norm || !d.w_out)
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_phi4_create: missing weights");
+  for (int l = 0; l < d.n_layers; ++l) {
+    const rrr_phi4_layer& L = d.layers[l];
+    if (!L.w_qkv || !L.w_o || !L.w_gate_up || !L.w_down || !L.attn_norm || !L.ffn_norm)
+      return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_phi4_create: layer %d has a null weight", l);
+  }
+  int rc = bind_device(ctx);
+  if (rc) return rc;
+  rrr_phi4* m = new rrr_phi4();
+  m->ctx = ctx;
+  m->d = d;
+  m->layers.assign(d.layers, d.layers + d.n_layers);
+  m->d.layers = nullptr;
+  const size_t qkv_dim = (size_t)(d.n_heads + 2 * d.n_kv_heads) * d.head_dim;
+  cudaError_t e = cudaMalloc(&m->qkv, qkv_dim * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&m->gate_up, 2 * (size_t)d.ffn_dim * sizeof(float));
+  if (e != cudaSuccess) {
+    rrr_phi4_destroy(m);
+    return cuda_error(ctx, e, "rrr_phi4_create: scratch allocation");
+  }
+  *out = m;
+  return RRR_OK;
+}
+
+int rrr_phi4_forward(rrr_phi4* m, float* hidden, float* logits, int* argmax_out, int use_graph,
+                     void* stream) {
+  if (!m) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null model");
+  rrr_ctx* ctx = m->ctx;
+  if (!hidden || !logits) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_phi4_forward: null buffer");
+  int rc = bind_device(ctx);
+  if (rc) return rc;
+  if (!use_graph) return phi4_issue(m, hidden, logits, argmax_out, stream);
+  if (!m->exec || m->g_hidden != hidden || m->g_logits != logits || m->g_argmax != argmax_out) {
+    phi4_drop_graph(m);
+    if (!m->cap_stream) {
+      cudaError_t e = cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking);
+      if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_phi4_forward: stream");
+    }
+    cudaError_t e;
+    e = cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeRelaxed);
+    if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_phi4_forward: begin capture");
+    rc = phi4_issue(m, hidden, logits, argmax_out, m->cap_stream);
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(m->cap_stream, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_phi4_forward: end capture");
+    e = cudaGraphInstantiate(&m->exec, g, 0);
+    if (e != cudaSuccess) {
+      cudaGraphDestroy(g);
+      return cuda_error(ctx, e, "rrr_phi4_forward: instantiate");
+    }
+    m->graph = g;
+    m->g_hidden = hidden;
+    m->g_logits = logits;
+    m->g_argmax = argmax_out;
+  }
+  cudaError_t e = cudaGraphLaunch(m->exec, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_phi4_forward: graph launch");
+  return RRR_OK;
+}
+
+int rrr_phi4_launches_per_step(rrr_phi4* m, int* n) {
+  if (!m || !n) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null argument");
+  const int chunk = m->d.logits_chunk_rows > 0 ? m->d.logits_chunk_rows : m->d.vocab;
+  *n = 4 * m->d.n_layers + (m->d.vocab + chunk - 1) / chunk;
+  return RRR_OK;
+}
+
+int rrr_phi4_destroy(rrr_phi4* m) {
+  if (!m) return RRR_OK;
+  bind_device(m->ctx);
+  phi4_drop_graph(m);
+  if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
+  if (m->qkv) cudaFree(m->qkv);
+  if (m->gate_up) cudaFree(m->gate_up);
+  delete m;
+  return RRR_OK;
+}
+
+}  // extern "C"
