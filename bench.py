@@ -177,23 +177,42 @@ def run_ours(args, rank, world, local_rank):
     cfg = phi4.ModelConfig()
     model = phi4.SyntheticPhi4(ctx, cfg, seed=1000 + rank, stream=sp)
     gemvs = cfg.layer_gemvs()
-    xs = {name: torch.randn(K * (2 if name == "down" else 1), device="cuda") for name, _, K, _ in gemvs}
-    ys = {name: torch.empty(N, device="cuda") for name, _, _, N in gemvs}
+    # x / y of every GEMV of the 32-layer pass, packed in one device buffer each (the
+    # end-to-end leg copies them from / to pinned host memory in one transfer each)
+    x_off, y_off, xo, yo = {}, {}, 0, 0
+    for l in range(cfg.n_layers):
+        for name, _, K, N in gemvs:
+            x_off[l, name], y_off[l, name] = xo, yo
+            xo += K
+            yo += N
+    X = torch.randn(xo, device="cuda")
+    Y = torch.empty(yo, device="cuda")
     bytes_layer = sum(cfg.weight_bytes(q, K, N) + 4 * K + 4 * N for _, q, K, N in gemvs)
     bytes_step = bytes_layer * cfg.n_layers
     launches_step = 4 * cfg.n_layers
+    qname = {12: "matmul_q4k", 13: "matmul_q5k", 14: "matmul_q6k"}
 
-    def gemv(layer, name):
-        p, qt, K, N = model.layers[layer][name]
-        return L.rrr_gemv_kq(ctx.h, qt, c_void_p(p), c_void_p(xs[name].data_ptr()),
-                             c_void_p(ys[name].data_ptr()), K, N, None, sp)
+    def add_gemv(batch, l, name):
+        p, qt, K, N = model.layers[l][name]
+        bufs = (c_void_p * 3)(X.data_ptr() + 4 * x_off[l, name], p, Y.data_ptr() + 4 * y_off[l, name])
+        sizes = (ctypes.c_uint64 * 3)(4 * K, cfg.weight_bytes(qt, K, N), 4 * N)
+        push = ctypes.create_string_buffer(rrr.push_u32(K, N), 8)
+        ctx.check(L.rrr_batch_add(batch, qname[qt].encode(), bufs, sizes, 3, push, 8))
+
+    def make_batch(names):
+        b = c_void_p()
+        ctx.check(L.rrr_batch_create(ctx.h, ctypes.byref(b)))
+        for l in range(cfg.n_layers):
+            for name in names:
+                add_gemv(b, l, name)
+        return b
+
+    # The step as a prebuilt dispatch table (the reference's pre_allocate_desc_set +
+    # dispatch_batch_persistent_v2), replayed as one CUDA graph per step.
+    step_batch = make_batch([g[0] for g in gemvs])
 
     def step():
-        for l in range(cfg.n_layers):
-            for name, _, _, _ in gemvs:
-                rc = gemv(l, name)
-                if rc:
-                    ctx.check(rc)
+        ctx.check(L.rrr_batch_launch(step_batch, sp))
 
     def barrier():
         torch.cuda.synchronize()
@@ -220,23 +239,24 @@ def run_ours(args, rank, world, local_rank):
     e1.record(stream)
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-    # ---------------- per-GEMV (same kernel, one shape at a time over 32 layers)
+    # ---------------- per-GEMV: one shape over the 32 layers' weights per replay
     per = {}
     for name, qt, K, N in gemvs:
-        for l in range(cfg.n_layers):
-            gemv(l, name)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = max(2, args.steps)
+        b = make_batch([name])
+        ctx.check(L.rrr_batch_launch(b, sp))
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(5, args.steps)
         a.record(stream)
         for _ in range(reps):
-            for l in range(cfg.n_layers):
-                gemv(l, name)
-        b.record(stream)
+            ctx.check(L.rrr_batch_launch(b, sp))
+        z.record(stream)
         torch.cuda.synchronize()
-        us = 1e3 * a.elapsed_time(b) / (reps * cfg.n_layers)
+        L.rrr_batch_destroy(b)
+        us = 1e3 * a.elapsed_time(z) / (reps * cfg.n_layers)
         nb = cfg.weight_bytes(qt, K, N) + 4 * K + 4 * N
         per[name] = {"qtype": {12: "Q4_K", 13: "Q5_K", 14: "Q6_K"}[qt], "K": K, "N": N, "bytes": nb,
-                     "us_per_launch": round(us, 3), "GBps": round(nb / us / 1e3, 1)}
+                     "us_per_launch": round(us, 3), "GBps": round(nb / us / 1e3, 1),
+                     "frac": round(nb / us / 1e3 / peaks()[0], 4)}
     clk = clocks.stop()
     peak, peak_src = peaks()
     # ---------------- decode step through the CUDA graph
@@ -261,29 +281,26 @@ def run_ours(args, rank, world, local_rank):
               "frac_of_peak": round(dec_bytes / dms / 1e6 / peak, 4),
               "launches_per_token": dec.launches_per_step() + 1, "graph": True}
     dec.close()
-    # ---------------- end to end through the C ABI with host buffers (pinned)
-    hx = {n: torch.randn(K * (2 if n == "down" else 1)).pin_memory() for n, _, K, _ in gemvs}
-    hy = {n: torch.empty(N).pin_memory() for n, _, _, N in gemvs}
-    h2d = sum(hx[n].numel() * 4 for n, _, _, _ in gemvs) * cfg.n_layers
-    d2h = sum(hy[n].numel() * 4 for n, _, _, _ in gemvs) * cfg.n_layers
+    # ---------------- end to end through the C ABI with host buffers (pinned): copy every
+    # x of the step in, replay the prebuilt table, copy every y out, synchronise
+    hX = torch.randn(xo).pin_memory()
+    hY = torch.empty(yo).pin_memory()
+    h2d, d2h = hX.numel() * 4, hY.numel() * 4
 
     def e2e_step():
-        for l in range(cfg.n_layers):
-            for name, _, _, _ in gemvs:
-                ctx.check(L.rrr_h2d(ctx.h, c_void_p(xs[name].data_ptr()), c_void_p(hx[name].data_ptr()),
-                                    hx[name].numel() * 4, sp))
-                ctx.check(gemv(l, name))
-                ctx.check(L.rrr_d2h(ctx.h, c_void_p(hy[name].data_ptr()), c_void_p(ys[name].data_ptr()),
-                                    hy[name].numel() * 4, sp))
+        ctx.check(L.rrr_h2d(ctx.h, c_void_p(X.data_ptr()), c_void_p(hX.data_ptr()), h2d, sp))
+        ctx.check(L.rrr_batch_launch(step_batch, sp))
+        ctx.check(L.rrr_d2h(ctx.h, c_void_p(hY.data_ptr()), c_void_p(Y.data_ptr()), d2h, sp))
         ctx.check(L.rrr_sync(ctx.h, sp))
 
-    for _ in range(2):
+    for _ in range(3):
         e2e_step()
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         e2e_step()
     e2e_ms = max_over_ranks(1e3 * (time.perf_counter() - t0) / args.steps)
+    L.rrr_batch_destroy(step_batch)
     code = ctx.device_error()
     if code:
         raise SystemExit(f"device error flag {code}")
@@ -315,7 +332,7 @@ def run_ours(args, rank, world, local_rank):
             "decode": decode,
             "e2e": {"value": round(bytes_step / e2e_ms / 1e6, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "rrr_h2d + rrr_gemv_kq + rrr_d2h per GEMV (pinned host buffers), one sync per step"},
+                    "path": "rrr_h2d (all x) + rrr_batch_launch (prebuilt table of 128 GEMVs) + rrr_d2h (all y) + rrr_sync, pinned host buffers"},
             "gpu_launches": launches_step * args.steps,
             "clocks": clk,
             "cpu_baseline": cb,

@@ -116,6 +116,13 @@ int rrr_gemv_kq_ex(rrr_ctx* ctx, int qtype, const void* w_raw, const float* x_in
                    float* y, int K, int N, const float* residual,
                    const rrr_gemv_prologue* pro, void* stream);
 
+/* gate_up GEMV with the SwiGLU epilogue (the `silu_gate` shader fused, phi4.rs:1023,
+ * 1368-1373): W has 2F rows [gate; up] (the Phi-3 ffn_up layout), y f32[F] =
+ * silu(W_gate . x_in) * (W_up . x_in), silu(g) = g / (1 + e^-g). pro: NULL, RRR_X_PLAIN or
+ * RRR_X_RMSNORM. No residual. */
+int rrr_gemv_kq_swiglu(rrr_ctx* ctx, int qtype, const void* w_raw, const float* x_in,
+                       float* y, int K, int F, const rrr_gemv_prologue* pro, void* stream);
+
 /* Bit-exact dequantisation of n_blocks raw blocks to f32 (n_blocks*256 values), the
  * reference's CPU dequant_q4_k / dequant_q5_k / dequant_q6_k (phi4.rs:481-542, 444-479)
  * on the GPU, with no FMA contraction. */

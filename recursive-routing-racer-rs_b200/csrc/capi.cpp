@@ -308,6 +308,30 @@ int rrr_gemv_kq(rrr_ctx* ctx, int qtype, const void* w, const float* x, float* y
   return rrr_gemv_kq_ex(ctx, qtype, w, x, y, K, N, residual, nullptr, stream);
 }
 
+int rrr_gemv_kq_swiglu(rrr_ctx* ctx, int qtype, const void* w, const float* x, float* y, int K,
+                       int F, const rrr_gemv_prologue* pro, void* stream) {
+  RRR_CHECK_CTX(ctx);
+  int rc = check_qtype(ctx, qtype, "rrr_gemv_kq_swiglu");
+  if (rc) return rc;
+  if (!w || !x || !y) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq_swiglu: null pointer");
+  if (K < 256 || K % 256 != 0 || K > kGemvMaxK || F < 1)
+    return set_error(ctx, RRR_ERR_BAD_SHAPE,
+                     "rrr_gemv_kq_swiglu: need K %% 256 == 0, 256 <= K <= %d, F >= 1", kGemvMaxK);
+  const int mode = pro ? pro->mode : RRR_X_PLAIN;
+  if (mode != RRR_X_PLAIN && mode != RRR_X_RMSNORM)
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq_swiglu: prologue must be PLAIN or RMSNORM");
+  if (mode == RRR_X_RMSNORM && (!pro->gamma || !aligned(pro->gamma, 16)))
+    return set_error(ctx, RRR_ERR_MISALIGNED, "rrr_gemv_kq_swiglu: gamma missing or not 16-byte aligned");
+  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(y, 4))
+    return set_error(ctx, RRR_ERR_MISALIGNED, "rrr_gemv_kq_swiglu: W and x 16-byte, y 4-byte aligned");
+  if (overlap(y, (size_t)F * 4, x, (size_t)K * 4))
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq_swiglu: y must not overlap x");
+  RRR_BIND(ctx);
+  RRR_LAUNCH_CHECK(ctx, launch_gemv_kq_swiglu(make_env(ctx, stream), qtype, w, x, y, K, F, pro),
+                   "rrr_gemv_kq_swiglu launch");
+  return RRR_OK;
+}
+
 int rrr_dequant_kq(rrr_ctx* ctx, int qtype, const void* w, float* out, int64_t n_blocks,
                    void* stream) {
   RRR_CHECK_CTX(ctx);
@@ -415,7 +439,8 @@ int rrr_argmax_f32(rrr_ctx* ctx, const float* x, int n, int* out_index, void* st
   if (!x || !out_index) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_argmax_f32: null pointer");
   if (n < 1) return set_error(ctx, RRR_ERR_BAD_SHAPE, "rrr_argmax_f32: n < 1");
   RRR_BIND(ctx);
-  RRR_LAUNCH_CHECK(ctx, launch_argmax(make_env(ctx, stream), x, n, out_index), "rrr_argmax_f32 launch");
+  RRR_LAUNCH_CHECK(ctx, launch_argmax(make_env(ctx, stream), x, n, out_index, ctx->argmax_scratch()),
+                   "rrr_argmax_f32 launch");
   return RRR_OK;
 }
 

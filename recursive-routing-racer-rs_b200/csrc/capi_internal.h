@@ -10,9 +10,11 @@
 struct rrr_ctx {
   int device = 0;
   int sm_count = 0;
-  int* d_err = nullptr;  // device error flag written by kernels whose bounded waits give up
+  int* d_err = nullptr;  // 256 B: [0] device error flag written by kernels whose bounded
+                         // waits give up; [64..79] argmax key + counter (kept zeroed)
   bool pdl = true;       // launch kernels with programmatic dependent launch
   std::string last_error;
+  void* argmax_scratch() { return reinterpret_cast<char*>(d_err) + 64; }
 };
 
 namespace rrr {

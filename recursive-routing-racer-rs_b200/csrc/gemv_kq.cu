@@ -4,25 +4,31 @@
 // phi4.rs:444-542).
 //
 // Design (sm_100a, HBM-bound):
-//  * One CTA = 1 producer warp + NW consumer warps. The producer streams 16-row tiles of
-//    raw blocks (K split into chunks of kc blocks) with 1-D bulk copies (cp.async.bulk,
-//    mbarrier complete_tx) into a ring of shared-memory stages; consumers free a stage
-//    through an "empty" mbarrier. Every wait is bounded (%globaltimer) and reports
-//    through the context's error flag instead of hanging.
+//  * One CTA = 1 producer warp + 8 consumer warps, two CTAs per SM. The producer streams 16-row tiles of raw blocks (K
+//    split into chunks of kc blocks) with 1-D bulk copies (cp.async.bulk, mbarrier
+//    complete_tx) into a ring of shared-memory stages; consumers free a stage through an
+//    "empty" mbarrier. Every wait is bounded (%globaltimer) and reports through the
+//    context's error flag instead of hanging.
 //  * x is decomposed once per CTA into three int8 "digits" per element against a per-
 //    256-element scale xs: x ~= xs*(d0 + d1/2^7 + d2/2^14), |error| <= xs*2^-15 (about
-//    f32 precision). The per-sub-block sums sum_j q_j*x_j then come from exact int8
-//    tensor-core dot products (mma.sync m16n8k32, u8 quants x s8 digits, int32
-//    accumulate): a 16-row x 32-weight tile per instruction, digits of two scale groups
-//    in columns 0-2 and 3-5. Scales are applied by integer multiply-add per sub-block,
-//    d/dmin in f32 once per block. This keeps the CUDA-core work near one instruction
-//    per weight so the kernel stays memory-bound. Dequantised weights are never
-//    materialised; the bit-exact dequantisation is rrr_dequant_kq (dequant.cu).
+//    f32 precision). The per-scale-group sums sum_j q_j*x_j then come from exact integer
+//    tensor-core dot products (mma.sync m16n8k32, u8 quants x s8 digits, s32
+//    accumulate): a 16-row x 32-weight tile per instruction, the digits of two scale
+//    groups in B columns 0-2 and 3-5. Scales are applied by integer multiply-add per
+//    group, d / dmin in f32 once per half block. The CUDA cores do about one instruction
+//    per weight, so the kernel stays memory-bound. Dequantised weights are never
+//    materialised; the bit-exact dequantisation is rrr_dequant_kq (kernels.cu).
+//  * Work items are whole blocks (256 weights of 16 rows); the warp that takes the first
+//    block rotates from stage to stage so that the blocks of a stage (12 for K = 3072,
+//    8 for Q6_K K = 8192) spread evenly over the warps.
 //  * Tile epilogue: shuffle reduction over the 4 lanes that share a row, then a
-//    deterministic sum over warps through shared memory, + residual, store.
+//    deterministic sum over warps through shared memory, + residual, store. The SwiGLU
+//    output mode pairs gate row tile t with up row tile t (rows F + 16t ...) in one CTA
+//    and stores silu(gate) * up (the `silu_gate` shader, phi4.rs:1368-1373, fused).
 //  * Programmatic dependent launch: the producer starts streaming weights before
 //    griddepcontrol.wait; x is read and y written only after it.
 #include <algorithm>
+#include <cstdlib>
 
 #include "internal.h"
 #include "kquant.cuh"
@@ -31,102 +37,82 @@ namespace rrr {
 namespace {
 
 constexpr int kTileRows = 16;
-constexpr int kNW = 4;  // consumer warps per CTA
-constexpr int kXBf16 = 100;  // internal prologue mode: x is bf16 (batched fallback)
+constexpr int kNW = 8;                  // consumer warps per CTA
+constexpr int kThreads = (kNW + 1) * 32;
+constexpr int kXBf16 = 100;             // internal prologue mode: x is bf16 (batched path)
+constexpr int kSmemBudget = 113 * 1024; // two CTAs per SM
+constexpr int kMaxStages = 6;
+constexpr int kSlots = 8;               // row-tile reduction slots (> stages + 1)
 
 struct GemvParams {
   const uint8_t* w;
   const float* x;
-  const uint16_t* xb;  // bf16 input (internal mode kXBf16)
+  const uint16_t* xb;  // bf16 input (mode kXBf16)
   float* y;
   const float* residual;
   const float* gamma;
   float eps;
-  int mode, n_q, n_kv, hd;
-  int K, N, nb;
+  int mode, out_mode, n_q, n_kv, hd;
+  int K, N, nb;        // N: weight rows
   long long row_bytes, total_bytes;
-  int kc, n_chunks, n_tiles;
-  int row_stride, stage_bytes, nstages;
-  int dig_stride;
-  int off_bars, off_dig, off_xscale, off_xsum, off_red, off_misc;
+  int kc, n_chunks, n_tiles, half_rows;
+  int row_stride, stage_bytes, nstages, dig_stride;
+  int off_bars, off_dig, off_xscale, off_xsum, off_red, off_gate, off_misc;
   int* err;
 };
 
 __device__ __forceinline__ void mma_u8s8(int& d0, int& d1, int& d2, int& d3, uint32_t a0,
                                          uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+r"(d0), "+r"(d1), "+r"(d2), "+r"(d3)
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Weight of B column c (digit c % 3 of scale group c / 3); columns 6 and 7 are unused.
-__device__ __forceinline__ float digit_weight(int c) {
-  return c >= 6 ? 0.f : (c % 3 == 0 ? 1.f : (c % 3 == 1 ? (1.f / 128.f) : (1.f / 16384.f)));
+// First MMA of an accumulation chain (C = 0).
+__device__ __forceinline__ void mma_u8s8_z(int& d0, int& d1, int& d2, int& d3, uint32_t a0,
+                                           uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                           uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
-__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
+// Lane roles inside an MMA tile: rows g and g+8 of the A operand; B column n = g carries
+// digit n of scale group A (n = 0..2) or digit n-4 of group B (n = 4..6), columns 3 and 7
+// are zero; the lane's D columns 2*tig, 2*tig+1 therefore belong to a single group
+// (hb = tig >> 1), so one scale per row applies to both.
+struct Lane {
+  int g, tig, hb;
+  uint32_t mA, mB;  // masks selecting which half of a compact B fragment this lane fills
+  int dsel;         // digit supplied in B column g (compact layout)
+  int frag_off;     // byte offset of this lane's B fragment inside a pair (fragment layout)
+  float w0, w1;     // f32 weights of the lane's two D columns
+};
 
-// ---------------------------------------------------------------- Q4_K block
-// Rows g and g+8 of the tile, block `kb` of the row. MMA (pair p, half h) covers qs
-// bytes 32p + 8*tig + 4h .. +3 of both rows: low nibbles = sub 2p (group A, slots 0-15),
-// high nibbles taken as (byte & 0xF0) = 16*q = sub 2p+1 (group B, slots 16-31).
-__device__ __forceinline__ void block_q4k(const uint8_t* b0, const uint8_t* b1, int kb,
-                                          const int8_t* dig, int ds, const float* xscale,
-                                          const float* xsum, int g, int tig, float& acc0,
-                                          float& acc1) {
-  const uint4 h0 = *reinterpret_cast<const uint4*>(b0);
-  const uint4 h1 = *reinterpret_cast<const uint4*>(b1);
-  const float d_0 = f16_bits_to_f32(h0.x & 0xFFFFu), dm_0 = f16_bits_to_f32(h0.x >> 16);
-  const float d_1 = f16_bits_to_f32(h1.x & 0xFFFFu), dm_1 = f16_bits_to_f32(h1.x >> 16);
-  const uint32_t sc03_0 = h0.y & 0x3F3F3F3Fu, m03_0 = h0.z & 0x3F3F3F3Fu;
-  const uint32_t sc47_0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
-  const uint32_t m47_0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
-  const uint32_t sc03_1 = h1.y & 0x3F3F3F3Fu, m03_1 = h1.z & 0x3F3F3F3Fu;
-  const uint32_t sc47_1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
-  const uint32_t m47_1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+__device__ __forceinline__ Lane make_lane(int lane, bool q4) {
+  Lane L;
+  L.g = lane >> 2;
+  L.tig = lane & 3;
+  L.hb = L.tig >> 1;
+  L.mA = L.g < 3 ? 0xFFFFFFFFu : 0u;
+  L.mB = (L.g >= 4 && L.g < 7) ? 0xFFFFFFFFu : 0u;
+  L.dsel = (L.g < 3) ? L.g : (L.g >= 4 && L.g < 7) ? L.g - 4 : 0;
+  L.frag_off = (L.g * 4 + L.tig) * 16;
+  // columns: tig 0 -> (d0, d1), tig 1 -> (d2, 0), tig 2 -> (d0, d1), tig 3 -> (d2, 0)
+  const float scale = (q4 && L.hb) ? (1.f / 16.f) : 1.f;  // Q4_K high nibbles enter x16
+  L.w0 = ((L.tig & 1) ? (1.f / 16384.f) : 1.f) * scale;
+  L.w1 = ((L.tig & 1) ? 0.f : (1.f / 128.f)) * scale;
+  return L;
+}
 
-  const int n = g;  // B column supplied by this lane
-  const bool nA = n < 3, nB = (n >= 3) && (n < 6);
-  const int8_t* dp = dig + (n < 6 ? (n % 3) * ds : 0) + kb * 256 + 8 * tig + (nB ? 32 : 0);
-  const bool c0B = (2 * tig) >= 3, c1B = (2 * tig + 1) >= 3;
-  int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
-#pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const uint2 w = *reinterpret_cast<const uint2*>(b0 + 16 + 32 * p + 8 * tig);
-    const uint2 v = *reinterpret_cast<const uint2*>(b1 + 16 + 32 * p + 8 * tig);
-    uint2 bb = make_uint2(0u, 0u);
-    if (nA || nB) bb = *reinterpret_cast<const uint2*>(dp + 64 * p);
-    int D0 = 0, D1 = 0, D2 = 0, D3 = 0;
-    mma_u8s8(D0, D1, D2, D3, w.x & 0x0F0F0F0Fu, v.x & 0x0F0F0F0Fu, w.x & 0xF0F0F0F0u,
-             v.x & 0xF0F0F0F0u, nA ? bb.x : 0u, nB ? bb.x : 0u);
-    mma_u8s8(D0, D1, D2, D3, w.y & 0x0F0F0F0Fu, v.y & 0x0F0F0F0Fu, w.y & 0xF0F0F0F0u,
-             v.y & 0xF0F0F0F0u, nA ? bb.y : 0u, nB ? bb.y : 0u);
-    const int sa = 2 * p, sb = 2 * p + 1;
-    const int sA0 = 16 * (int)byte_of(sa < 4 ? sc03_0 : sc47_0, sa & 3);
-    const int sB0 = (int)byte_of(sb < 4 ? sc03_0 : sc47_0, sb & 3);
-    const int sA1 = 16 * (int)byte_of(sa < 4 ? sc03_1 : sc47_1, sa & 3);
-    const int sB1 = (int)byte_of(sb < 4 ? sc03_1 : sc47_1, sb & 3);
-    i00 += (c0B ? sB0 : sA0) * D0;
-    i01 += (c1B ? sB0 : sA0) * D1;
-    i10 += (c0B ? sB1 : sA1) * D2;
-    i11 += (c1B ? sB1 : sA1) * D3;
-  }
-  const float xs = xscale[kb];
-  const float w0 = digit_weight(2 * tig) * (1.f / 16.f), w1 = digit_weight(2 * tig + 1) * (1.f / 16.f);
-  const float v0 = (float)i00 * w0 + (float)i01 * w1;
-  const float v1 = (float)i10 * w0 + (float)i11 * w1;
-  // min term of sub-blocks 2*tig and 2*tig+1: dmin * (m_a*S_a + m_b*S_b)
-  const float* xsb = xsum + kb * 16 + 4 * tig;
-  const float Sa = xsb[0] + xsb[1], Sb = xsb[2] + xsb[3];
-  const int sh = 16 * (tig & 1);
-  const uint32_t mw0 = tig < 2 ? m03_0 : m47_0, mw1 = tig < 2 ? m03_1 : m47_1;
-  const float ma0 = (float)((mw0 >> sh) & 0xFFu), mb0 = (float)((mw0 >> (sh + 8)) & 0xFFu);
-  const float ma1 = (float)((mw1 >> sh) & 0xFFu), mb1 = (float)((mw1 >> (sh + 8)) & 0xFFu);
-  acc0 += d_0 * xs * v0 - dm_0 * (ma0 * Sa + mb0 * Sb);
-  acc1 += d_1 * xs * v1 - dm_1 * (ma1 * Sa + mb1 * Sb);
+// Exact float of an integer 0 <= u < 2^23 without a conversion instruction.
+__device__ __forceinline__ float small_u2f(uint32_t u) {
+  return __fsub_rn(__uint_as_float(0x4B000000u | u), 8388608.0f);
 }
 
 // qh bit `s` of each byte moved to bit 4.
@@ -134,66 +120,86 @@ __device__ __forceinline__ uint32_t qh_bit4(uint32_t x, int s) {
   return (s <= 4 ? (x << (4 - s)) : (x >> (s - 4))) & 0x10101010u;
 }
 
-// ---------------------------------------------------------------- Q5_K block
-__device__ __forceinline__ void block_q5k(const uint8_t* b0, const uint8_t* b1, int kb,
+// B fragments of one sub-block pair (64 x elements) for the two MMAs of the pair:
+// (b0, b1) of MMA 1 and (b0, b1) of MMA 2. FRAG: read ready-made from the per-lane
+// fragment layout (one 16-byte load); otherwise from the compact digit rows with masks.
+template <bool FRAG>
+__device__ __forceinline__ uint4 load_bfrag(const int8_t* dig, int ds, int pair, const Lane& L) {
+  if (FRAG) return *reinterpret_cast<const uint4*>(dig + pair * 512 + L.frag_off);
+  const uint2 bb = *reinterpret_cast<const uint2*>(dig + L.dsel * ds + pair * 64 + 8 * L.tig +
+                                                   (L.mB ? 32 : 0));
+  return make_uint4(bb.x & L.mA, bb.x & L.mB, bb.y & L.mA, bb.y & L.mB);
+}
+
+// One Q4_K / Q5_K block (256 weights) of rows g and g+8. MMA (pair p, half-word h) covers
+// qs bytes 32p + 8*tig + 4h .. +3 of both rows: low nibbles = sub 2p (group A, k-slots
+// 0-15), high nibbles = sub 2p+1 (group B, k-slots 16-31). For Q4_K the high nibbles
+// enter as (byte & 0xF0) = 16*q (no shift). Scale / min unpacking follows phi4.rs:492-498
+// four sub-blocks per 32-bit word; the integer scale of each pair is applied to the s32
+// sums by multiply-add, d and dmin once per block in f32.
+template <int QT, bool FRAG>
+__device__ __forceinline__ void block_q45(const uint8_t* b0, const uint8_t* b1, int kb,
                                           const int8_t* dig, int ds, const float* xscale,
-                                          const float* xsum, int g, int tig, float& acc0,
+                                          const float* xsum32, const Lane& L, float& acc0,
                                           float& acc1) {
+  constexpr int QS = (QT == RRR_Q4_K) ? 16 : 48;
   const uint4 h0 = *reinterpret_cast<const uint4*>(b0);
   const uint4 h1 = *reinterpret_cast<const uint4*>(b1);
-  const float d_0 = f16_bits_to_f32(h0.x & 0xFFFFu), dm_0 = f16_bits_to_f32(h0.x >> 16);
-  const float d_1 = f16_bits_to_f32(h1.x & 0xFFFFu), dm_1 = f16_bits_to_f32(h1.x >> 16);
-  const uint32_t sc03_0 = h0.y & 0x3F3F3F3Fu, m03_0 = h0.z & 0x3F3F3F3Fu;
-  const uint32_t sc47_0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
-  const uint32_t m47_0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
-  const uint32_t sc03_1 = h1.y & 0x3F3F3F3Fu, m03_1 = h1.z & 0x3F3F3F3Fu;
-  const uint32_t sc47_1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
-  const uint32_t m47_1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
-  const uint2 qh0 = *reinterpret_cast<const uint2*>(b0 + 16 + 8 * tig);
-  const uint2 qh1 = *reinterpret_cast<const uint2*>(b1 + 16 + 8 * tig);
-
-  const int n = g;
-  const bool nA = n < 3, nB = (n >= 3) && (n < 6);
-  const int8_t* dp = dig + (n < 6 ? (n % 3) * ds : 0) + kb * 256 + 8 * tig + (nB ? 32 : 0);
-  const bool c0B = (2 * tig) >= 3, c1B = (2 * tig + 1) >= 3;
+  // this lane's group (sub 2p + hb): byte 2*(p&1) + hb of the packed word of subs 0-3 / 4-7
+  const uint32_t s03_0 = (h0.y & 0x3F3F3F3Fu) >> (8 * L.hb);
+  const uint32_t s47_0 = ((h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u)) >> (8 * L.hb);
+  const uint32_t s03_1 = (h1.y & 0x3F3F3F3Fu) >> (8 * L.hb);
+  const uint32_t s47_1 = ((h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u)) >> (8 * L.hb);
+  uint2 qh0 = make_uint2(0u, 0u), qh1 = make_uint2(0u, 0u);
+  if (QT == RRR_Q5_K) {
+    qh0 = *reinterpret_cast<const uint2*>(b0 + 16 + 8 * L.tig);
+    qh1 = *reinterpret_cast<const uint2*>(b1 + 16 + 8 * L.tig);
+  }
   int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    const uint2 w = *reinterpret_cast<const uint2*>(b0 + 48 + 32 * p + 8 * tig);
-    const uint2 v = *reinterpret_cast<const uint2*>(b1 + 48 + 32 * p + 8 * tig);
-    uint2 bb = make_uint2(0u, 0u);
-    if (nA || nB) bb = *reinterpret_cast<const uint2*>(dp + 64 * p);
-    const int sa = 2 * p, sb = 2 * p + 1;
-    int D0 = 0, D1 = 0, D2 = 0, D3 = 0;
-    mma_u8s8(D0, D1, D2, D3, (w.x & 0x0F0F0F0Fu) | qh_bit4(qh0.x, sa),
-             (v.x & 0x0F0F0F0Fu) | qh_bit4(qh1.x, sa),
-             ((w.x >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh0.x, sb),
-             ((v.x >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh1.x, sb), nA ? bb.x : 0u, nB ? bb.x : 0u);
-    mma_u8s8(D0, D1, D2, D3, (w.y & 0x0F0F0F0Fu) | qh_bit4(qh0.y, sa),
-             (v.y & 0x0F0F0F0Fu) | qh_bit4(qh1.y, sa),
-             ((w.y >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh0.y, sb),
-             ((v.y >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh1.y, sb), nA ? bb.y : 0u, nB ? bb.y : 0u);
-    const int sA0 = (int)byte_of(sa < 4 ? sc03_0 : sc47_0, sa & 3);
-    const int sB0 = (int)byte_of(sb < 4 ? sc03_0 : sc47_0, sb & 3);
-    const int sA1 = (int)byte_of(sa < 4 ? sc03_1 : sc47_1, sa & 3);
-    const int sB1 = (int)byte_of(sb < 4 ? sc03_1 : sc47_1, sb & 3);
-    i00 += (c0B ? sB0 : sA0) * D0;
-    i01 += (c1B ? sB0 : sA0) * D1;
-    i10 += (c0B ? sB1 : sA1) * D2;
-    i11 += (c1B ? sB1 : sA1) * D3;
+    const uint2 w = *reinterpret_cast<const uint2*>(b0 + QS + 32 * p + 8 * L.tig);
+    const uint2 v = *reinterpret_cast<const uint2*>(b1 + QS + 32 * p + 8 * L.tig);
+    const uint4 bf = load_bfrag<FRAG>(dig, ds, kb * 4 + p, L);
+    int D0, D1, D2, D3;
+    if (QT == RRR_Q4_K) {
+      mma_u8s8_z(D0, D1, D2, D3, w.x & 0x0F0F0F0Fu, v.x & 0x0F0F0F0Fu, w.x & 0xF0F0F0F0u,
+                 v.x & 0xF0F0F0F0u, bf.x, bf.y);
+      mma_u8s8(D0, D1, D2, D3, w.y & 0x0F0F0F0Fu, v.y & 0x0F0F0F0Fu, w.y & 0xF0F0F0F0u,
+               v.y & 0xF0F0F0F0u, bf.z, bf.w);
+    } else {
+      const int sa = 2 * p, sb = 2 * p + 1;
+      mma_u8s8_z(D0, D1, D2, D3, (w.x & 0x0F0F0F0Fu) | qh_bit4(qh0.x, sa),
+                 (v.x & 0x0F0F0F0Fu) | qh_bit4(qh1.x, sa),
+                 ((w.x >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh0.x, sb),
+                 ((v.x >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh1.x, sb), bf.x, bf.y);
+      mma_u8s8(D0, D1, D2, D3, (w.y & 0x0F0F0F0Fu) | qh_bit4(qh0.y, sa),
+               (v.y & 0x0F0F0F0Fu) | qh_bit4(qh1.y, sa),
+               ((w.y >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh0.y, sb),
+               ((v.y >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh1.y, sb), bf.z, bf.w);
+    }
+    const int r0 = (int)(((p < 2 ? s03_0 : s47_0) >> (16 * (p & 1))) & 0xFFu);
+    const int r1 = (int)(((p < 2 ? s03_1 : s47_1) >> (16 * (p & 1))) & 0xFFu);
+    i00 += r0 * D0;
+    i01 += r0 * D1;
+    i10 += r1 * D2;
+    i11 += r1 * D3;
   }
   const float xs = xscale[kb];
-  const float w0 = digit_weight(2 * tig), w1 = digit_weight(2 * tig + 1);
-  const float v0 = (float)i00 * w0 + (float)i01 * w1;
-  const float v1 = (float)i10 * w0 + (float)i11 * w1;
-  const float* xsb = xsum + kb * 16 + 4 * tig;
-  const float Sa = xsb[0] + xsb[1], Sb = xsb[2] + xsb[3];
-  const int sh = 16 * (tig & 1);
-  const uint32_t mw0 = tig < 2 ? m03_0 : m47_0, mw1 = tig < 2 ? m03_1 : m47_1;
-  const float ma0 = (float)((mw0 >> sh) & 0xFFu), mb0 = (float)((mw0 >> (sh + 8)) & 0xFFu);
-  const float ma1 = (float)((mw1 >> sh) & 0xFFu), mb1 = (float)((mw1 >> (sh + 8)) & 0xFFu);
-  acc0 += d_0 * xs * v0 - dm_0 * (ma0 * Sa + mb0 * Sb);
-  acc1 += d_1 * xs * v1 - dm_1 * (ma1 * Sa + mb1 * Sb);
+  const float d0 = f16_bits_to_f32(h0.x & 0xFFFFu), d1 = f16_bits_to_f32(h1.x & 0xFFFFu);
+  const float dm0 = f16_bits_to_f32(h0.x >> 16), dm1 = f16_bits_to_f32(h1.x >> 16);
+  // min term of sub-blocks 2*tig, 2*tig+1 (bytes 2(tig&1), +1 of the mins of subs 0-3 /
+  // 4-7): dmin * (m_a * S_a + m_b * S_b), S = sum of x over the sub-block
+  const uint32_t mw0 = L.tig < 2 ? (h0.z & 0x3F3F3F3Fu)
+                                 : (((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u));
+  const uint32_t mw1 = L.tig < 2 ? (h1.z & 0x3F3F3F3Fu)
+                                 : (((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u));
+  const int sh = 16 * (L.tig & 1);
+  const float2 S = *reinterpret_cast<const float2*>(xsum32 + kb * 8 + 2 * L.tig);
+  const float mt0 = small_u2f((mw0 >> sh) & 0xFFu) * S.x + small_u2f((mw0 >> (sh + 8)) & 0xFFu) * S.y;
+  const float mt1 = small_u2f((mw1 >> sh) & 0xFFu) * S.x + small_u2f((mw1 >> (sh + 8)) & 0xFFu) * S.y;
+  acc0 += d0 * xs * ((float)i00 * L.w0 + (float)i01 * L.w1) - dm0 * mt0;
+  acc1 += d1 * xs * ((float)i10 * L.w0 + (float)i11 * L.w1) - dm1 * mt1;
 }
 
 // 32-bit load from a shared-memory byte address that is 4-byte or 2-byte aligned.
@@ -207,89 +213,80 @@ __device__ __forceinline__ uint32_t ldw(const uint8_t* p) {
 
 __device__ __forceinline__ int sbyte(uint32_t w, int i) { return (int)(int8_t)(w >> (8 * i)); }
 
-// Q6_K bits of element group (k): nibble (k>>1) of the ql word | 2 qh bits (2k) << 4.
+// Q6_K bits of element group k: nibble (k>>1) of the ql word | 2 qh bits (2k) << 4.
 __device__ __forceinline__ uint32_t q6_bytes(uint32_t ql, uint32_t qh, int k) {
   const uint32_t lo = (k >> 1) ? ((ql >> 4) & 0x0F0F0F0Fu) : (ql & 0x0F0F0F0Fu);
   const uint32_t hi = (k <= 2 ? (qh << (4 - 2 * k)) : (qh >> (2 * k - 4))) & 0x30303030u;
   return lo | hi;
 }
 
-// ---------------------------------------------------------------- Q6_K block
-// MMA (g, k) covers elements g*128 + 32k + l of rows g and g+8: group A = l in [0,16)
-// (scale g*8+2k), group B = l in [16,32) (scale g*8+2k+1); lane tig holds l = 4tig+i
-// (A) and 16+4tig+i (B). q is taken unsigned (0..63); the -32 offset is applied in f32
-// with the 16-element sums of x.
+// One Q6_K block of rows g and g+8. MMA (hg, k) covers elements hg*128 + 32k + l: group
+// A = l in [0,16) (scale hg*8+2k), group B = l in [16,32) (scale hg*8+2k+1); lane tig
+// holds l = 4tig+i (A) and 16+4tig+i (B) (element layout of phi4.rs:456-475). q is taken
+// unsigned (0..63); the -32 offset is applied in f32 with the 16-element sums of x.
 template <bool AL>
-__device__ __forceinline__ void block_q6k(const uint8_t* b0, const uint8_t* b1, int kb,
-                                          const int8_t* dig, int ds, const float* xscale,
-                                          const float* xsum, int g, int tig, float& acc0,
-                                          float& acc1) {
-  const float d_0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(b0 + 208));
-  const float d_1 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(b1 + 208));
+__device__ __forceinline__ void block_q6(const uint8_t* b0, const uint8_t* b1, int kb,
+                                         const int8_t* dig, int ds, const float* xscale,
+                                         const float* xsum, const Lane& L, float& acc0,
+                                         float& acc1) {
   uint32_t sw0[4], sw1[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     sw0[i] = ldw<AL>(b0 + 192 + 4 * i);
     sw1[i] = ldw<AL>(b1 + 192 + 4 * i);
   }
-  const int n = g;
-  const bool nA = n < 3, nB = (n >= 3) && (n < 6);
-  const int8_t* dp = dig + (n < 6 ? (n % 3) * ds : 0) + kb * 256 + 4 * tig + (nB ? 16 : 0);
-  const bool c0B = (2 * tig) >= 3, c1B = (2 * tig + 1) >= 3;
+  const int8_t* dp = dig + L.dsel * ds + kb * 256 + 4 * L.tig + (L.mB ? 16 : 0);
   int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
 #pragma unroll
   for (int hg = 0; hg < 2; ++hg) {
-    const uint8_t* p0 = b0 + hg * 64 + 4 * tig;
-    const uint8_t* p1 = b1 + hg * 64 + 4 * tig;
+    const uint8_t* p0 = b0 + hg * 64 + 4 * L.tig;
+    const uint8_t* p1 = b1 + hg * 64 + 4 * L.tig;
     const uint32_t qlA0_0 = ldw<AL>(p0), qlB0_0 = ldw<AL>(p0 + 16);
     const uint32_t qlA1_0 = ldw<AL>(p0 + 32), qlB1_0 = ldw<AL>(p0 + 48);
     const uint32_t qlA0_1 = ldw<AL>(p1), qlB0_1 = ldw<AL>(p1 + 16);
     const uint32_t qlA1_1 = ldw<AL>(p1 + 32), qlB1_1 = ldw<AL>(p1 + 48);
-    const uint8_t* h0p = b0 + 128 + hg * 32 + 4 * tig;
-    const uint8_t* h1p = b1 + 128 + hg * 32 + 4 * tig;
+    const uint8_t* h0p = b0 + 128 + hg * 32 + 4 * L.tig;
+    const uint8_t* h1p = b1 + 128 + hg * 32 + 4 * L.tig;
     const uint32_t qhA_0 = ldw<AL>(h0p), qhB_0 = ldw<AL>(h0p + 16);
     const uint32_t qhA_1 = ldw<AL>(h1p), qhB_1 = ldw<AL>(h1p + 16);
+    // this lane's scale group of MMA k: byte 2*(k&1) + hb of word 2hg + (k >> 1)
+    const uint32_t tA0 = sw0[2 * hg] >> (8 * L.hb), tB0 = sw0[2 * hg + 1] >> (8 * L.hb);
+    const uint32_t tA1 = sw1[2 * hg] >> (8 * L.hb), tB1 = sw1[2 * hg + 1] >> (8 * L.hb);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const uint32_t qlA_0 = (k & 1) ? qlA1_0 : qlA0_0, qlB_0 = (k & 1) ? qlB1_0 : qlB0_0;
       const uint32_t qlA_1 = (k & 1) ? qlA1_1 : qlA0_1, qlB_1 = (k & 1) ? qlB1_1 : qlB0_1;
-      const int8_t* dk = dp + hg * 128 + 32 * k;
-      const uint32_t bv = (nA || nB) ? *reinterpret_cast<const uint32_t*>(dk) : 0u;
-      int D0 = 0, D1 = 0, D2 = 0, D3 = 0;
-      mma_u8s8(D0, D1, D2, D3, q6_bytes(qlA_0, qhA_0, k), q6_bytes(qlA_1, qhA_1, k),
-               q6_bytes(qlB_0, qhB_0, k), q6_bytes(qlB_1, qhB_1, k), nA ? bv : 0u,
-               nB ? bv : 0u);
-      const int ga = hg * 8 + 2 * k, gb = ga + 1;
-      const int sA0 = sbyte(sw0[ga >> 2], ga & 3), sB0 = sbyte(sw0[gb >> 2], gb & 3);
-      const int sA1 = sbyte(sw1[ga >> 2], ga & 3), sB1 = sbyte(sw1[gb >> 2], gb & 3);
-      i00 += (c0B ? sB0 : sA0) * D0;
-      i01 += (c1B ? sB0 : sA0) * D1;
-      i10 += (c0B ? sB1 : sA1) * D2;
-      i11 += (c1B ? sB1 : sA1) * D3;
+      const uint32_t bv = *reinterpret_cast<const uint32_t*>(dp + hg * 128 + 32 * k);
+      int D0, D1, D2, D3;
+      mma_u8s8_z(D0, D1, D2, D3, q6_bytes(qlA_0, qhA_0, k), q6_bytes(qlA_1, qhA_1, k),
+                 q6_bytes(qlB_0, qhB_0, k), q6_bytes(qlB_1, qhB_1, k), bv & L.mA, bv & L.mB);
+      const int sc0 = sbyte(k < 2 ? tA0 : tB0, 2 * (k & 1));
+      const int sc1 = sbyte(k < 2 ? tA1 : tB1, 2 * (k & 1));
+      i00 += sc0 * D0;
+      i01 += sc0 * D1;
+      i10 += sc1 * D2;
+      i11 += sc1 * D3;
     }
   }
   const float xs = xscale[kb];
-  const float w0 = digit_weight(2 * tig), w1 = digit_weight(2 * tig + 1);
-  const float v0 = (float)i00 * w0 + (float)i01 * w1;
-  const float v1 = (float)i10 * w0 + (float)i11 * w1;
-  // -32 offset: sum over scale groups 4tig..4tig+3 of scale * (16-element sum of x)
-  const float* xg = xsum + kb * 16 + 4 * tig;
-  const uint32_t s0 = tig == 0 ? sw0[0] : tig == 1 ? sw0[1] : tig == 2 ? sw0[2] : sw0[3];
-  const uint32_t s1 = tig == 0 ? sw1[0] : tig == 1 ? sw1[1] : tig == 2 ? sw1[2] : sw1[3];
-  float o0 = 0.f, o1 = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    o0 += (float)sbyte(s0, i) * xg[i];
-    o1 += (float)sbyte(s1, i) * xg[i];
-  }
-  acc0 += d_0 * (xs * v0 - 32.f * o0);
-  acc1 += d_1 * (xs * v1 - 32.f * o1);
+  const float d_0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(b0 + 208));
+  const float d_1 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(b1 + 208));
+  // -32 offset: scale groups 4tig .. 4tig+3 (bytes of word tig)
+  const float4 xg = *reinterpret_cast<const float4*>(xsum + kb * 16 + 4 * L.tig);
+  const uint32_t t0 = L.tig == 0 ? sw0[0] : L.tig == 1 ? sw0[1] : L.tig == 2 ? sw0[2] : sw0[3];
+  const uint32_t t1 = L.tig == 0 ? sw1[0] : L.tig == 1 ? sw1[1] : L.tig == 2 ? sw1[2] : sw1[3];
+  const float o0 = (float)sbyte(t0, 0) * xg.x + (float)sbyte(t0, 1) * xg.y +
+                   (float)sbyte(t0, 2) * xg.z + (float)sbyte(t0, 3) * xg.w;
+  const float o1 = (float)sbyte(t1, 0) * xg.x + (float)sbyte(t1, 1) * xg.y +
+                   (float)sbyte(t1, 2) * xg.z + (float)sbyte(t1, 3) * xg.w;
+  acc0 += d_0 * (xs * ((float)i00 * L.w0 + (float)i01 * L.w1) - 32.f * o0);
+  acc1 += d_1 * (xs * ((float)i10 * L.w0 + (float)i11 * L.w1) - 32.f * o1);
 }
 
 // ---------------------------------------------------------------- x preparation
-// Eight consecutive GEMV inputs starting at k0 (a multiple of 8), after the prologue.
-__device__ __forceinline__ void load_input8(const GemvParams& p, int k0, float inv_rms,
-                                            float v[8]) {
+// Raw inputs of elements k0 .. k0+7 (k0 a multiple of 8): v = x (after the GQA index map
+// or bf16 widening), a = gamma (RMSNORM) or up (SILU_GATE).
+__device__ __forceinline__ void load_raw8(const GemvParams& p, int k0, float v[8], float a[8]) {
   if (p.mode == kXBf16) {
     const uint4 r = *reinterpret_cast<const uint4*>(p.xb + k0);
     const uint32_t u[4] = {r.x, r.y, r.z, r.w};
@@ -300,44 +297,67 @@ __device__ __forceinline__ void load_input8(const GemvParams& p, int k0, float i
     }
     return;
   }
+  int kx = k0;
   if (p.mode == RRR_X_GQA_V) {
     const int hpk = p.n_q / p.n_kv;
     const int head = k0 / p.hd, e = k0 % p.hd;
-    k0 = p.n_q * p.hd + p.n_kv * p.hd + (head / hpk) * p.hd + e;
+    kx = p.n_q * p.hd + p.n_kv * p.hd + (head / hpk) * p.hd + e;
   }
-  const float4 a = *reinterpret_cast<const float4*>(p.x + k0);
-  const float4 b = *reinterpret_cast<const float4*>(p.x + k0 + 4);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  if (p.mode == RRR_X_RMSNORM) {
-    const float4 ga = *reinterpret_cast<const float4*>(p.gamma + k0);
-    const float4 gb = *reinterpret_cast<const float4*>(p.gamma + k0 + 4);
-    const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(gg[i], v[i]), inv_rms);
-  } else if (p.mode == RRR_X_SILU_GATE) {
-    const float4 ua = *reinterpret_cast<const float4*>(p.x + p.K + k0);
-    const float4 ub = *reinterpret_cast<const float4*>(p.x + p.K + k0 + 4);
-    const float uu[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float s = __fdiv_rn(v[i], __fadd_rn(1.0f, expf(-v[i])));
-      v[i] = __fmul_rn(s, uu[i]);
-    }
+  const float4 x0 = *reinterpret_cast<const float4*>(p.x + kx);
+  const float4 x1 = *reinterpret_cast<const float4*>(p.x + kx + 4);
+  v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+  v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+  const float* aux = p.mode == RRR_X_RMSNORM ? p.gamma + k0
+                     : p.mode == RRR_X_SILU_GATE ? p.x + p.K + k0 : nullptr;
+  if (aux) {
+    const float4 a0 = *reinterpret_cast<const float4*>(aux);
+    const float4 a1 = *reinterpret_cast<const float4*>(aux + 4);
+    a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+    a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
   }
 }
 
+// The GEMV input from the raw values: rms_norm(x)*gamma is (gamma*x)*inv (phi4.rs:598);
+// silu(g)*u is g/(1+e^-g)*u (phi4.rs:1368-1373).
+__device__ __forceinline__ void finish8(const GemvParams& p, float v[8], const float a[8],
+                                        float inv_rms) {
+  if (p.mode == RRR_X_RMSNORM) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(a[i], v[i]), inv_rms);
+  } else if (p.mode == RRR_X_SILU_GATE) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      v[i] = __fmul_rn(__fdiv_rn(v[i], __fadd_rn(1.0f, expf(-v[i]))), a[i]);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+template <bool FRAG>
 __device__ void prepare_x(const GemvParams& p, int8_t* dig, float* xscale, float* xsum,
                           float* misc, int warp, int lane) {
-  const int NT = kNW * 32, t = warp * 32 + lane;
+  constexpr int NT = kNW * 32;
+  const int t = warp * 32 + lane;
   float inv_rms = 1.f;
   if (p.mode == RRR_X_RMSNORM) {
-    float ss = 0.f;
-    for (int k4 = t; k4 < p.K / 4; k4 += NT) {
-      const float4 v = reinterpret_cast<const float4*>(p.x)[k4];
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    const float4* x4 = reinterpret_cast<const float4*>(p.x);
+    const int K4 = p.K / 4;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int k = t;
+    for (; k + 3 * NT < K4; k += 4 * NT) {
+      const float4 a = x4[k], b = x4[k + NT], c = x4[k + 2 * NT], d = x4[k + 3 * NT];
+      s0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+      s1 += b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
+      s2 += c.x * c.x + c.y * c.y + c.z * c.z + c.w * c.w;
+      s3 += d.x * d.x + d.y * d.y + d.z * d.z + d.w * d.w;
     }
-    ss = warp_sum(ss);
+    for (; k < K4; k += NT) {
+      const float4 a = x4[k];
+      s0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+    }
+    const float ss = warp_sum((s0 + s1) + (s2 + s3));
     if (lane == 0) misc[warp] = ss;
     named_barrier(1, NT);
     float tot = 0.f;
@@ -345,41 +365,83 @@ __device__ void prepare_x(const GemvParams& p, int8_t* dig, float* xscale, float
     for (int w = 0; w < kNW; ++w) tot += misc[w];
     inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)p.K), p.eps)));
   }
-  for (int b = warp; b < p.nb; b += kNW) {
-    const int k0 = b * 256 + lane * 8;
-    float v[8];
-    load_input8(p, k0, inv_rms, v);
-    float m = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
-    m = warp_max(m);
-    const float inv = m > 0.f ? 127.f / m : 0.f;
-    uint32_t q[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
-    float s8 = 0.f;
+  // warp w digitises blocks w, w+8, ...; the next block's loads are issued before the
+  // current block is processed
+  float v[8], a[8], vn[8], an[8];
+  int b = warp;
+  if (b < p.nb) load_raw8(p, b * 256 + lane * 8, v, a);
+  for (; b < p.nb; b += kNW) {
+    const int bn = b + kNW;
+    if (bn < p.nb) load_raw8(p, bn * 256 + lane * 8, vn, an);
+    finish8(p, v, a, inv_rms);
+    float m = 0.f, s8 = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float t0 = v[i] * inv;
-      const float r0 = rintf(t0);
-      const float t1 = (t0 - r0) * 128.f;
-      const float r1 = rintf(t1);
-      const float r2 = rintf((t1 - r1) * 128.f);
-      q[0][i >> 2] |= ((uint32_t)(int)r0 & 0xFFu) << (8 * (i & 3));
-      q[1][i >> 2] |= ((uint32_t)(int)r1 & 0xFFu) << (8 * (i & 3));
-      q[2][i >> 2] |= ((uint32_t)(int)r2 & 0xFFu) << (8 * (i & 3));
+      m = fmaxf(m, fabsf(v[i]));
       s8 += v[i];
     }
+    m = warp_max(m);
+    // T = round(x * 127 * 2^14 / max) as an integer (|T| <= 127 * 2^14 < 2^22, through the
+    // 1.5 * 2^23 magic constant), split into balanced base-128 digits:
+    // T = q0 * 2^14 + q1 * 2^7 + q2 with q0 in [-127, 127], q1, q2 in [-64, 64].
+    const float inv = m > 0.f ? __fdividef(127.f * 16384.f, m) : 0.f;
+    int q0[8], q1[8], q2[8];
 #pragma unroll
-    for (int dgt = 0; dgt < 3; ++dgt)
-      *reinterpret_cast<uint2*>(dig + dgt * p.dig_stride + k0) = make_uint2(q[dgt][0], q[dgt][1]);
+    for (int i = 0; i < 8; ++i) {
+      const int T = __float_as_int(__fmaf_rn(v[i], inv, 12582912.0f)) - 0x4B400000;
+      q0[i] = (T + 8192) >> 14;
+      const int r = T - q0[i] * 16384;
+      q1[i] = (r + 64) >> 7;
+      q2[i] = r - q1[i] * 128;
+    }
+    if (FRAG) {
+      // per-lane B fragments: pair P = 4b + lane/8, group (lane>>2)&1, tig = lane&3;
+      // column n of the pair at n*64 + tig*16 holds (b0, b1) of MMA 1 and MMA 2
+      const int grp = (lane >> 2) & 1;
+      uint8_t* fb = reinterpret_cast<uint8_t*>(dig) + (b * 4 + (lane >> 3)) * 512 + (lane & 3) * 16;
+      const uint32_t m1[3] = {pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q1[0], q1[1], q1[2], q1[3]),
+                              pack4(q2[0], q2[1], q2[2], q2[3])};
+      const uint32_t m2[3] = {pack4(q0[4], q0[5], q0[6], q0[7]), pack4(q1[4], q1[5], q1[6], q1[7]),
+                              pack4(q2[4], q2[5], q2[6], q2[7])};
+#pragma unroll
+      for (int dgt = 0; dgt < 3; ++dgt)
+        *reinterpret_cast<uint4*>(fb + (grp * 4 + dgt) * 64) =
+            grp ? make_uint4(0u, m1[dgt], 0u, m2[dgt]) : make_uint4(m1[dgt], 0u, m2[dgt], 0u);
+      *reinterpret_cast<uint4*>(fb + (grp * 4 + 3) * 64) = make_uint4(0u, 0u, 0u, 0u);
+    } else {
+      const int k0 = b * 256 + lane * 8;
+      *reinterpret_cast<uint2*>(dig + k0) =
+          make_uint2(pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q0[4], q0[5], q0[6], q0[7]));
+      *reinterpret_cast<uint2*>(dig + p.dig_stride + k0) =
+          make_uint2(pack4(q1[0], q1[1], q1[2], q1[3]), pack4(q1[4], q1[5], q1[6], q1[7]));
+      *reinterpret_cast<uint2*>(dig + 2 * p.dig_stride + k0) =
+          make_uint2(pack4(q2[0], q2[1], q2[2], q2[3]), pack4(q2[4], q2[5], q2[6], q2[7]));
+    }
     const float s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
     if ((lane & 1) == 0) xsum[b * 16 + (lane >> 1)] = s16;
-    if (lane == 0) xscale[b] = m * (1.f / 127.f);
+    const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
+    if ((lane & 3) == 0) xsum[p.K / 16 + b * 8 + (lane >> 2)] = s32;
+    if (lane == 0) xscale[b] = m / 127.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[i] = vn[i];
+      a[i] = an[i];
+    }
   }
 }
 
+// Row tile j (0 = gate / plain, 1 = up) of work tile wt: first weight row and row count.
+__device__ __forceinline__ int tile_row0(const GemvParams& p, int wt, int j) {
+  return (j ? p.half_rows : 0) + wt * kTileRows;
+}
+__device__ __forceinline__ int tile_rows(const GemvParams& p, int wt) {
+  const int lim = p.out_mode ? p.half_rows : p.N;
+  return min(kTileRows, lim - wt * kTileRows);
+}
+
 // ---------------------------------------------------------------- the kernel
-template <int QT>
-__global__ void __launch_bounds__((kNW + 1) * 32) gemv_kq_kernel(const GemvParams p) {
+template <int QT, bool FRAG>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kq_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int BB = KQ<QT>::kBlockBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
@@ -387,9 +449,12 @@ __global__ void __launch_bounds__((kNW + 1) * 32) gemv_kq_kernel(const GemvParam
   int8_t* dig = reinterpret_cast<int8_t*>(smem + p.off_dig);
   float* xscale = reinterpret_cast<float*>(smem + p.off_xscale);
   float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);
+  float* xsum32 = xsum + p.K / 16;
   float* red = reinterpret_cast<float*>(smem + p.off_red);
+  float* gate = reinterpret_cast<float*>(smem + p.off_gate);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.off_misc);
   float* misc = reinterpret_cast<float*>(smem + p.off_misc + 16);
+  const int n_sub = p.out_mode ? 2 : 1;  // row tiles per work tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -398,6 +463,8 @@ __global__ void __launch_bounds__((kNW + 1) * 32) gemv_kq_kernel(const GemvParam
       mbar_init(&empty[s], kNW);
     }
     *abort_flag = 0;
+    int* cnt0 = reinterpret_cast<int*>(smem + p.off_misc + 16 + kNW * 4);
+    for (int i = 0; i < kSlots; ++i) cnt0[i] = 0;
     fence_mbarrier_init();
   }
   __syncthreads();
@@ -406,47 +473,53 @@ __global__ void __launch_bounds__((kNW + 1) * 32) gemv_kq_kernel(const GemvParam
   if (warp == kNW) {
     // ------------------------------------------------------------ producer warp
     const long long floor_total = p.total_bytes & ~15ll;
-    int it = 0, issued = 0;
+    int issued = 0, s = 0;
+    uint32_t ph = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
-      const int rows = min(kTileRows, p.N - tile * kTileRows);
-      for (int c = 0; c < p.n_chunks && ok; ++c, ++it) {
-        const int s = it % p.nstages;
-        const uint32_t ph = (uint32_t)(it / p.nstages) & 1u;
-        if (it >= p.nstages) {
-          int w = 1;
-          if (lane == 0) {
-            w = mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, kDevErrEmptyTimeout) ? 1 : 0;
-            if (!w) *abort_flag = 1;
+    for (int wt = blockIdx.x; wt < p.n_tiles && ok; wt += gridDim.x) {
+      const int rows = tile_rows(p, wt);
+      for (int j = 0; j < n_sub && ok; ++j) {
+        const int row0 = tile_row0(p, wt, j);
+        for (int c = 0; c < p.n_chunks; ++c) {
+          if (issued >= p.nstages) {
+            int w = 1;
+            if (lane == 0) {
+              w = mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, kDevErrEmptyTimeout) ? 1 : 0;
+              if (!w) *abort_flag = 1;
+            }
+            w = __shfl_sync(0xffffffffu, w, 0);
+            if (!w || *abort_flag) { ok = false; break; }
           }
-          w = __shfl_sync(0xffffffffu, w, 0);
-          if (!w || *abort_flag) { ok = false; break; }
-        }
-        const int kb0 = c * p.kc;
-        const int kcount = min(p.kc, p.nb - kb0);
-        const long long chunk = (long long)kcount * BB;
-        uint8_t* stage = smem + (size_t)s * p.stage_bytes;
-        long long a0 = 0, a1 = 0;
-        uint32_t tx = 0;
-        if (lane < rows) {
-          const long long start = (long long)(tile * kTileRows + lane) * p.row_bytes + (long long)kb0 * BB;
-          const long long end = start + chunk;
-          a0 = start & ~15ll;
-          a1 = min((end + 15) & ~15ll, floor_total);
-          if (a1 < a0) a1 = a0;
-          tx = (uint32_t)(a1 - a0);
-          // bytes after the last whole 16-B granule of the buffer: plain loads
-          for (long long q = max(a1, start); q < end; ++q)
-            stage[lane * p.row_stride + (int)(q - a0)] = p.w[q];
-        }
-        uint32_t tot = tx;
+          const int kb0 = c * p.kc;
+          const int kcount = min(p.kc, p.nb - kb0);
+          const long long chunk = (long long)kcount * BB;
+          uint8_t* stage = smem + (size_t)s * p.stage_bytes;
+          long long a0 = 0, a1 = 0;
+          uint32_t tx = 0;
+          if (lane < rows) {
+            const long long start = (long long)(row0 + lane) * p.row_bytes + (long long)kb0 * BB;
+            const long long end = start + chunk;
+            a0 = start & ~15ll;
+            a1 = min((end + 15) & ~15ll, floor_total);
+            if (a1 < a0) a1 = a0;
+            tx = (uint32_t)(a1 - a0);
+            // bytes after the last whole 16-B granule of the buffer: plain loads
+            for (long long q = max(a1, start); q < end; ++q)
+              stage[lane * p.row_stride + (int)(q - a0)] = p.w[q];
+          }
+          uint32_t tot = tx;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], tot);
-        __syncwarp();
-        if (tx > 0) bulk_g2s(stage + lane * p.row_stride, p.w + a0, tx, &full[s]);
-        ++issued;
+          for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_expect_tx(&full[s], tot);
+          __syncwarp();
+          if (tx > 0) bulk_g2s(stage + lane * p.row_stride, p.w + a0, tx, &full[s]);
+          ++issued;
+          if (++s == p.nstages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
       }
     }
     // No copy may still be in flight when the CTA exits.
@@ -455,117 +528,231 @@ __global__ void __launch_bounds__((kNW + 1) * 32) gemv_kq_kernel(const GemvParam
       for (int i = first; i < issued; ++i)
         mbar_wait_bounded(&full[i % p.nstages], (uint32_t)(i / p.nstages) & 1u, p.err,
                           kDevErrDrainTimeout);
-    }
+    }  // (runs once per CTA)
     return;
   }
 
   // -------------------------------------------------------------- consumer warps
   pdl_wait();
-  prepare_x(p, dig, xscale, xsum, misc, warp, lane);
+  prepare_x<FRAG>(p, dig, xscale, xsum, misc, warp, lane);
   named_barrier(1, kNW * 32);
 
-  const int g = lane >> 2, tig = lane & 3;
-  int it = 0, par = 0;
-  for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-    const int rows = min(kTileRows, p.N - tile * kTileRows);
-    float acc0 = 0.f, acc1 = 0.f;
-    for (int c = 0; c < p.n_chunks; ++c, ++it) {
-      const int s = it % p.nstages;
-      const uint32_t ph = (uint32_t)(it / p.nstages) & 1u;
-      bool have = (*abort_flag == 0);
-      if (have) {
-        have = mbar_wait_bounded(&full[s], ph, p.err, kDevErrFullTimeout);
-        if (!have) *abort_flag = 1;
-      }
-      if (!have) continue;
-      const int kb0 = c * p.kc;
-      const int kcount = min(p.kc, p.nb - kb0);
-      const uint8_t* stage = smem + (size_t)s * p.stage_bytes;
-      const long long base = (long long)tile * kTileRows * p.row_bytes + (long long)kb0 * BB;
-      const int off0 = (int)((base + (long long)g * p.row_bytes) & 15);
-      const int off1 = (int)((base + (long long)(g + 8) * p.row_bytes) & 15);
-      const uint8_t* r0 = stage + g * p.row_stride + off0;
-      const uint8_t* r1 = stage + (g + 8) * p.row_stride + off1;
-      for (int bi = warp; bi < kcount; bi += kNW) {
-        const uint8_t* q0 = r0 + bi * BB;
-        const uint8_t* q1 = r1 + bi * BB;
-        if constexpr (QT == RRR_Q4_K) {
-          block_q4k(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, g, tig, acc0, acc1);
-        } else if constexpr (QT == RRR_Q5_K) {
-          block_q5k(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, g, tig, acc0, acc1);
-        } else {
-          const bool al = __all_sync(0xffffffffu, (((uintptr_t)q0 | (uintptr_t)q1) & 3) == 0);
-          if (al)
-            block_q6k<true>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, g, tig, acc0, acc1);
-          else
-            block_q6k<false>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, g, tig, acc0, acc1);
+  const Lane L = make_lane(lane, QT == RRR_Q4_K);
+  int* cnt = reinterpret_cast<int*>(smem + p.off_misc + 16 + kNW * 4);
+
+  // Byte offset mod 16 of a chunk start inside its 16-byte granule (only Q6_K rows and
+  // chunks can start unaligned); 32-bit arithmetic on the residues.
+  const int rb16 = (int)(p.row_bytes & 15), cb16 = (p.kc * BB) & 15;
+  int s = 0, ts = 0, ss = 0;  // stage index, row-tile sequence, stage sequence
+  uint32_t ph = 0;    // phase parity of stage s
+  for (int wt = blockIdx.x; wt < p.n_tiles; wt += gridDim.x) {
+    const int rows = tile_rows(p, wt);
+    for (int j = 0; j < n_sub; ++j, ++ts) {
+      const int row0 = tile_row0(p, wt, j);
+      float acc0 = 0.f, acc1 = 0.f;
+      for (int c = 0; c < p.n_chunks; ++c) {
+        const int cs = s;
+        const uint32_t cph = ph;
+        if (++s == p.nstages) {
+          s = 0;
+          ph ^= 1u;
         }
+        bool have = (*abort_flag == 0);
+        if (have) {
+          have = mbar_wait_bounded(&full[cs], cph, p.err, kDevErrFullTimeout);
+          if (!have) *abort_flag = 1;
+        }
+        if (!have) continue;
+        const int kb0 = c * p.kc;
+        const int items = min(p.kc, p.nb - kb0);
+        const uint8_t* stage = smem + cs * p.stage_bytes;
+        int off0 = 0, off1 = 0;
+        if (QT == RRR_Q6_K) {
+          off0 = ((row0 + L.g) * rb16 + c * cb16) & 15;
+          off1 = ((row0 + L.g + 8) * rb16 + c * cb16) & 15;
+        }
+        const uint8_t* r0 = stage + L.g * p.row_stride + off0;
+        const uint8_t* r1 = stage + (L.g + 8) * p.row_stride + off1;
+        // Whole blocks are the work items; the warp that starts the list rotates from
+        // stage to stage so leftover blocks (12 per stage for K = 3072) spread over warps.
+        const int w0 = (warp + ss * items) % kNW;
+        ++ss;
+        for (int bi = w0; bi < items; bi += kNW) {
+          const uint8_t* q0 = r0 + bi * BB;
+          const uint8_t* q1 = r1 + bi * BB;
+          if constexpr (QT == RRR_Q6_K) {
+            const bool al = __all_sync(0xffffffffu, (((uintptr_t)q0 | (uintptr_t)q1) & 3) == 0);
+            if (al)
+              block_q6<true>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
+            else
+              block_q6<false>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
+          } else {
+            block_q45<QT, FRAG>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum32, L, acc0, acc1);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[cs]);
+      }
+      // Row sums of this warp (over the 4 lanes of a row), parked in slot ts % kSlots; the
+      // last warp to finish the tile (shared counter) adds the warps' sums in warp order
+      // and stores the rows: no CTA-wide barrier, warps run ahead into the next tile.
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+      const int slot = ts % kSlots;
+      float* rb = red + slot * kNW * kTileRows;
+      if (L.tig == 0) {
+        rb[warp * kTileRows + L.g] = acc0;
+        rb[warp * kTileRows + L.g + 8] = acc1;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-    float* rb = red + par * kNW * kTileRows;
-    if (tig == 0) {
-      rb[warp * kTileRows + g] = acc0;
-      rb[warp * kTileRows + g + 8] = acc1;
-    }
-    named_barrier(1, kNW * 32);
-    if (threadIdx.x < rows && *abort_flag == 0) {
-      float v = 0.f;
+      int last = 0;
+      if (lane == 0) {
+        __threadfence_block();
+        last = atomicAdd(&cnt[slot], 1) == kNW - 1;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence_block();
+        if (lane < rows && *abort_flag == 0) {
+          float v = 0.f;
 #pragma unroll
-      for (int w = 0; w < kNW; ++w) v += rb[w * kTileRows + threadIdx.x];
-      const int row = tile * kTileRows + threadIdx.x;
-      if (p.residual) v = p.residual[row] + v;
-      p.y[row] = v;
+          for (int w = 0; w < kNW; ++w) v += rb[w * kTileRows + lane];
+          if (p.out_mode == 0) {
+            const int row = row0 + lane;
+            if (p.residual) v = p.residual[row] + v;
+            p.y[row] = v;
+          } else if (j == 0) {
+            gate[slot * kTileRows + lane] = v;
+          } else {
+            // gate of this work tile was finalised (by some warp) before every warp
+            // arrived here
+            const float g = gate[((ts - 1) % kSlots) * kTileRows + lane];
+            const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+            p.y[wt * kTileRows + lane] = __fmul_rn(sg, v);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) cnt[slot] = 0;
+      }
     }
-    par ^= 1;
   }
+}
+
+// Shared-memory layout of one launch. FRAG: the x digits are stored as ready-made per-lane
+// B fragments (8 bytes per element; Q4_K / Q5_K) instead of three compact digit rows.
+template <int QT>
+int plan_layout(GemvParams& p, bool frag) {
+  constexpr int BB = KQ<QT>::kBlockBytes;
+  const int chunk = p.kc * BB;
+  const bool aligned16 = (p.row_bytes % 16 == 0) && (chunk % 16 == 0);
+  // Stage row stride: room for the chunk plus the 16-byte rounding of unaligned chunk
+  // starts, padded so that rows fall in distinct shared-memory banks (the Q4_K/Q5_K
+  // 8-byte reads of 4 rows, the Q6_K 4-byte reads of 8 rows).
+  const int need = chunk + (aligned16 ? 0 : 30);
+  const int target = (QT == RRR_Q6_K) ? 16 : 96;
+  int rs = (need / 128) * 128 + target;
+  if (rs < need) rs += 128;
+  p.row_stride = rs;
+  p.stage_bytes = kTileRows * p.row_stride;
+  p.dig_stride = p.K + 96;
+  const int dig_bytes = frag ? p.K * 8 : 3 * p.dig_stride;
+  int fixed = 2 * kMaxStages * 8 + dig_bytes + 16;
+  fixed += p.nb * 4 + 16 + (p.K / 16) * 4 + (p.K / 32) * 4;  // xscale, xsum16, xsum32
+  fixed += kSlots * kNW * kTileRows * 4;                     // red
+  fixed += kSlots * kTileRows * 4 + 16 + kNW * 4 + kSlots * 4 + 64;  // gate, misc
+  p.nstages = std::max(2, std::min(kMaxStages, (kSmemBudget - fixed) / p.stage_bytes));
+  int off = p.nstages * p.stage_bytes;
+  p.off_bars = off;          off += 2 * p.nstages * 8;
+  off = (off + 15) & ~15;
+  p.off_dig = off;           off += dig_bytes;
+  off = (off + 15) & ~15;
+  p.off_xscale = off;        off += p.nb * 4;
+  off = (off + 15) & ~15;
+  p.off_xsum = off;          off += (p.K / 16) * 4 + (p.K / 32) * 4;  // xsum16, xsum32
+  p.off_red = off;           off += kSlots * kNW * kTileRows * 4;
+  p.off_gate = off;          off += kSlots * kTileRows * 4;
+  p.off_misc = off;          off += 16 + kNW * 4 + kSlots * 4;
+  return (off + 127) & ~127;
+}
+
+struct OccEntry {
+  const void* fn;
+  int dev, smem, per_sm;
+};
+
+template <int QT, bool FRAG>
+cudaError_t launch_k(const LaunchEnv& env, const GemvParams& p, int smem) {
+  auto kern = gemv_kq_kernel<QT, FRAG>;
+  // Kernel attribute and occupancy per (kernel, device, shared-memory size), computed once:
+  // the launch path stays a single cudaLaunchKernelEx.
+  static thread_local OccEntry cache[32];
+  static thread_local int n_cache = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int per_sm = 0;
+  for (int i = 0; i < n_cache; ++i)
+    if (cache[i].fn == (const void*)kern && cache[i].dev == dev && cache[i].smem == smem)
+      per_sm = cache[i].per_sm;
+  if (per_sm == 0) {
+    // the attribute is per kernel: set it to the device maximum so that every layout of
+    // this kernel (different K) can launch
+    int optin = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    if (smem > optin) return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    if (n_cache < 32) cache[n_cache++] = OccEntry{(const void*)kern, dev, smem, per_sm};
+  }
+  // Two CTAs per SM (two producers and 16 consumer warps per SM); RRR_GEMV_CTAS_PER_SM
+  // overrides.
+  static int ctas_per_sm = [] {
+    const char* e = getenv("RRR_GEMV_CTAS_PER_SM");
+    const int v = e ? atoi(e) : 2;
+    return v >= 1 && v <= 4 ? v : 2;
+  }();
+  const int grid = std::min(p.n_tiles, std::min(per_sm, ctas_per_sm) * env.sm_count);
+  return rrr_launch_pdl(kern, dim3(grid), dim3(kThreads), smem, env.stream, env.pdl, p);
 }
 
 template <int QT>
 cudaError_t launch_t(const LaunchEnv& env, GemvParams& p) {
-  constexpr int BB = KQ<QT>::kBlockBytes;
   const int kc_max = (QT == RRR_Q6_K) ? 8 : 12;
   const int n_ch = (p.nb + kc_max - 1) / kc_max;
   p.kc = (p.nb + n_ch - 1) / n_ch;
   p.n_chunks = (p.nb + p.kc - 1) / p.kc;
-  p.n_tiles = (p.N + kTileRows - 1) / kTileRows;
-  const int chunk = p.kc * BB;
-  p.row_stride = ((chunk + 32 + 127) / 128) * 128 + (QT == RRR_Q6_K ? 16 : 32);
-  p.stage_bytes = kTileRows * p.row_stride;
-  p.nstages = 2;
-  p.dig_stride = p.K + 96;
-  int off = p.nstages * p.stage_bytes;
-  p.off_bars = off;          off += 2 * p.nstages * 8;
-  p.off_dig = off;           off += 3 * p.dig_stride;
-  off = (off + 15) & ~15;
-  p.off_xscale = off;        off += p.nb * 4;
-  p.off_xsum = off;          off += (p.K / 16) * 4;
-  p.off_red = off;           off += 2 * kNW * kTileRows * 4;
-  p.off_misc = off;          off += 16 + kNW * 4;
-  const int smem = (off + 127) & ~127;
-
-  static unsigned long long configured = 0;  // one bit per device ordinal
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kq_kernel<QT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    configured |= 1ull << (dev & 63);
+  p.half_rows = p.out_mode ? p.N / 2 : 0;
+  const int lim = p.out_mode ? p.half_rows : p.N;
+  p.n_tiles = (lim + kTileRows - 1) / kTileRows;
+  if constexpr (QT != RRR_Q6_K) {
+    // fragment layout when three stages still fit beside it
+    GemvParams q = p;
+    const int smem = plan_layout<QT>(q, true);
+    if (q.nstages >= 3 || (QT == RRR_Q5_K && q.nstages >= 2 && p.K <= 4096)) {
+      p = q;
+      return launch_k<QT, true>(env, p, smem);
+    }
   }
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kq_kernel<QT>,
-                                                                (kNW + 1) * 32, smem);
-  if (e != cudaSuccess) return e;
-  if (per_sm < 1) return cudaErrorInvalidConfiguration;
-  const int grid = std::min(p.n_tiles, per_sm * env.sm_count);
-  return rrr_launch_pdl(gemv_kq_kernel<QT>, dim3(grid), dim3((kNW + 1) * 32), smem,
-                        env.stream, env.pdl, p);
+  const int smem = plan_layout<QT>(p, false);
+  return launch_k<QT, false>(env, p, smem);
+}
+
+cudaError_t launch_any(const LaunchEnv& env, int qtype, GemvParams& p) {
+  p.nb = p.K / 256;
+  p.row_bytes = (long long)p.nb * kq_block_bytes(qtype);
+  p.total_bytes = p.row_bytes * p.N;
+  p.err = env.d_err;
+  switch (qtype) {
+    case RRR_Q4_K: return launch_t<RRR_Q4_K>(env, p);
+    case RRR_Q5_K: return launch_t<RRR_Q5_K>(env, p);
+    case RRR_Q6_K: return launch_t<RRR_Q6_K>(env, p);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 // ---------------------------------------------------------------- layout self-test
@@ -615,16 +802,26 @@ cudaError_t launch_gemv_kq(const LaunchEnv& env, int qtype, const void* w, const
   p.hd = pro ? pro->head_dim : 0;
   p.K = K;
   p.N = N;
-  p.nb = K / 256;
-  p.row_bytes = (long long)p.nb * kq_block_bytes(qtype);
-  p.total_bytes = p.row_bytes * N;
-  p.err = env.d_err;
-  switch (qtype) {
-    case RRR_Q4_K: return launch_t<RRR_Q4_K>(env, p);
-    case RRR_Q5_K: return launch_t<RRR_Q5_K>(env, p);
-    case RRR_Q6_K: return launch_t<RRR_Q6_K>(env, p);
-    default: return cudaErrorInvalidValue;
-  }
+  return launch_any(env, qtype, p);
+}
+
+cudaError_t launch_gemv_kq_swiglu(const LaunchEnv& env, int qtype, const void* w,
+                                  const float* x, float* y, int K, int F,
+                                  const rrr_gemv_prologue* pro) {
+  GemvParams p = {};
+  p.w = static_cast<const uint8_t*>(w);
+  p.x = x;
+  p.y = y;
+  p.out_mode = 1;
+  p.mode = pro ? pro->mode : RRR_X_PLAIN;
+  p.gamma = pro ? pro->gamma : nullptr;
+  p.eps = pro ? pro->eps : 0.f;
+  p.n_q = pro ? pro->n_q_heads : 0;
+  p.n_kv = pro ? pro->n_kv_heads : 0;
+  p.hd = pro ? pro->head_dim : 0;
+  p.K = K;
+  p.N = 2 * F;
+  return launch_any(env, qtype, p);
 }
 
 cudaError_t launch_gemv_kq_bf16(const LaunchEnv& env, int qtype, const void* w,
@@ -636,16 +833,7 @@ cudaError_t launch_gemv_kq_bf16(const LaunchEnv& env, int qtype, const void* w,
   p.mode = kXBf16;
   p.K = K;
   p.N = N;
-  p.nb = K / 256;
-  p.row_bytes = (long long)p.nb * kq_block_bytes(qtype);
-  p.total_bytes = p.row_bytes * N;
-  p.err = env.d_err;
-  switch (qtype) {
-    case RRR_Q4_K: return launch_t<RRR_Q4_K>(env, p);
-    case RRR_Q5_K: return launch_t<RRR_Q5_K>(env, p);
-    case RRR_Q6_K: return launch_t<RRR_Q6_K>(env, p);
-    default: return cudaErrorInvalidValue;
-  }
+  return launch_any(env, qtype, p);
 }
 
 cudaError_t launch_mma_selftest(const LaunchEnv& env, int* d_ok) {

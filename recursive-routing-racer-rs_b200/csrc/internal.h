@@ -33,7 +33,14 @@ cudaError_t launch_logits_f32(const LaunchEnv& env, const float* W, const float*
 cudaError_t launch_silu_gate(const LaunchEnv& env, const float* gu, float* out, int F);
 cudaError_t launch_residual_add(const LaunchEnv& env, const float* a, const float* b,
                                 float* out, int n);
-cudaError_t launch_argmax(const LaunchEnv& env, const float* x, int n, int* out_index);
+// scratch: 16 bytes of zero-initialised device memory (a 64-bit key and a 32-bit counter),
+// left zeroed by every completed launch; one launch at a time per scratch slot.
+cudaError_t launch_argmax(const LaunchEnv& env, const float* x, int n, int* out_index,
+                          void* scratch);
+// gate_up GEMV with the SwiGLU epilogue: W has 2F rows [gate; up], y[i] = silu(gate_i) * up_i.
+cudaError_t launch_gemv_kq_swiglu(const LaunchEnv& env, int qtype, const void* w,
+                                  const float* x, float* y, int K, int F,
+                                  const rrr_gemv_prologue* pro);
 cudaError_t launch_matmul_f32(const LaunchEnv& env, const float* A, const float* B, float* C,
                               int M, int K, int N);
 cudaError_t launch_fill_kquant(const LaunchEnv& env, int qtype, void* dst, int64_t n_blocks,

@@ -148,16 +148,22 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
   return ((unsigned long long)b << 32) | (uint32_t)(~(uint32_t)idx);
 }
 
-// Single-CTA greedy argmax: first maximum wins, NaN is skipped (reference scan
-// `if src[j] > best_val`, phi4.rs:1172-1183); index 0 when nothing compares greater
-// than -inf.
+// Greedy argmax: first maximum wins, NaN is skipped (reference scan
+// `if src[j] > best_val`, phi4.rs:1172-1183); index 0 when nothing compares greater than
+// -inf. Each CTA reduces its range to one order-preserving key and folds it into `key`
+// with an atomic max (order-independent, so the result is deterministic); the last CTA to
+// finish (counter) converts the key to the index and resets key and counter to zero for
+// the next call.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int n,
-                                                      int* __restrict__ out) {
+                                                      int* __restrict__ out,
+                                                      unsigned long long* key,
+                                                      unsigned int* counter) {
   __shared__ unsigned long long sh[32];
+  __shared__ bool last;
   pdl_launch_dependents();
   pdl_wait();
   unsigned long long best = 0ull;
-  for (int i = threadIdx.x; i < n; i += 1024) {
+  for (int i = blockIdx.x * 1024 + threadIdx.x; i < n; i += gridDim.x * 1024) {
     const float v = x[i];
     if (v == v && v > -INFINITY) {
       const unsigned long long k = argmax_key(v, i);
@@ -178,7 +184,18 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
       const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
       best = t > best ? t : best;
     }
-    if (threadIdx.x == 0) *out = best ? (int)(~(uint32_t)(best & 0xFFFFFFFFull)) : 0;
+    if (threadIdx.x == 0) {
+      if (best) atomicMax(key, best);
+      __threadfence();
+      last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    }
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    const unsigned long long k = atomicExch(key, 0ull);
+    *out = k ? (int)(~(uint32_t)(k & 0xFFFFFFFFull)) : 0;
+    atomicExch(counter, 0u);
   }
 }
 
@@ -341,9 +358,13 @@ cudaError_t launch_residual_add(const LaunchEnv& env, const float* a, const floa
                         out, n);
 }
 
-cudaError_t launch_argmax(const LaunchEnv& env, const float* x, int n, int* out_index) {
-  return rrr_launch_pdl(argmax_kernel, dim3(1), dim3(1024), 0, env.stream, env.pdl, x, n,
-                        out_index);
+cudaError_t launch_argmax(const LaunchEnv& env, const float* x, int n, int* out_index,
+                          void* scratch) {
+  unsigned long long* key = static_cast<unsigned long long*>(scratch);
+  unsigned int* counter = reinterpret_cast<unsigned int*>(key + 1);
+  const int grid = std::max(1, std::min((n + 4095) / 4096, env.sm_count));
+  return rrr_launch_pdl(argmax_kernel, dim3(grid), dim3(1024), 0, env.stream, env.pdl, x, n,
+                        out_index, key, counter);
 }
 
 cudaError_t launch_matmul_f32(const LaunchEnv& env, const float* A, const float* B, float* C,

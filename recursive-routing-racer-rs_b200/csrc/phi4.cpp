@@ -4,10 +4,10 @@
 //
 // Per layer the reference issues 11 dispatches (rmsnorm, qkv, rope_kv_store, attention,
 // o-proj, residual_add, rmsnorm, ffn_up, silu_gate, ffn_down, residual_add). Here the
-// norms, the SiLU gate, the attention output at position 0 and both residual adds are
-// fused into the four GEMVs (prologues / epilogues of rrr_gemv_kq_ex), so a layer is 4
-// launches and the step is 4*L + logits chunks (+ argmax). The whole step can be
-// captured once into a CUDA graph and replayed.
+// norms, the attention output at position 0 and both residual adds are fused into the
+// GEMV prologues / epilogues (rrr_gemv_kq_ex) and SiLU(gate)*up into the gate_up GEMV's
+// epilogue (rrr_gemv_kq_swiglu), so a layer is 4 launches and the step is
+// 4*L + logits chunks (+ argmax). The whole step can be captured once into a CUDA graph.
 #include <cuda_runtime.h>
 
 #include <vector>
@@ -21,7 +21,8 @@ struct rrr_phi4 {
   rrr_phi4_desc d{};
   std::vector<rrr_phi4_layer> layers;
   float* qkv = nullptr;      // f32[n_q*hd + 2*n_kv*hd]
-  float* gate_up = nullptr;  // f32[2*ffn]
+  float* mid = nullptr;      // f32[ffn]: silu(gate) * up
+  void* argmax_scratch = nullptr;  // 16 B, kept zeroed by the argmax kernel
   // graph cache
   cudaGraphExec_t exec = nullptr;
   cudaGraph_t graph = nullptr;
@@ -47,18 +48,20 @@ static int phi4_issue(rrr_phi4* m, float* hidden, float* logits, int* argmax, vo
                              d.d_model, hidden, &pv, stream)))
       return rc;
     rrr_gemv_prologue pf{RRR_X_RMSNORM, L.ffn_norm, d.rms_eps, 0, 0, 0};
-    if ((rc = rrr_gemv_kq_ex(ctx, L.gate_up_type, L.w_gate_up, hidden, m->gate_up, d.d_model,
-                             2 * d.ffn_dim, nullptr, &pf, stream)))
+    if ((rc = rrr_gemv_kq_swiglu(ctx, L.gate_up_type, L.w_gate_up, hidden, m->mid, d.d_model,
+                                 d.ffn_dim, &pf, stream)))
       return rc;
-    rrr_gemv_prologue ps{RRR_X_SILU_GATE, nullptr, 0.f, 0, 0, 0};
-    if ((rc = rrr_gemv_kq_ex(ctx, L.down_type, L.w_down, m->gate_up, hidden, d.ffn_dim, d.d_model,
-                             hidden, &ps, stream)))
+    if ((rc = rrr_gemv_kq_ex(ctx, L.down_type, L.w_down, m->mid, hidden, d.ffn_dim, d.d_model,
+                             hidden, nullptr, stream)))
       return rc;
   }
   if ((rc = rrr_logits_f32(ctx, d.w_out, hidden, logits, d.vocab, d.d_model, d.logits_chunk_rows,
                            d.output_norm, d.rms_eps, stream)))
     return rc;
-  if (argmax && (rc = rrr_argmax_f32(ctx, logits, d.vocab, argmax, stream))) return rc;
+  if (argmax) {
+    cudaError_t e = launch_argmax(make_env(ctx, stream), logits, d.vocab, argmax, m->argmax_scratch);
+    if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_phi4_forward: argmax launch");
+  }
   return RRR_OK;
 }
 
@@ -99,7 +102,9 @@ int rrr_phi4_create(rrr_ctx* ctx, const rrr_phi4_desc* desc, rrr_phi4** out) {
   m->d.layers = nullptr;
   const size_t qkv_dim = (size_t)(d.n_heads + 2 * d.n_kv_heads) * d.head_dim;
   cudaError_t e = cudaMalloc(&m->qkv, qkv_dim * sizeof(float));
-  if (e == cudaSuccess) e = cudaMalloc(&m->gate_up, 2 * (size_t)d.ffn_dim * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&m->mid, (size_t)d.ffn_dim * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&m->argmax_scratch, 64);
+  if (e == cudaSuccess) e = cudaMemset(m->argmax_scratch, 0, 64);
   if (e != cudaSuccess) {
     rrr_phi4_destroy(m);
     return cuda_error(ctx, e, "rrr_phi4_create: scratch allocation");
@@ -161,7 +166,8 @@ int rrr_phi4_destroy(rrr_phi4* m) {
   phi4_drop_graph(m);
   if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
   if (m->qkv) cudaFree(m->qkv);
-  if (m->gate_up) cudaFree(m->gate_up);
+  if (m->mid) cudaFree(m->mid);
+  if (m->argmax_scratch) cudaFree(m->argmax_scratch);
   delete m;
   return RRR_OK;
 }

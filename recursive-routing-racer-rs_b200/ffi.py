@@ -76,6 +76,7 @@ PROTOS = {
     "rrr_selftest_mma": (c_int, [vp, POINTER(c_int)]),
     "rrr_gemv_kq": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, vp, vp]),
     "rrr_gemv_kq_ex": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, vp, POINTER(GemvPrologue), vp]),
+    "rrr_gemv_kq_swiglu": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, POINTER(GemvPrologue), vp]),
     "rrr_dequant_kq": (c_int, [vp, c_int, vp, vp, c_int64, vp]),
     "rrr_gemm_kq_batched": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, c_int, vp]),
     "rrr_rmsnorm": (c_int, [vp, vp, vp, vp, c_int, c_int, c_float, vp]),

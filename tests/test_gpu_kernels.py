@@ -173,6 +173,23 @@ def test_gemv_prologue_gqa_v(rrr, ctx, oracle, G, qt):
     assert rel_l2(got, ref) < TOL
 
 
+@pytest.mark.parametrize("qt", QTYPES)
+@pytest.mark.parametrize("K,F,norm", [(3072, 8192, True), (512, 40, False), (256, 17, True)])
+def test_gemv_swiglu_epilogue(rrr, ctx, oracle, G, qt, K, F, norm):
+    """gate_up GEMV with silu(gate)*up fused (W rows [gate; up])."""
+    rng = np.random.default_rng(K + F + qt)
+    raw = oracle.random_blocks(qt, 2 * F * (K // 256), rng)
+    h = (rng.standard_normal(K) * 2).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, K).astype(np.float32)
+    gd, hd, y = G.dev(gamma), G.dev(h), G.empty_f32(F)
+    wd = G.dev(raw)
+    pro = rrr.ffi.GemvPrologue(rrr.ffi.X_RMSNORM if norm else rrr.ffi.X_PLAIN, gd.data_ptr(), 1e-5, 0, 0, 0)
+    ctx.check(rrr.ffi.lib().rrr_gemv_kq_swiglu(ctx.h, qt, vp(wd), vp(hd), vp(y), K, F, ctypes.byref(pro), None))
+    x = oracle.rms_norm(h, gamma, 1e-5) if norm else h
+    ref = oracle.silu_gate(oracle.gemv_kq(qt, raw, x, K, 2 * F, threads=8))
+    assert rel_l2(G.host(y), ref) < TOL
+
+
 def test_gemv_error_codes(rrr, ctx, oracle, G):
     L = rrr.ffi.lib()
     raw = G.dev(oracle.random_blocks(12, 4, np.random.default_rng(0)))  # held for the test
