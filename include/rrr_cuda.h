@@ -158,6 +158,19 @@ int rrr_residual_add(rrr_ctx* ctx, const float* a, const float* b, float* out, i
  * wins on ties, NaN is never selected. out_index: device int32[1]. */
 int rrr_argmax_f32(rrr_ctx* ctx, const float* x, int n, int* out_index, void* stream);
 
+/* Allocation-free argmax (no counterpart in the reference). For callers that cannot
+ * allocate device memory — a host whose memory is fully reserved by its own caching
+ * allocator, code running inside a stream capture it does not own (cudaMalloc is not
+ * allowed there), latency-critical paths that cannot afford cudaMalloc's implicit
+ * synchronisation — and so cannot create a context: takes no context, calls no
+ * cudaMalloc / cudaFree, and uses a fixed file-scope device scratch array (16 KB on every
+ * GPU that loads this library, until the process exits). Same result as rrr_argmax_f32.
+ * Limit: 1 <= n <= 8,388,608 (larger n is rejected with RRR_ERR_BAD_SHAPE). The first
+ * call on a device looks up the scratch array's device address; make that first call
+ * before any stream capture. Every call shares the scratch array, so calls that overlap
+ * on the GPU (concurrent streams) race; serialise them. Errors: rrr_last_error(NULL). */
+int rrr_argmax_f32_noalloc(const float* x, int n, int* out_index, void* stream);
+
 /* f32 GEMM C[M,N] = A[M,K] B[K,N] with B in the reference's transposed chunk layout
  * ([K, N] row-major, phi4.rs:874-893); the `matmul_tiled` / `matmul_reg_tiled`
  * shaders (push [M, K, N], ops.rs:65-84). */

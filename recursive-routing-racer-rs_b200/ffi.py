@@ -84,6 +84,7 @@ PROTOS = {
     "rrr_silu_gate": (c_int, [vp, vp, vp, c_int, vp]),
     "rrr_residual_add": (c_int, [vp, vp, vp, vp, c_int, vp]),
     "rrr_argmax_f32": (c_int, [vp, vp, c_int, vp, vp]),
+    "rrr_argmax_f32_noalloc": (c_int, [vp, c_int, vp, vp]),
     "rrr_matmul_f32": (c_int, [vp, vp, vp, vp, c_int, c_int, c_int, vp]),
     "rrr_dispatch_by_name": (c_int, [vp, c_char_p, POINTER(vp), POINTER(c_uint64), c_int, vp, c_int, vp]),
     "rrr_batch_create": (c_int, [vp, POINTER(vp)]),
