@@ -1,0 +1,92 @@
+"""Small, self-checking workloads for profiling one kernel at a time under ncu.
+
+Each case builds its inputs on cuda:0, runs a few warm-up rounds and then the launches a
+capture selects (`ncu -k regex:<kernel> -s <skip> -c <count>`), checks the context's
+device error flag and prints "<case> ok". Sizes are the Phi-4-mini layer shapes, so the
+DRAM figures of a capture are those of the bench's per-GEMV lines.
+
+    python -m recursive-routing-racer-rs_b200.profcases gemv            # 3 GEMV shapes x 6
+    python -m recursive-routing-racer-rs_b200.profcases decode --layers 32
+    python -m recursive-routing-racer-rs_b200.profcases gemm --m 256    # batched tcgen05 GEMM
+"""
+import argparse
+import importlib
+from ctypes import c_void_p
+
+_PKG = "recursive-routing-racer-rs_b200"
+BLOCK_BYTES = {12: 144, 13: 176, 14: 210}
+
+
+def _weights(ctx, L, torch, qt, K, N, seed):
+    nb = N * (K // 256)
+    w = torch.empty(nb * BLOCK_BYTES[qt], dtype=torch.uint8, device="cuda")
+    ctx.check(L.rrr_fill_kquant_random(ctx.h, qt, c_void_p(w.data_ptr()), nb, seed, None))
+    return w
+
+
+def case_gemv(ctx, L, torch, args):
+    """gate_up Q4_K 16384x3072, o_proj Q4_K 3072x3072, down Q6_K 3072x8192; `rounds` rounds."""
+    shapes = [(12, 3072, 16384), (12, 3072, 3072), (14, 8192, 3072)]
+    bufs = []
+    for qt, K, N in shapes:
+        w = _weights(ctx, L, torch, qt, K, N, 7)
+        bufs.append((qt, K, N, w, torch.randn(K, device="cuda"), torch.empty(N, device="cuda")))
+    torch.cuda.synchronize()
+    for _ in range(args.rounds):
+        for qt, K, N, w, x, y in bufs:
+            ctx.check(L.rrr_gemv_kq(ctx.h, qt, c_void_p(w.data_ptr()), c_void_p(x.data_ptr()),
+                                    c_void_p(y.data_ptr()), K, N, None, None))
+
+
+def case_decode(ctx, L, torch, args):
+    """Eager decode steps of the synthetic Phi-4-mini model (136 launches per step at 32 layers)."""
+    phi4 = importlib.import_module(_PKG + ".phi4")
+    cfg = phi4.ModelConfig(n_layers=args.layers)
+    m = phi4.SyntheticPhi4(ctx, cfg, seed=5)
+    dec = phi4.Phi4Decoder(ctx, m)
+    h = torch.randn(cfg.d_model, device="cuda")
+    lg = torch.empty(cfg.vocab_size, device="cuda")
+    am = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for _ in range(args.rounds):
+        dec.forward(h.data_ptr(), lg.data_ptr(), am.data_ptr(), False)
+
+
+def case_gemm(ctx, L, torch, args):
+    """Batched GEMM, M = --m tokens, on gate_up Q4_K 16384x3072 and down Q6_K 3072x8192."""
+    shapes = [(12, 3072, 16384), (14, 8192, 3072)]
+    bufs = []
+    for qt, K, N in shapes:
+        w = _weights(ctx, L, torch, qt, K, N, 11)
+        x = torch.randn(args.m, K, device="cuda").to(torch.bfloat16)
+        bufs.append((qt, K, N, w, x, torch.empty(args.m, N, device="cuda")))
+    torch.cuda.synchronize()
+    for _ in range(args.rounds):
+        for qt, K, N, w, x, y in bufs:
+            ctx.check(L.rrr_gemm_kq_batched(ctx.h, qt, c_void_p(w.data_ptr()), c_void_p(x.data_ptr()),
+                                            c_void_p(y.data_ptr()), args.m, K, N, None))
+
+
+CASES = {"gemv": case_gemv, "decode": case_decode, "gemm": case_gemm}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("--rounds", type=int, default=6)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--m", type=int, default=256)
+    args = ap.parse_args(argv)
+    import torch
+    rrr = importlib.import_module(_PKG)
+    L = rrr.ffi.lib()
+    ctx = rrr.Context(0)
+    CASES[args.case](ctx, L, torch, args)
+    torch.cuda.synchronize()
+    err = ctx.device_error()
+    if err != 0:
+        raise SystemExit("device error flag %d" % err)
+    print("%s ok" % args.case)
+
+
+if __name__ == "__main__":
+    main()
