@@ -34,6 +34,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
+# DRAM bytes (read + write) of one gate_up GEMV launch, from the ncu capture summarised in
+# profiles/gemv_kq_phi4_layer_shapes.md (28,363,520 read + 0 written; the algorithmic
+# bytes are 28,389,376).
+GATE_UP_DRAM_BYTES = 28363520
 METRIC = "K-quant GEMV HBM GB/s (% of peak) per B200; Phi-4-mini-shape decode tok/s"
 
 
@@ -328,7 +332,9 @@ def run_ours(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "kernel": "gemv_kq_kernel<Q4_K> (gate_up)",
                          "achieved": dom["GBps"], "peak": peak, "unit": "GB/s",
                          "frac": round(dom["GBps"] / peak, 4), "peak_source": peak_src,
-                         "traffic": None},
+                         "traffic": GATE_UP_DRAM_BYTES,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one gate_up "
+                                           "launch (profiles/gemv_kq_phi4_layer_shapes.md)"},
             "decode": decode,
             "e2e": {"value": round(bytes_step / e2e_ms / 1e6, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -153,6 +153,8 @@ int rrr_destroy(rrr_ctx* ctx) {
   bind_device(ctx);
   cudaDeviceSynchronize();
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->tc_ws) cudaFree(ctx->tc_ws);
+  if (ctx->tc_counters) cudaFree(ctx->tc_counters);
   delete ctx;
   return RRR_OK;
 }
@@ -363,11 +365,32 @@ int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w, const uint16_t* 
     return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemm_kq_batched: Y must not overlap X");
   RRR_BIND(ctx);
   const LaunchEnv env = make_env(ctx, stream);
-  if (M >= 16) {
-    cudaError_t e = launch_gemm_kq_tc(env, qtype, w, x, y, M, K, N);
-    if (e == cudaSuccess) return RRR_OK;
-    if (e != cudaErrorNotSupported) return cuda_error(ctx, e, "rrr_gemm_kq_batched launch");
-    cudaGetLastError();
+  TcPlan plan;
+  if (M >= 16 && plan_gemm_kq_tc(qtype, M, K, N, ctx->sm_count, &plan)) {
+    // grow the split-K workspace (kept by the context; the counters start at zero and
+    // every completed launch leaves them at zero)
+    if (plan.ws_floats > ctx->tc_ws_floats) {
+      if (ctx->tc_ws) cudaFree(ctx->tc_ws);
+      ctx->tc_ws = nullptr;
+      ctx->tc_ws_floats = 0;
+      RRR_LAUNCH_CHECK(ctx, cudaMalloc(&ctx->tc_ws, plan.ws_floats * sizeof(float)),
+                       "rrr_gemm_kq_batched: workspace");
+      ctx->tc_ws_floats = plan.ws_floats;
+    }
+    if (plan.n_counters > ctx->tc_n_counters) {
+      if (ctx->tc_counters) cudaFree(ctx->tc_counters);
+      ctx->tc_counters = nullptr;
+      ctx->tc_n_counters = 0;
+      RRR_LAUNCH_CHECK(ctx, cudaMalloc(&ctx->tc_counters, plan.n_counters * sizeof(unsigned)),
+                       "rrr_gemm_kq_batched: tile counters");
+      RRR_LAUNCH_CHECK(ctx, cudaMemset(ctx->tc_counters, 0, plan.n_counters * sizeof(unsigned)),
+                       "rrr_gemm_kq_batched: tile counters");
+      ctx->tc_n_counters = plan.n_counters;
+    }
+    const TcWorkspace wsp{ctx->tc_ws, ctx->tc_counters};
+    RRR_LAUNCH_CHECK(ctx, launch_gemm_kq_tc(env, qtype, w, x, y, M, K, N, plan, wsp),
+                     "rrr_gemm_kq_batched (tensor cores) launch");
+    return RRR_OK;
   }
   for (int m = 0; m < M; ++m)
     RRR_LAUNCH_CHECK(ctx, launch_gemv_kq_bf16(env, qtype, w, x + (size_t)m * K, y + (size_t)m * N, K, N),

@@ -368,6 +368,60 @@ def test_gemm_batched(rrr, ctx, oracle, G, qt, M):
         assert rel_l2(got[m], oracle.gemv_kq(qt, raw, Xf[m], K, N)) < 1e-2
 
 
+def _gemm_tc_case(rrr, ctx, oracle, G, qt, M, K, N, seed, repeats=1):
+    """Runs rrr_gemm_kq_batched `repeats` times; returns (outputs, f32 reference)."""
+    import torch
+    rng = np.random.default_rng(seed)
+    raw = oracle.random_blocks(qt, N * (K // 256), rng)
+    X = torch.randn(M, K, dtype=torch.bfloat16)
+    W = oracle.dequant(qt, raw, N * K).reshape(N, K).astype(np.float64)
+    ref = (X.float().numpy().astype(np.float64) @ W.T).astype(np.float32)
+    wd, xd = G.dev(raw), X.cuda()
+    outs = []
+    for _ in range(repeats):
+        Y = G.empty_f32(M * N)
+        Y.fill_(float("nan"))
+        ctx.check(rrr.ffi.lib().rrr_gemm_kq_batched(ctx.h, qt, vp(wd), vp(xd), vp(Y), M, K, N, None))
+        outs.append(G.host(Y).reshape(M, N))
+    assert ctx.device_error() == 0
+    return outs, ref
+
+
+# Tensor-core tile path (M >= 16): split-K (tile grid smaller than the GPU) and single
+# split (more than 148 row tiles), ragged row and token tiles, Q6_K rows that are not
+# 16-byte aligned (K = 768: 630-byte rows), two token tiles (M > 256).
+TC_SHAPES = [
+    (16, 2048, 96),      # 1 tile, split-K 4
+    (64, 3072, 200),     # ragged row tile, split-K 6
+    (37, 768, 130),      # ragged token tile (TN 48), odd-aligned Q6_K rows
+    (256, 1024, 384),    # TN 256
+    (300, 512, 256),     # 2 token tiles of 160
+    (16, 512, 19000),    # 149 row tiles: no split
+]
+
+
+@pytest.mark.parametrize("qt", QTYPES)
+@pytest.mark.parametrize("M,K,N", TC_SHAPES)
+def test_gemm_tc(rrr, ctx, oracle, G, qt, M, K, N):
+    """tcgen05 batched GEMM vs the f32 product of the oracle's dequantised weights and the
+    bf16 activations: within 1e-2 relative L2 per token row (north star)."""
+    (got,), ref = _gemm_tc_case(rrr, ctx, oracle, G, qt, M, K, N, seed=M * 7 + K + N + qt)
+    assert np.isfinite(got).all()
+    for m in range(M):
+        assert rel_l2(got[m], ref[m]) < 1e-2, (m, rel_l2(got[m], ref[m]))
+    assert rel_l2(got.ravel(), ref.ravel()) < 5e-3
+
+
+@pytest.mark.parametrize("qt", QTYPES)
+def test_gemm_tc_repeat_deterministic(rrr, ctx, oracle, G, qt):
+    """Split-K partial sums are added in split order by the last CTA of each tile, and the
+    tile counters are left at zero: repeated calls give identical bits."""
+    outs, ref = _gemm_tc_case(rrr, ctx, oracle, G, qt, 48, 4096, 256, seed=99 + qt, repeats=3)
+    assert rel_l2(outs[0].ravel(), ref.ravel()) < 5e-3
+    for o in outs[1:]:
+        assert np.array_equal(o, outs[0])
+
+
 def test_decode_step_small(rrr, ctx, oracle, G):
     """A small Phi-4-shaped model (numpy weights): eager and graph decode steps against
     the oracle's position-0 decode step."""
