@@ -41,14 +41,16 @@ GATE_UP_DRAM_BYTES = 28363520
 METRIC = "K-quant GEMV HBM GB/s (% of peak) per B200; Phi-4-mini-shape decode tok/s"
 
 
-def peaks():
+def peaks(tensor: bool = False):
+    """(peak, source): HBM copy GB/s, or with tensor=True the dense bf16 TFLOP/s burst
+    figure, from MEASURED_PEAKS.json; the pool's earlier measurement when it is absent."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
+        return (float(d["bf16_tflops"]) if tensor else float(d["hbm_gbs"])), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return (1590.0 if tensor else 6650.0), "fallback"
 
 
 class Clocks:
@@ -261,6 +263,36 @@ def run_ours(args, rank, world, local_rank):
         per[name] = {"qtype": {12: "Q4_K", 13: "Q5_K", 14: "Q6_K"}[qt], "K": K, "N": N, "bytes": nb,
                      "us_per_launch": round(us, 3), "GBps": round(nb / us / 1e3, 1),
                      "frac": round(nb / us / 1e3 / peaks()[0], 4)}
+    # ---------------- batched-token GEMM: tcgen05 tiles, one launch per layer's
+    # weights (32 distinct matrices per pass, larger than L2), M tokens of bf16 input
+    batched = {}
+    for name, M in [(n, m) for n in ("gate_up", "down") for m in (16, 64, 256)]:
+        _, qt, K, N = model.layers[0][name]
+        Xb = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        Yb = torch.empty(M, N, device="cuda")
+
+        def gemm(l):
+            ctx.check(L.rrr_gemm_kq_batched(ctx.h, qt, c_void_p(model.layers[l][name][0]),
+                                            c_void_p(Xb.data_ptr()), c_void_p(Yb.data_ptr()), M, K, N, sp))
+        for l in range(3):
+            gemm(l)
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        passes = 2
+        a.record(stream)
+        for _ in range(passes):
+            for l in range(cfg.n_layers):
+                gemm(l)
+        z.record(stream)
+        torch.cuda.synchronize()
+        us = 1e3 * a.elapsed_time(z) / (passes * cfg.n_layers)
+        flops = 2.0 * M * N * K
+        wb = cfg.weight_bytes(qt, K, N) + 2 * M * K + 4 * M * N
+        batched[f"{name}_M{M}"] = {
+            "qtype": {12: "Q4_K", 13: "Q5_K", 14: "Q6_K"}[qt], "M": M, "K": K, "N": N,
+            "us_per_launch": round(us, 3), "TFLOPs": round(flops / us / 1e6, 1),
+            "tensor_frac": round(flops / us / 1e6 / peaks(tensor=True)[0], 4),
+            "GBps": round(wb / us / 1e3, 1), "hbm_frac": round(wb / us / 1e3 / peaks()[0], 4)}
+        del Xb, Yb
     clk = clocks.stop()
     peak, peak_src = peaks()
     # ---------------- decode step through the CUDA graph
@@ -336,6 +368,9 @@ def run_ours(args, rank, world, local_rank):
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one gate_up "
                                            "launch (profiles/gemv_kq_phi4_layer_shapes.md)"},
             "decode": decode,
+            "batched_gemm": {"note": "configs[3]: rrr_gemm_kq_batched (tcgen05, bf16 x bf16 -> f32); "
+                                     "tensor_frac against the measured dense bf16 burst peak",
+                             "cases": batched},
             "e2e": {"value": round(bytes_step / e2e_ms / 1e6, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "rrr_h2d (all x) + rrr_batch_launch (prebuilt table of 128 GEMVs) + rrr_d2h (all y) + rrr_sync, pinned host buffers"},

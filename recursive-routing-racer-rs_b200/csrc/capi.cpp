@@ -153,8 +153,6 @@ int rrr_destroy(rrr_ctx* ctx) {
   bind_device(ctx);
   cudaDeviceSynchronize();
   if (ctx->d_err) cudaFree(ctx->d_err);
-  if (ctx->tc_ws) cudaFree(ctx->tc_ws);
-  if (ctx->tc_counters) cudaFree(ctx->tc_counters);
   delete ctx;
   return RRR_OK;
 }
@@ -367,28 +365,7 @@ int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w, const uint16_t* 
   const LaunchEnv env = make_env(ctx, stream);
   TcPlan plan;
   if (M >= 16 && plan_gemm_kq_tc(qtype, M, K, N, ctx->sm_count, &plan)) {
-    // grow the split-K workspace (kept by the context; the counters start at zero and
-    // every completed launch leaves them at zero)
-    if (plan.ws_floats > ctx->tc_ws_floats) {
-      if (ctx->tc_ws) cudaFree(ctx->tc_ws);
-      ctx->tc_ws = nullptr;
-      ctx->tc_ws_floats = 0;
-      RRR_LAUNCH_CHECK(ctx, cudaMalloc(&ctx->tc_ws, plan.ws_floats * sizeof(float)),
-                       "rrr_gemm_kq_batched: workspace");
-      ctx->tc_ws_floats = plan.ws_floats;
-    }
-    if (plan.n_counters > ctx->tc_n_counters) {
-      if (ctx->tc_counters) cudaFree(ctx->tc_counters);
-      ctx->tc_counters = nullptr;
-      ctx->tc_n_counters = 0;
-      RRR_LAUNCH_CHECK(ctx, cudaMalloc(&ctx->tc_counters, plan.n_counters * sizeof(unsigned)),
-                       "rrr_gemm_kq_batched: tile counters");
-      RRR_LAUNCH_CHECK(ctx, cudaMemset(ctx->tc_counters, 0, plan.n_counters * sizeof(unsigned)),
-                       "rrr_gemm_kq_batched: tile counters");
-      ctx->tc_n_counters = plan.n_counters;
-    }
-    const TcWorkspace wsp{ctx->tc_ws, ctx->tc_counters};
-    RRR_LAUNCH_CHECK(ctx, launch_gemm_kq_tc(env, qtype, w, x, y, M, K, N, plan, wsp),
+    RRR_LAUNCH_CHECK(ctx, launch_gemm_kq_tc(env, qtype, w, x, y, M, K, N, plan),
                      "rrr_gemm_kq_batched (tensor cores) launch");
     return RRR_OK;
   }

@@ -13,11 +13,6 @@ struct rrr_ctx {
   int* d_err = nullptr;  // 256 B: [0] device error flag written by kernels whose bounded
                          // waits give up; [64..79] argmax key + counter (kept zeroed)
   bool pdl = true;       // launch kernels with programmatic dependent launch
-  // split-K workspace of the batched tensor-core GEMM, grown on demand (rrr_gemm_kq_batched)
-  float* tc_ws = nullptr;
-  size_t tc_ws_floats = 0;
-  unsigned* tc_counters = nullptr;  // zero between launches
-  int tc_n_counters = 0;
   std::string last_error;
   void* argmax_scratch() { return reinterpret_cast<char*>(d_err) + 64; }
 };

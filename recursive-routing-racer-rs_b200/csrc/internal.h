@@ -50,22 +50,21 @@ cudaError_t launch_fill_f32(const LaunchEnv& env, float* dst, int64_t n, int nor
 cudaError_t launch_bf16_to_f32_rows(const LaunchEnv& env, const uint16_t* x, float* out,
                                     int64_t n);
 // Batched-token GEMM on the tensor cores (gemm_kq_tc.cu). plan_gemm_kq_tc picks the tile
-// shape, the ring depth and the split-K factor for this GPU and says how much workspace a
-// split-K launch needs; it returns false for shapes the kernel does not handle (M < 16).
+// shape, the ring depth and the split-K factor for this GPU; it returns false for shapes
+// the kernel does not handle (M < 16).
 struct TcPlan {
   int tn;          // tokens per tile (MMA N), multiple of 16, <= 256
-  int m_tiles, n_tiles, splits, stages, smem, tmem_cols;
-  size_t ws_floats;  // split-K partial tiles: splits * M * N floats (0 when splits == 1)
-  int n_counters;    // one zero-initialised counter per output tile (0 when splits == 1)
-};
-struct TcWorkspace {
-  float* ws;
-  unsigned* counters;  // left at zero by every completed launch
+  int m_tiles, n_tiles;
+  int splits;      // K splits = CTAs per cluster (1..8)
+  int stages, smem, tmem_cols;
+  int raw_stages;  // raw-block ring depth
+  int kbs;         // super-blocks per raw stage
+  int raw_tma;     // raw blocks staged by one 2-D TMA box per stage
 };
 bool plan_gemm_kq_tc(int qtype, int M, int K, int N, int sm_count, TcPlan* plan);
 cudaError_t launch_gemm_kq_tc(const LaunchEnv& env, int qtype, const void* w,
                               const uint16_t* x_bf16, float* y, int M, int K, int N,
-                              const TcPlan& plan, const TcWorkspace& ws);
+                              const TcPlan& plan);
 // Self-test of the integer tensor-core fragment layout used by the GEMV (writes 1 to
 // *d_ok when the device result matches the expected product).
 cudaError_t launch_mma_selftest(const LaunchEnv& env, int* d_ok);
