@@ -104,13 +104,19 @@ int rrr_gemv_kq(rrr_ctx* ctx, int qtype, const void* w_raw, const float* x, floa
  *                   V[(h / (n_q/n_kv))*hd + d] — attention output at position 0
  *                   (seq_len 1: softmax = 1, output = V of the head's KV group;
  *                   `attention` push [seq_len, n_kv, heads_per_kv, head_dim],
- *                   phi4.rs:1120). K must equal n_q*hd. */
+ *                   phi4.rs:1120). K = n_q*hd for the whole model. A tensor-parallel
+ *                   shard whose heads do not cover whole super-blocks passes the
+ *                   super-block window around them: input[k] is the head output at
+ *                   k - k_offset for k_offset <= k < k_offset + n_q*hd and 0 elsewhere
+ *                   (k_offset % 8 == 0, k_offset + n_q*hd <= K). The window has no
+ *                   reference counterpart (the reference runs on one GPU). */
 enum { RRR_X_PLAIN = 0, RRR_X_RMSNORM = 1, RRR_X_SILU_GATE = 2, RRR_X_GQA_V = 3 };
 typedef struct rrr_gemv_prologue {
   int mode;            /* RRR_X_* */
   const float* gamma;  /* RRR_X_RMSNORM */
   float eps;           /* RRR_X_RMSNORM */
   int n_q_heads, n_kv_heads, head_dim; /* RRR_X_GQA_V */
+  int k_offset;        /* RRR_X_GQA_V: first input element of the heads (0: no window) */
 } rrr_gemv_prologue;
 int rrr_gemv_kq_ex(rrr_ctx* ctx, int qtype, const void* w_raw, const float* x_in,
                    float* y, int K, int N, const float* residual,
@@ -275,6 +281,16 @@ int rrr_fill_f32_normal(rrr_ctx* ctx, float* dst, int64_t n, float mean, float s
                         uint64_t seed, void* stream);
 int rrr_fill_f32_uniform(rrr_ctx* ctx, float* dst, int64_t n, float lo, float hi,
                          uint64_t seed, void* stream);
+/* Sub-ranges of the same streams, for tensor-parallel shards that must equal slices of
+ * the full tensors: dst block (r, c), r < rows, c < blocks_per_row, row-major, is generator
+ * block block0 + r*src_row_blocks + c of rrr_fill_kquant_random's stream; dst[i] of
+ * rrr_fill_f32_range is element offset + i of rrr_fill_f32_normal (normal != 0: a = mean,
+ * b = std) or rrr_fill_f32_uniform (a = lo, b = hi). No reference counterpart. */
+int rrr_fill_kquant_random_2d(rrr_ctx* ctx, int qtype, void* dst, int64_t rows,
+                              int64_t blocks_per_row, int64_t src_row_blocks, int64_t block0,
+                              uint64_t seed, void* stream);
+int rrr_fill_f32_range(rrr_ctx* ctx, float* dst, int64_t n, int64_t offset, int normal, float a,
+                       float b, uint64_t seed, void* stream);
 
 #ifdef __cplusplus
 }

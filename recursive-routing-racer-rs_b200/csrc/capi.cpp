@@ -284,10 +284,13 @@ int rrr_gemv_kq_ex(rrr_ctx* ctx, int qtype, const void* w, const float* x, float
     x_elems = 2 * (size_t)K;
   } else if (mode == RRR_X_GQA_V) {
     const int nq = pro->n_q_heads, nkv = pro->n_kv_heads, hd = pro->head_dim;
-    if (nq <= 0 || nkv <= 0 || hd <= 0 || nq % nkv != 0 || hd % 8 != 0 || nq * hd != K)
+    const int ko = pro->k_offset;
+    if (nq <= 0 || nkv <= 0 || hd <= 0 || nq % nkv != 0 || hd % 8 != 0 || ko < 0 || ko % 8 != 0 ||
+        ko + nq * hd > K)
       return set_error(ctx, RRR_ERR_BAD_SHAPE,
                        "rrr_gemv_kq: GQA_V needs n_q %% n_kv == 0, head_dim %% 8 == 0, "
-                       "n_q*head_dim == K (n_q=%d n_kv=%d hd=%d K=%d)", nq, nkv, hd, K);
+                       "k_offset %% 8 == 0 and k_offset + n_q*head_dim <= K "
+                       "(n_q=%d n_kv=%d hd=%d k_offset=%d K=%d)", nq, nkv, hd, ko, K);
     x_elems = (size_t)(nq + 2 * nkv) * hd;
   } else if (mode != RRR_X_PLAIN) {
     return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq: unknown prologue mode %d", mode);
@@ -463,8 +466,36 @@ int rrr_fill_kquant_random(rrr_ctx* ctx, int qtype, void* dst, int64_t n_blocks,
   if (rc) return rc;
   if (!dst || n_blocks < 0) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_fill_kquant_random: bad args");
   RRR_BIND(ctx);
-  RRR_LAUNCH_CHECK(ctx, launch_fill_kquant(make_env(ctx, stream), qtype, dst, n_blocks, seed),
+  RRR_LAUNCH_CHECK(ctx, launch_fill_kquant(make_env(ctx, stream), qtype, dst, 1, n_blocks,
+                                           n_blocks, 0, seed),
                    "rrr_fill_kquant_random launch");
+  return RRR_OK;
+}
+
+int rrr_fill_kquant_random_2d(rrr_ctx* ctx, int qtype, void* dst, int64_t rows,
+                              int64_t blocks_per_row, int64_t src_row_blocks, int64_t block0,
+                              uint64_t seed, void* stream) {
+  RRR_CHECK_CTX(ctx);
+  int rc = check_qtype(ctx, qtype, "rrr_fill_kquant_random_2d");
+  if (rc) return rc;
+  if (!dst || rows < 0 || blocks_per_row < 0 || src_row_blocks < blocks_per_row || block0 < 0)
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_fill_kquant_random_2d: bad args");
+  RRR_BIND(ctx);
+  if (blocks_per_row == 0) return RRR_OK;
+  RRR_LAUNCH_CHECK(ctx, launch_fill_kquant(make_env(ctx, stream), qtype, dst, rows,
+                                           blocks_per_row, src_row_blocks, block0, seed),
+                   "rrr_fill_kquant_random_2d launch");
+  return RRR_OK;
+}
+
+int rrr_fill_f32_range(rrr_ctx* ctx, float* dst, int64_t n, int64_t offset, int normal, float a,
+                       float b, uint64_t seed, void* stream) {
+  RRR_CHECK_CTX(ctx);
+  if (!dst || n < 0 || offset < 0)
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_fill_f32_range: bad args");
+  RRR_BIND(ctx);
+  RRR_LAUNCH_CHECK(ctx, launch_fill_f32(make_env(ctx, stream), dst, n, offset, normal ? 1 : 0, a, b, seed),
+                   "rrr_fill_f32_range launch");
   return RRR_OK;
 }
 
@@ -473,7 +504,7 @@ int rrr_fill_f32_normal(rrr_ctx* ctx, float* dst, int64_t n, float mean, float s
   RRR_CHECK_CTX(ctx);
   if (!dst || n < 0) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_fill_f32_normal: bad args");
   RRR_BIND(ctx);
-  RRR_LAUNCH_CHECK(ctx, launch_fill_f32(make_env(ctx, stream), dst, n, 1, mean, std, seed),
+  RRR_LAUNCH_CHECK(ctx, launch_fill_f32(make_env(ctx, stream), dst, n, 0, 1, mean, std, seed),
                    "rrr_fill_f32_normal launch");
   return RRR_OK;
 }
@@ -483,7 +514,7 @@ int rrr_fill_f32_uniform(rrr_ctx* ctx, float* dst, int64_t n, float lo, float hi
   RRR_CHECK_CTX(ctx);
   if (!dst || n < 0) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_fill_f32_uniform: bad args");
   RRR_BIND(ctx);
-  RRR_LAUNCH_CHECK(ctx, launch_fill_f32(make_env(ctx, stream), dst, n, 0, lo, hi, seed),
+  RRR_LAUNCH_CHECK(ctx, launch_fill_f32(make_env(ctx, stream), dst, n, 0, 0, lo, hi, seed),
                    "rrr_fill_f32_uniform launch");
   return RRR_OK;
 }

@@ -52,7 +52,7 @@ struct GemvParams {
   const float* residual;
   const float* gamma;
   float eps;
-  int mode, out_mode, n_q, n_kv, hd;
+  int mode, out_mode, n_q, n_kv, hd, k_off;
   int K, N, nb;        // N: weight rows
   long long row_bytes, total_bytes;
   int kc, n_chunks, n_tiles, half_rows;
@@ -299,8 +299,14 @@ __device__ __forceinline__ void load_raw8(const GemvParams& p, int k0, float v[8
   }
   int kx = k0;
   if (p.mode == RRR_X_GQA_V) {
+    const int kh = k0 - p.k_off;  // outside the heads' window the input is 0
+    if (kh < 0 || kh >= p.n_q * p.hd) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+      return;
+    }
     const int hpk = p.n_q / p.n_kv;
-    const int head = k0 / p.hd, e = k0 % p.hd;
+    const int head = kh / p.hd, e = kh % p.hd;
     kx = p.n_q * p.hd + p.n_kv * p.hd + (head / hpk) * p.hd + e;
   }
   const float4 x0 = *reinterpret_cast<const float4*>(p.x + kx);
@@ -800,6 +806,7 @@ cudaError_t launch_gemv_kq(const LaunchEnv& env, int qtype, const void* w, const
   p.n_q = pro ? pro->n_q_heads : 0;
   p.n_kv = pro ? pro->n_kv_heads : 0;
   p.hd = pro ? pro->head_dim : 0;
+  p.k_off = pro && pro->mode == RRR_X_GQA_V ? pro->k_offset : 0;
   p.K = K;
   p.N = N;
   return launch_any(env, qtype, p);
@@ -819,6 +826,7 @@ cudaError_t launch_gemv_kq_swiglu(const LaunchEnv& env, int qtype, const void* w
   p.n_q = pro ? pro->n_q_heads : 0;
   p.n_kv = pro ? pro->n_kv_heads : 0;
   p.hd = pro ? pro->head_dim : 0;
+  p.k_off = pro && pro->mode == RRR_X_GQA_V ? pro->k_offset : 0;
   p.K = K;
   p.N = 2 * F;
   return launch_any(env, qtype, p);

@@ -43,10 +43,10 @@ cudaError_t launch_gemv_kq_swiglu(const LaunchEnv& env, int qtype, const void* w
                                   const rrr_gemv_prologue* pro);
 cudaError_t launch_matmul_f32(const LaunchEnv& env, const float* A, const float* B, float* C,
                               int M, int K, int N);
-cudaError_t launch_fill_kquant(const LaunchEnv& env, int qtype, void* dst, int64_t n_blocks,
-                               uint64_t seed);
-cudaError_t launch_fill_f32(const LaunchEnv& env, float* dst, int64_t n, int normal, float a,
-                            float b, uint64_t seed);
+cudaError_t launch_fill_kquant(const LaunchEnv& env, int qtype, void* dst, int64_t rows,
+                               int64_t bpr, int64_t src_row, int64_t block0, uint64_t seed);
+cudaError_t launch_fill_f32(const LaunchEnv& env, float* dst, int64_t n, int64_t offset,
+                            int normal, float a, float b, uint64_t seed);
 cudaError_t launch_bf16_to_f32_rows(const LaunchEnv& env, const uint16_t* x, float* out,
                                     int64_t n);
 // Batched-token GEMM on the tensor cores (gemm_kq_tc.cu). plan_gemm_kq_tc picks the tile

@@ -250,12 +250,16 @@ __device__ __forceinline__ uint32_t gen_scale_f16(uint64_t r) {
   return f32_to_f16_rne(__fadd_rn(lo, __fmul_rn(u, step)));
 }
 
+// dst block i = (r, c) of a rows x bpr block grid is generator block
+// block0 + r * src_row + c (a row range, or a column window of every row)
 template <int QT>
-__global__ void fill_kquant_kernel(uint8_t* __restrict__ dst, int64_t n_blocks, uint64_t seed) {
+__global__ void fill_kquant_kernel(uint8_t* __restrict__ dst, int64_t n_blocks, int64_t bpr,
+                                   int64_t src_row, int64_t block0, uint64_t seed) {
   constexpr int BB = KQ<QT>::kBlockBytes;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_blocks;
        i += (int64_t)gridDim.x * blockDim.x) {
-    uint64_t s = seed ^ ((uint64_t)i * 0xD1B54A32D192ED03ull);
+    const int64_t gi = block0 + (i / bpr) * src_row + i % bpr;
+    uint64_t s = seed ^ ((uint64_t)gi * 0xD1B54A32D192ED03ull);
     uint8_t buf[BB + 8];
     for (int o = 0; o < BB; o += 8) {
       const uint64_t r = splitmix64(s);
@@ -279,11 +283,11 @@ __global__ void fill_kquant_kernel(uint8_t* __restrict__ dst, int64_t n_blocks, 
   }
 }
 
-__global__ void fill_f32_kernel(float* __restrict__ dst, int64_t n, int normal, float a,
-                                float b, uint64_t seed) {
+__global__ void fill_f32_kernel(float* __restrict__ dst, int64_t n, int64_t offset, int normal,
+                                float a, float b, uint64_t seed) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    uint64_t s = seed ^ ((uint64_t)i * 0xD1B54A32D192ED03ull);
+    uint64_t s = seed ^ ((uint64_t)(offset + i) * 0xD1B54A32D192ED03ull);
     const uint64_t r = splitmix64(s);
     const float u1 = ((float)(uint32_t)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
     const float u2 = (float)(uint32_t)(r & 0xFFFFFFu) * (1.0f / 16777216.0f);
@@ -374,25 +378,32 @@ cudaError_t launch_matmul_f32(const LaunchEnv& env, const float* A, const float*
                         env.pdl, A, B, C, M, K, N);
 }
 
-cudaError_t launch_fill_kquant(const LaunchEnv& env, int qtype, void* dst, int64_t n_blocks,
-                               uint64_t seed) {
+cudaError_t launch_fill_kquant(const LaunchEnv& env, int qtype, void* dst, int64_t rows,
+                               int64_t bpr, int64_t src_row, int64_t block0, uint64_t seed) {
+  const int64_t n_blocks = rows * bpr;
   if (n_blocks <= 0) return cudaSuccess;
   const int grid = (int)std::min<int64_t>((n_blocks + 127) / 128, (int64_t)env.sm_count * 32);
   uint8_t* d = static_cast<uint8_t*>(dst);
   switch (qtype) {
-    case RRR_Q4_K: fill_kquant_kernel<RRR_Q4_K><<<grid, 128, 0, env.stream>>>(d, n_blocks, seed); break;
-    case RRR_Q5_K: fill_kquant_kernel<RRR_Q5_K><<<grid, 128, 0, env.stream>>>(d, n_blocks, seed); break;
-    case RRR_Q6_K: fill_kquant_kernel<RRR_Q6_K><<<grid, 128, 0, env.stream>>>(d, n_blocks, seed); break;
+    case RRR_Q4_K:
+      fill_kquant_kernel<RRR_Q4_K><<<grid, 128, 0, env.stream>>>(d, n_blocks, bpr, src_row, block0, seed);
+      break;
+    case RRR_Q5_K:
+      fill_kquant_kernel<RRR_Q5_K><<<grid, 128, 0, env.stream>>>(d, n_blocks, bpr, src_row, block0, seed);
+      break;
+    case RRR_Q6_K:
+      fill_kquant_kernel<RRR_Q6_K><<<grid, 128, 0, env.stream>>>(d, n_blocks, bpr, src_row, block0, seed);
+      break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
 }
 
-cudaError_t launch_fill_f32(const LaunchEnv& env, float* dst, int64_t n, int normal, float a,
-                            float b, uint64_t seed) {
+cudaError_t launch_fill_f32(const LaunchEnv& env, float* dst, int64_t n, int64_t offset,
+                            int normal, float a, float b, uint64_t seed) {
   if (n <= 0) return cudaSuccess;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)env.sm_count * 32);
-  fill_f32_kernel<<<grid, 256, 0, env.stream>>>(dst, n, normal, a, b, seed);
+  fill_f32_kernel<<<grid, 256, 0, env.stream>>>(dst, n, offset, normal, a, b, seed);
   return cudaGetLastError();
 }
 

@@ -34,7 +34,7 @@ class RRRError(RuntimeError):
 
 class GemvPrologue(ctypes.Structure):
     _fields_ = [("mode", c_int), ("gamma", c_void_p), ("eps", c_float), ("n_q_heads", c_int),
-                ("n_kv_heads", c_int), ("head_dim", c_int)]
+                ("n_kv_heads", c_int), ("head_dim", c_int), ("k_offset", c_int)]
 
 
 class GGUFTensor(ctypes.Structure):
@@ -110,6 +110,8 @@ PROTOS = {
     "rrr_fill_kquant_random": (c_int, [vp, c_int, vp, c_int64, c_uint64, vp]),
     "rrr_fill_f32_normal": (c_int, [vp, vp, c_int64, c_float, c_float, c_uint64, vp]),
     "rrr_fill_f32_uniform": (c_int, [vp, vp, c_int64, c_float, c_float, c_uint64, vp]),
+    "rrr_fill_kquant_random_2d": (c_int, [vp, c_int, vp, c_int64, c_int64, c_int64, c_int64, c_uint64, vp]),
+    "rrr_fill_f32_range": (c_int, [vp, vp, c_int64, c_int64, c_int, c_float, c_float, c_uint64, vp]),
 }
 
 _lib = None

@@ -1,0 +1,281 @@
+"""Tensor-parallel decode step of the weight path over G GPUs of one box (one process per
+GPU, torch.distributed over NCCL for the exchanges).
+
+The reference runs the whole model on one GPU (src/model/phi4.rs:1099-1196); this module
+splits the same per-layer weight GEMVs so that every rank streams 1/G of the bytes:
+
+    QKV       rows of the rank's query heads [h0, h1) and their KV heads [v0, v1): the
+              position-0 attention (output = V of the head's KV group) is then local
+    O-proj    the K columns of those heads (Megatron split). When the heads do not cover
+              whole 256-wide super-blocks (8 GPUs: 384 columns), the rank keeps the
+              super-block window around them and the GEMV input is zero outside the
+              heads (RRR_X_GQA_V with k_offset), so no block is split; the partial
+              outputs are summed with an all-reduce
+    gate_up   rows [f0, f1) of gate and the same rows of up: SiLU(gate)*up stays local
+    down      the matching K columns [f0, f1) of every row; all-reduce of the partials
+    logits    vocab rows [V*g/G, V*(g+1)/G), output RMSNorm fused; all-gather of the rows
+
+The residual is added by rank 0 only (in its O-proj / down epilogue), so the all-reduced
+sum carries it once. Everything else (RMSNorm, the argmax) is replicated. Per token: 2
+all-reduces per layer and one all-gather.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_void_p
+from dataclasses import dataclass
+
+from . import ffi
+from .phi4 import BLOCK_BYTES, DeviceArena, ModelConfig, tensor_seed
+
+
+@dataclass(frozen=True)
+class TPShard:
+    """Rows and K windows of rank g's shards (all ranges are [start, stop))."""
+    G: int
+    g: int
+    q_heads: tuple
+    kv_heads: tuple
+    qkv_rows: tuple          # row ranges of the full QKV matrix, in shard order (Q, K, V)
+    o_blocks: tuple          # super-block window of O-proj's K (n_heads*head_dim)
+    o_k_offset: int          # first column of the rank's heads inside the window
+    ffn: tuple               # rows [f0, f1) of gate and of up; K columns of down
+    vocab: tuple             # rows of the logits matrix
+
+    @property
+    def qkv_dim(self) -> int:
+        return sum(b - a for a, b in self.qkv_rows)
+
+    @property
+    def o_k(self) -> int:
+        return 256 * (self.o_blocks[1] - self.o_blocks[0])
+
+    @property
+    def ffn_dim(self) -> int:
+        return self.ffn[1] - self.ffn[0]
+
+    @property
+    def vocab_rows(self) -> int:
+        return self.vocab[1] - self.vocab[0]
+
+
+def plan(cfg: ModelConfig, G: int, g: int) -> TPShard:
+    """Shard ranges of rank g of G (the split of the tensor-parallel section above)."""
+    if G < 1 or not 0 <= g < G:
+        raise ValueError(f"bad rank {g} of {G}")
+    nq, nkv, hd, F, V = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab_size
+    if nq % G or nkv % G or nq % nkv:
+        raise ValueError(f"{nq} query / {nkv} KV heads do not split over {G} GPUs")
+    if F % (256 * G):
+        raise ValueError(f"ffn_dim {F} is not a multiple of 256*{G}")
+    if V % G:
+        raise ValueError(f"vocab {V} is not a multiple of {G}")
+    h0, h1 = nq * g // G, nq * (g + 1) // G
+    v0, v1 = nkv * g // G, nkv * (g + 1) // G
+    qkv_rows = ((h0 * hd, h1 * hd),
+                (nq * hd + v0 * hd, nq * hd + v1 * hd),
+                ((nq + nkv) * hd + v0 * hd, (nq + nkv) * hd + v1 * hd))
+    c0, c1 = h0 * hd, h1 * hd
+    b0, b1 = c0 // 256, (c1 + 255) // 256
+    f0, f1 = F * g // G, F * (g + 1) // G
+    return TPShard(G, g, (h0, h1), (v0, v1), qkv_rows, (b0, b1), c0 - 256 * b0, (f0, f1),
+                   (V * g // G, V * (g + 1) // G))
+
+
+class SyntheticPhi4TP:
+    """Rank g's shards of SyntheticPhi4(cfg, seed): every shard holds exactly the bytes of
+    the corresponding slice of the 1-GPU model (same generator streams), so a G-GPU step
+    can be checked against the 1-GPU step."""
+
+    def __init__(self, ctx: ffi.Context, cfg: ModelConfig, shard: TPShard, seed: int = 0,
+                 stream=None):
+        self.ctx, self.cfg, self.shard, self.seed = ctx, cfg, shard, seed
+        self.arena = DeviceArena(ctx)
+        L = ffi.lib()
+        s = stream
+        sh = shard
+        d, F = cfg.d_model, cfg.ffn_dim
+
+        def kq(qt, name, l, rows_ranges, nb_row, blocks=None):
+            """Rows `rows_ranges` of tensor `name` of layer l (nb_row blocks per row),
+            restricted to the super-block column window `blocks`."""
+            c0, c1 = blocks if blocks else (0, nb_row)
+            n_rows = sum(b - a for a, b in rows_ranges)
+            p = self.arena.alloc(n_rows * (c1 - c0) * BLOCK_BYTES[qt])
+            off, sd = 0, tensor_seed(seed, l, name)
+            for a, b in rows_ranges:
+                ctx.check(L.rrr_fill_kquant_random_2d(ctx.h, qt, c_void_p(p + off), b - a, c1 - c0,
+                                                      nb_row, a * nb_row + c0, sd, s))
+                off += (b - a) * (c1 - c0) * BLOCK_BYTES[qt]
+            return p
+
+        self.layers = []
+        for l in range(cfg.n_layers):
+            ent = {
+                "qkv": kq(cfg.qkv_type, "qkv", l, sh.qkv_rows, d // 256),
+                "o_proj": kq(cfg.o_type, "o_proj", l, ((0, d),), cfg.n_heads * cfg.head_dim // 256,
+                             sh.o_blocks),
+                "gate_up": kq(cfg.gate_up_type, "gate_up", l,
+                              (sh.ffn, (F + sh.ffn[0], F + sh.ffn[1])), d // 256),
+                "down": kq(cfg.down_type, "down", l, ((0, d),), F // 256,
+                           (sh.ffn[0] // 256, sh.ffn[1] // 256)),
+            }
+            for nn in ("attn_norm", "ffn_norm"):
+                p = self.arena.alloc(d * 4)
+                ctx.check(L.rrr_fill_f32_uniform(ctx.h, p, d, 0.5, 1.5, tensor_seed(seed, l, nn), s))
+                ent[nn] = p
+            self.layers.append(ent)
+        self.output_norm = self.arena.alloc(d * 4)
+        ctx.check(L.rrr_fill_f32_uniform(ctx.h, self.output_norm, d, 0.5, 1.5,
+                                         tensor_seed(seed, -1, "output_norm"), s))
+        v0, v1 = sh.vocab
+        self.w_out = self.arena.alloc((v1 - v0) * d * 4)
+        ctx.check(L.rrr_fill_f32_range(ctx.h, self.w_out, (v1 - v0) * d, v0 * d, 1, 0.0, 0.02,
+                                       tensor_seed(seed, -1, "output"), s))
+        ctx.check(L.rrr_sync(ctx.h, s))
+
+    def shard_bytes(self) -> int:
+        """Weight bytes one decode step streams on this rank."""
+        c, sh = self.cfg, self.shard
+        d = c.d_model
+        b = (sh.qkv_dim * (d // 256) * BLOCK_BYTES[c.qkv_type]
+             + d * (sh.o_blocks[1] - sh.o_blocks[0]) * BLOCK_BYTES[c.o_type]
+             + 2 * sh.ffn_dim * (d // 256) * BLOCK_BYTES[c.gate_up_type]
+             + d * (sh.ffn_dim // 256) * BLOCK_BYTES[c.down_type])
+        return b * c.n_layers + (2 * c.n_layers + 1) * d * 4 + sh.vocab_rows * d * 4
+
+    def close(self) -> None:
+        self.arena.free_all()
+
+
+class TPDecoder:
+    """One rank's position-0 decode step: the kernels of the 1-GPU step on the rank's
+    shards, with torch.distributed all-reduce / all-gather (NCCL) between them. The step
+    can be captured into a CUDA graph (kernels and collectives) and replayed."""
+
+    def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4TP, group=None):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.ctx, self.w, self.group = ctx, weights, group
+        cfg, sh = weights.cfg, weights.shard
+        dev = torch.device("cuda", ctx.device)
+        self.qkv = torch.empty(sh.qkv_dim, device=dev)
+        self.mid = torch.empty(sh.ffn_dim, device=dev)
+        self.logits_loc = torch.empty(sh.vocab_rows, device=dev)
+        self.graph = None
+        self._graph_key = None
+
+    def steps(self, hidden, logits, argmax, stream=None):
+        """The step as a generator: launches the kernels on `stream` (default: the current
+        torch stream) and yields at each exchange ("all_reduce", t) -- sum t over the
+        ranks in place -- and ("all_gather", out, part) -- out = concatenation of every
+        rank's part. hidden: f32[d] (in/out); logits: f32[vocab]; argmax: int32[1] or None."""
+        L, ctx, cfg, sh, w = ffi.lib(), self.ctx, self.w.cfg, self.w.shard, self.w
+        torch = self.torch
+        st = c_void_p(stream if stream is not None else torch.cuda.current_stream().cuda_stream)
+        d, hd = cfg.d_model, cfg.head_dim
+        hp = c_void_p(hidden.data_ptr())
+        res = hp if sh.g == 0 else None
+        nq_loc = sh.q_heads[1] - sh.q_heads[0]
+        nkv_loc = sh.kv_heads[1] - sh.kv_heads[0]
+        qkv_p, mid_p = c_void_p(self.qkv.data_ptr()), c_void_p(self.mid.data_ptr())
+        for l, e in enumerate(w.layers):
+            pn = ffi.GemvPrologue(1, e["attn_norm"], cfg.rms_eps, 0, 0, 0, 0)
+            ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.qkv_type, c_void_p(e["qkv"]), hp, qkv_p, d,
+                                       sh.qkv_dim, None, ctypes.byref(pn), st))
+            pv = ffi.GemvPrologue(3, None, 0.0, nq_loc, nkv_loc, hd, sh.o_k_offset)
+            ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.o_type, c_void_p(e["o_proj"]), qkv_p, hp, sh.o_k,
+                                       d, res, ctypes.byref(pv), st))
+            if sh.G > 1:
+                yield ("all_reduce", hidden)
+            pf = ffi.GemvPrologue(1, e["ffn_norm"], cfg.rms_eps, 0, 0, 0, 0)
+            ctx.check(L.rrr_gemv_kq_swiglu(ctx.h, cfg.gate_up_type, c_void_p(e["gate_up"]), hp, mid_p,
+                                           d, sh.ffn_dim, ctypes.byref(pf), st))
+            ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.down_type, c_void_p(e["down"]), mid_p, hp, sh.ffn_dim,
+                                       d, res, None, st))
+            if sh.G > 1:
+                yield ("all_reduce", hidden)
+        lp = c_void_p(self.logits_loc.data_ptr() if sh.G > 1 else logits.data_ptr())
+        ctx.check(L.rrr_logits_f32(ctx.h, c_void_p(w.w_out), hp, lp, sh.vocab_rows, d,
+                                   cfg.logits_chunk_rows, c_void_p(w.output_norm), cfg.rms_eps, st))
+        if sh.G > 1:
+            yield ("all_gather", logits, self.logits_loc)
+        if argmax is not None:
+            ctx.check(L.rrr_argmax_f32(ctx.h, c_void_p(logits.data_ptr()), cfg.vocab_size,
+                                       c_void_p(argmax.data_ptr()), st))
+
+    def _issue(self, hidden, logits, argmax):
+        """The step with its exchanges as torch.distributed collectives (NCCL)."""
+        dist = self.dist
+        for op in self.steps(hidden, logits, argmax):
+            if op[0] == "all_reduce":
+                dist.all_reduce(op[1], group=self.group)
+            else:
+                dist.all_gather_into_tensor(op[1], op[2], group=self.group)
+
+    def launches_per_step(self) -> int:
+        """Kernels of this library per step (collectives not counted)."""
+        cfg = self.w.cfg
+        return 4 * cfg.n_layers + -(-self.w.shard.vocab_rows // cfg.logits_chunk_rows) + 1
+
+    def forward(self, hidden, logits, argmax=None, use_graph: bool = False) -> None:
+        """One step on the current stream. hidden / logits / argmax are torch tensors on
+        this rank's device; with use_graph the step is captured on the first call for these
+        tensors and replayed afterwards."""
+        if not use_graph:
+            self._issue(hidden, logits, argmax)
+            return
+        torch = self.torch
+        key = (hidden.data_ptr(), logits.data_ptr(), None if argmax is None else argmax.data_ptr())
+        if self.graph is None or self._graph_key != key:
+            self.release_graph()
+            saved = hidden.clone()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                # warm-up outside the capture (first collectives set up the communicator)
+                self._issue(hidden, logits, argmax)
+            torch.cuda.current_stream().wait_stream(s)
+            hidden.copy_(saved)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="relaxed"):
+                self._issue(hidden, logits, argmax)
+            self.graph, self._graph_key = g, key
+        self.graph.replay()
+
+    def release_graph(self) -> None:
+        """Drop the captured graph (it holds NCCL calls: release it before the process
+        group is destroyed)."""
+        if self.graph is not None:
+            self.graph.reset()
+            self.graph = None
+            self._graph_key = None
+
+
+def emulate_step(decoders, hiddens, logits_list, argmaxes=None) -> None:
+    """Runs the ranks' steps of one process (all shards on the current device) in lockstep,
+    doing each exchange with torch ops: the sum of the ranks' tensors for an all-reduce,
+    the concatenation for an all-gather. For checking the split on one GPU."""
+    import torch
+    gens = [dec.steps(h, lg, None if argmaxes is None else argmaxes[i])
+            for i, (dec, h, lg) in enumerate(zip(decoders, hiddens, logits_list))]
+    while True:
+        ops = []
+        for gi in gens:
+            try:
+                ops.append(next(gi))
+            except StopIteration:
+                ops.append(None)
+        if all(o is None for o in ops):
+            return
+        if any(o is None for o in ops):
+            raise RuntimeError("ranks disagree on the exchange sequence")
+        if ops[0][0] == "all_reduce":
+            total = torch.stack([o[1] for o in ops]).sum(0)
+            for o in ops:
+                o[1].copy_(total)
+        else:
+            full = torch.cat([o[2] for o in ops])
+            for o in ops:
+                o[1].copy_(full)

@@ -1,0 +1,153 @@
+"""Tensor-parallel decode step on the GPU (recursive-routing-racer-rs_b200/tp.py).
+
+* the range fills give exactly the slices of the full synthetic tensors;
+* the G-rank split run in one process (exchanges done with torch ops, all shards on one
+  GPU) equals the 1-GPU rrr_phi4_forward step at G = 2 and 8 (8: O-proj windows that
+  cut super-blocks) within 1e-4 relative L2 (only the summation order differs);
+* with 2+ GPUs: the NCCL run (one process per GPU, CUDA graph with the collectives)
+  equals the 1-GPU step.
+"""
+import importlib
+import os
+import socket
+from ctypes import c_void_p
+
+import numpy as np
+import pytest
+
+tp = importlib.import_module("recursive-routing-racer-rs_b200.tp")
+phi4 = importlib.import_module("recursive-routing-racer-rs_b200.phi4")
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def test_range_fills_are_slices(rrr, ctx):
+    import torch
+    L = rrr.ffi.lib()
+    qt, rows, nb = 14, 40, 12
+    full = torch.empty(rows * nb * 210, dtype=torch.uint8, device="cuda")
+    ctx.check(L.rrr_fill_kquant_random(ctx.h, qt, c_void_p(full.data_ptr()), rows * nb, 77, None))
+    part = torch.empty(9 * 5 * 210, dtype=torch.uint8, device="cuda")
+    # rows 30..38, block columns 4..8
+    ctx.check(L.rrr_fill_kquant_random_2d(ctx.h, qt, c_void_p(part.data_ptr()), 9, 5, nb, 30 * nb + 4, 77, None))
+    ref = full.view(rows, nb, 210)[30:39, 4:9].reshape(-1)
+    assert torch.equal(part, ref)
+    f = torch.empty(10000, device="cuda")
+    g = torch.empty(3000, device="cuda")
+    ctx.check(L.rrr_fill_f32_normal(ctx.h, c_void_p(f.data_ptr()), 10000, 0.0, 0.02, 5, None))
+    ctx.check(L.rrr_fill_f32_range(ctx.h, c_void_p(g.data_ptr()), 3000, 6000, 1, 0.0, 0.02, 5, None))
+    assert torch.equal(g, f[6000:9000])
+    ctx.check(L.rrr_fill_f32_uniform(ctx.h, c_void_p(f.data_ptr()), 10000, 0.5, 1.5, 6, None))
+    ctx.check(L.rrr_fill_f32_range(ctx.h, c_void_p(g.data_ptr()), 3000, 100, 0, 0.5, 1.5, 6, None))
+    assert torch.equal(g, f[100:3100])
+
+
+def _single_gpu(ctx, cfg, seed, hidden0):
+    import torch
+    m = phi4.SyntheticPhi4(ctx, cfg, seed=seed)
+    dec = phi4.Phi4Decoder(ctx, m)
+    h = hidden0.clone()
+    lg = torch.empty(cfg.vocab_size, device="cuda")
+    am = torch.zeros(1, dtype=torch.int32, device="cuda")
+    dec.forward(h.data_ptr(), lg.data_ptr(), am.data_ptr(), False)
+    torch.cuda.synchronize()
+    out = (h.cpu().numpy(), lg.cpu().numpy(), int(am.item()))
+    dec.close()
+    m.close()
+    return out
+
+
+@pytest.mark.parametrize("G", [2, 8])
+def test_tp_split_emulated_matches_single_gpu(rrr, ctx, G):
+    """Phi-4-mini shapes (2 layers, full vocab), all G ranks' shards on this GPU."""
+    import torch
+    cfg = phi4.ModelConfig(n_layers=2)
+    seed = 11
+    hidden0 = torch.randn(cfg.d_model, device="cuda")
+    h1, lg1, am1 = _single_gpu(ctx, cfg, seed, hidden0)
+    ws = [tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, G, g), seed=seed) for g in range(G)]
+    decs = [tp.TPDecoder(ctx, w) for w in ws]
+    hs = [hidden0.clone() for _ in range(G)]
+    lgs = [torch.empty(cfg.vocab_size, device="cuda") for _ in range(G)]
+    ams = [torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(G)]
+    tp.emulate_step(decs, hs, lgs, ams)
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+    for g in range(G):
+        assert _rel(hs[g].cpu().numpy(), h1) < 1e-4
+        assert _rel(lgs[g].cpu().numpy(), lg1) < 1e-4
+        assert int(ams[g].item()) == am1
+    for w in ws:
+        w.close()
+
+
+# ------------------------------------------------------------------ NCCL, 2 GPUs
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_rank(rank, world, port, q):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    rrr = importlib.import_module("recursive-routing-racer-rs_b200")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    dec = None
+    try:
+        ctx = rrr.Context(rank)
+        cfg = phi4.ModelConfig(n_layers=2)
+        seed = 12
+        gen = torch.Generator(device="cuda").manual_seed(5)
+        hidden0 = torch.randn(cfg.d_model, device="cuda", generator=gen)
+        w = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, world, rank), seed=seed)
+        dec = tp.TPDecoder(ctx, w)
+        lg = torch.empty(cfg.vocab_size, device="cuda")
+        am = torch.zeros(1, dtype=torch.int32, device="cuda")
+        results = []
+        for use_graph in (False, True, True):
+            h = hidden0.clone()
+            dec.forward(h, lg, am, use_graph=use_graph)
+            torch.cuda.synchronize()
+            results.append((h.cpu().numpy(), lg.cpu().numpy(), int(am.item())))
+        dec.release_graph()
+        if rank == 0:
+            h1, lg1, am1 = _single_gpu(ctx, cfg, seed, hidden0)
+            q.put([(_rel(h, h1), _rel(lgr, lg1), a == am1) for h, lgr, a in results]
+                  + [ctx.device_error()])
+        w.close()
+    finally:
+        if dec is not None:
+            dec.release_graph()
+        dist.destroy_process_group()
+
+
+def test_tp_nccl_two_gpus():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = _free_port()
+    procs = [mpc.Process(target=_nccl_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+        assert p.exitcode == 0
+    res = q.get(timeout=10)
+    assert res[-1] == 0
+    for rh, rl, same in res[:-1]:
+        assert rh < 1e-4 and rl < 1e-4 and same
