@@ -176,7 +176,9 @@ def run_ours(args, rank, world, local_rank):
     dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=120))
     ctx = ffi.Context(local_rank)
     stream = torch.cuda.current_stream()
     sp = c_void_p(stream.cuda_stream)
@@ -317,6 +319,45 @@ def run_ours(args, rank, world, local_rank):
               "frac_of_peak": round(dec_bytes / dms / 1e6 / peak, 4),
               "launches_per_token": dec.launches_per_step() + 1, "graph": True}
     dec.close()
+    # ---------------- tensor-parallel decode step (configs[4], batch 1) over all ranks
+    tp_decode = None
+    if world > 1:
+        tpm = importlib.import_module("recursive-routing-racer-rs_b200.tp")
+        shard = tpm.plan(cfg, world, rank)
+        tw = tpm.SyntheticPhi4TP(ctx, cfg, shard, seed=7, stream=sp)
+        th = torch.randn(cfg.d_model, device="cuda")
+        tl = torch.empty(cfg.vocab_size, device="cuda")
+        ta = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+        def time_tp(comm):
+            tdec = tpm.TPDecoder(ctx, tw, comm=comm)
+            for _ in range(max(3, args.warmup)):
+                tdec.forward(th, tl, ta, use_graph=True)
+            barrier()
+            t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0e.record(stream)
+            for _ in range(dsteps):
+                tdec.forward(th, tl, ta, use_graph=True)
+            t1e.record(stream)
+            barrier()
+            t = max_over_ranks(t0e.elapsed_time(t1e) / dsteps)
+            n_l = tdec.launches_per_step()
+            tdec.close()
+            return t, n_l
+
+        tms, tl_p2p = time_tp("p2p")
+        tms_nccl, _ = time_tp("nccl")
+        tp_decode = {"tok_s": round(1e3 / tms, 2), "ms_per_token": round(tms, 4), "n_gpus": world,
+                     "exchange": "rrr_comm peer-memory kernels over NVLink (all-reduce x2 per layer "
+                                 "+ logits all-gather)",
+                     "tok_s_nccl": round(1e3 / tms_nccl, 2),
+                     "bytes_per_rank": tw.shard_bytes(),
+                     "GBps_per_rank": round(tw.shard_bytes() / tms / 1e6, 1),
+                     "exchanges_per_token": 2 * cfg.n_layers + 1,
+                     "launches_per_token": tl_p2p, "graph": True,
+                     "split": "QKV by KV-head group, O-proj by head columns (super-block window), "
+                              "gate_up rows / down columns, logits by vocab"}
+        tw.close()
     # ---------------- end to end through the C ABI with host buffers (pinned): copy every
     # x of the step in, replay the prebuilt table, copy every y out, synchronise
     hX = torch.randn(xo).pin_memory()
@@ -368,6 +409,7 @@ def run_ours(args, rank, world, local_rank):
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one gate_up "
                                            "launch (profiles/gemv_kq_phi4_layer_shapes.md)"},
             "decode": decode,
+            "tp_decode": tp_decode,
             "batched_gemm": {"note": "configs[3]: rrr_gemm_kq_batched (tcgen05, bf16 x bf16 -> f32); "
                                      "tensor_frac against the measured dense bf16 burst peak",
                              "cases": batched},

@@ -271,6 +271,29 @@ int rrr_phi4_forward(rrr_phi4* m, float* hidden, float* logits, int* argmax_out,
 int rrr_phi4_launches_per_step(rrr_phi4* m, int* n);
 int rrr_phi4_destroy(rrr_phi4* m);
 
+/* ---- exchanges between the GPUs of one box (tensor-parallel decode step) ------------
+ * No reference counterpart (the reference runs on one GPU). One process per GPU; every
+ * rank creates its exchange buffer, passes its 64-byte CUDA IPC handle to the other
+ * ranks (any host channel: torch.distributed, a file, MPI) and connects with all
+ * world handles in rank order. The exchanges then run as one kernel over NVLink peer
+ * memory (peer stores plus release/acquire flags, no NCCL), capturable in CUDA graphs:
+ *   all-reduce: x[i] = sum over ranks in rank order (identical bits on every rank),
+ *   all-gather: out[r*n + i] = rank r's part[i] (part may be out + rank*n).
+ * Every rank must issue the same sequence of calls with the same n <= max_elems. A wait
+ * that exceeds about a second records an error in the context's device flag. */
+typedef struct rrr_comm rrr_comm;
+int rrr_comm_create(rrr_ctx* ctx, int rank, int world, int64_t max_elems, rrr_comm** out,
+                    void* ipc_handle_out /* 64 bytes */);
+int rrr_comm_connect(rrr_comm* comm, const void* ipc_handles /* world x 64 bytes */);
+int rrr_comm_allreduce_f32(rrr_comm* comm, float* x, int64_t n, void* stream);
+int rrr_comm_allgather_f32(rrr_comm* comm, float* out, const float* part, int64_t n_per_rank,
+                           void* stream);
+/* Unmaps the other ranks' buffers (after this rank's last exchange has completed). Call
+ * it on every rank and synchronise the ranks before any rank calls rrr_comm_destroy,
+ * which frees this rank's buffer (and disconnects first if needed). */
+int rrr_comm_disconnect(rrr_comm* comm);
+int rrr_comm_destroy(rrr_comm* comm);
+
 /* ---- seeded synthetic data on the device (bench / tests) --------------------------
  * Blocks follow the distributions of the benchmark configs: d, dmin f16 ~ U[1e-4,1e-2];
  * Q6_K scales int8 ~ U[-32,31]; all other bytes uniform. Block i depends only on

@@ -49,7 +49,6 @@ constexpr int kThreads = 352;         // 11 warps
 constexpr int kDqThreads = 256;       // warps 3..10
 constexpr int kMaxRawStages = 4;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB per A slot
-constexpr int kMaxStages = 4;
 constexpr int kMaxSplits = 8;         // portable cluster size
 constexpr int kMaxKbs = 4;            // super-blocks per raw stage
 constexpr int kSmemBudget = 232448;   // 227 KB opt-in maximum on sm_100

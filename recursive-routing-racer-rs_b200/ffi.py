@@ -110,6 +110,12 @@ PROTOS = {
     "rrr_fill_kquant_random": (c_int, [vp, c_int, vp, c_int64, c_uint64, vp]),
     "rrr_fill_f32_normal": (c_int, [vp, vp, c_int64, c_float, c_float, c_uint64, vp]),
     "rrr_fill_f32_uniform": (c_int, [vp, vp, c_int64, c_float, c_float, c_uint64, vp]),
+    "rrr_comm_create": (c_int, [vp, c_int, c_int, c_int64, POINTER(vp), vp]),
+    "rrr_comm_connect": (c_int, [vp, vp]),
+    "rrr_comm_allreduce_f32": (c_int, [vp, vp, c_int64, vp]),
+    "rrr_comm_allgather_f32": (c_int, [vp, vp, vp, c_int64, vp]),
+    "rrr_comm_disconnect": (c_int, [vp]),
+    "rrr_comm_destroy": (c_int, [vp]),
     "rrr_fill_kquant_random_2d": (c_int, [vp, c_int, vp, c_int64, c_int64, c_int64, c_int64, c_uint64, vp]),
     "rrr_fill_f32_range": (c_int, [vp, vp, c_int64, c_int64, c_int, c_float, c_float, c_uint64, vp]),
 }

@@ -148,16 +148,59 @@ class SyntheticPhi4TP:
         self.arena.free_all()
 
 
+class P2PComm:
+    """The C ABI's NVLink peer-memory exchanges (rrr_comm_*) for one rank; the 64-byte IPC
+    handles are swapped with torch.distributed.all_gather_object."""
+
+    def __init__(self, ctx: ffi.Context, rank: int, world: int, max_elems: int, group=None):
+        import torch.distributed as dist
+        L = ffi.lib()
+        self.ctx, self.group = ctx, group
+        h = c_void_p()
+        buf = ctypes.create_string_buffer(64)
+        ctx.check(L.rrr_comm_create(ctx.h, rank, world, max_elems, ctypes.byref(h), buf))
+        self.h = h
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(buf.raw), group=group)
+        allh = ctypes.create_string_buffer(b"".join(handles), 64 * world)
+        ctx.check(L.rrr_comm_connect(self.h, allh))
+        dist.barrier(group=group)
+
+    def all_reduce(self, t, stream) -> None:
+        self.ctx.check(ffi.lib().rrr_comm_allreduce_f32(self.h, c_void_p(t.data_ptr()), t.numel(), stream))
+
+    def all_gather(self, out, part, stream) -> None:
+        self.ctx.check(ffi.lib().rrr_comm_allgather_f32(self.h, c_void_p(out.data_ptr()),
+                                                        c_void_p(part.data_ptr()), part.numel(), stream))
+
+    def close(self) -> None:
+        """Collective: every rank unmaps the others' buffers, then frees its own."""
+        import torch.distributed as dist
+        if self.h:
+            ffi.lib().rrr_comm_disconnect(self.h)
+            dist.barrier(group=self.group)
+            ffi.lib().rrr_comm_destroy(self.h)
+            self.h = None
+
+
 class TPDecoder:
     """One rank's position-0 decode step: the kernels of the 1-GPU step on the rank's
     shards, with torch.distributed all-reduce / all-gather (NCCL) between them. The step
     can be captured into a CUDA graph (kernels and collectives) and replayed."""
 
-    def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4TP, group=None):
+    def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4TP, group=None, comm: str = "nccl"):
+        """comm: "nccl" (torch.distributed collectives) or "p2p" (rrr_comm_* kernels over
+        NVLink peer memory)."""
         import torch
         import torch.distributed as dist
         self.torch, self.dist = torch, dist
         self.ctx, self.w, self.group = ctx, weights, group
+        self.p2p = None
+        if comm == "p2p" and weights.shard.G > 1:
+            self.p2p = P2PComm(ctx, weights.shard.g, weights.shard.G,
+                               max(weights.cfg.d_model, weights.shard.vocab_rows), group)
+        elif comm not in ("nccl", "p2p"):
+            raise ValueError(f"unknown comm {comm!r}")
         cfg, sh = weights.cfg, weights.shard
         dev = torch.device("cuda", ctx.device)
         self.qkv = torch.empty(sh.qkv_dim, device=dev)
@@ -206,18 +249,35 @@ class TPDecoder:
                                        c_void_p(argmax.data_ptr()), st))
 
     def _issue(self, hidden, logits, argmax):
-        """The step with its exchanges as torch.distributed collectives (NCCL)."""
+        """The step with its exchanges as torch.distributed collectives (NCCL) or as the
+        peer-memory kernels."""
         dist = self.dist
+        st = c_void_p(self.torch.cuda.current_stream().cuda_stream)
         for op in self.steps(hidden, logits, argmax):
-            if op[0] == "all_reduce":
+            if self.p2p is not None:
+                if op[0] == "all_reduce":
+                    self.p2p.all_reduce(op[1], st)
+                else:
+                    self.p2p.all_gather(op[1], op[2], st)
+            elif op[0] == "all_reduce":
                 dist.all_reduce(op[1], group=self.group)
             else:
                 dist.all_gather_into_tensor(op[1], op[2], group=self.group)
 
+    def close(self) -> None:
+        self.release_graph()
+        if self.p2p is not None:
+            self.p2p.close()
+            self.p2p = None
+
     def launches_per_step(self) -> int:
-        """Kernels of this library per step (collectives not counted)."""
+        """Kernels of this library per step (NCCL collectives not counted; the peer-memory
+        exchanges are)."""
         cfg = self.w.cfg
-        return 4 * cfg.n_layers + -(-self.w.shard.vocab_rows // cfg.logits_chunk_rows) + 1
+        n = 4 * cfg.n_layers + -(-self.w.shard.vocab_rows // cfg.logits_chunk_rows) + 1
+        if self.p2p is not None:
+            n += 2 * cfg.n_layers + 1
+        return n
 
     def forward(self, hidden, logits, argmax=None, use_graph: bool = False) -> None:
         """One step on the current stream. hidden / logits / argmax are torch tensors on

@@ -4,8 +4,8 @@
 * the G-rank split run in one process (exchanges done with torch ops, all shards on one
   GPU) equals the 1-GPU rrr_phi4_forward step at G = 2 and 8 (8: O-proj windows that
   cut super-blocks) within 1e-4 relative L2 (only the summation order differs);
-* with 2+ GPUs: the NCCL run (one process per GPU, CUDA graph with the collectives)
-  equals the 1-GPU step.
+* with 2+ GPUs: the run with one process per GPU, eager and as a CUDA graph, with the
+  exchanges as NCCL collectives or as the peer-memory kernels, equals the 1-GPU step.
 """
 import importlib
 import os
@@ -92,7 +92,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_rank(rank, world, port, q):
+def _nccl_rank(rank, world, port, q, comm):
     import datetime
     import torch
     import torch.distributed as dist
@@ -109,7 +109,7 @@ def _nccl_rank(rank, world, port, q):
         gen = torch.Generator(device="cuda").manual_seed(5)
         hidden0 = torch.randn(cfg.d_model, device="cuda", generator=gen)
         w = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, world, rank), seed=seed)
-        dec = tp.TPDecoder(ctx, w)
+        dec = tp.TPDecoder(ctx, w, comm=comm)
         lg = torch.empty(cfg.vocab_size, device="cuda")
         am = torch.zeros(1, dtype=torch.int32, device="cuda")
         results = []
@@ -118,7 +118,7 @@ def _nccl_rank(rank, world, port, q):
             dec.forward(h, lg, am, use_graph=use_graph)
             torch.cuda.synchronize()
             results.append((h.cpu().numpy(), lg.cpu().numpy(), int(am.item())))
-        dec.release_graph()
+        dec.close()
         if rank == 0:
             h1, lg1, am1 = _single_gpu(ctx, cfg, seed, hidden0)
             q.put([(_rel(h, h1), _rel(lgr, lg1), a == am1) for h, lgr, a in results]
@@ -126,11 +126,13 @@ def _nccl_rank(rank, world, port, q):
         w.close()
     finally:
         if dec is not None:
-            dec.release_graph()
+            dec.close()
         dist.destroy_process_group()
 
 
-def test_tp_nccl_two_gpus():
+@pytest.mark.parametrize("comm", ["nccl", "p2p"])
+def test_tp_nccl_two_gpus(comm):
+    """comm = nccl: torch.distributed collectives; p2p: the rrr_comm_* peer-memory kernels."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -138,7 +140,7 @@ def test_tp_nccl_two_gpus():
     mpc = mp.get_context("spawn")
     q = mpc.Queue()
     port = _free_port()
-    procs = [mpc.Process(target=_nccl_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [mpc.Process(target=_nccl_rank, args=(r, 2, port, q, comm)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
