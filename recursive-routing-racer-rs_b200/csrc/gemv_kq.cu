@@ -37,10 +37,13 @@ namespace rrr {
 namespace {
 
 constexpr int kTileRows = 16;
-constexpr int kNW = 8;                  // consumer warps per CTA
-constexpr int kThreads = (kNW + 1) * 32;
+constexpr int kNW = 8;                  // consumer warps per group
+constexpr int kGroups = 2;              // producer + consumer groups per CTA; they share the
+                                        // x digits, which are prepared once per CTA
+constexpr int kThreads = kGroups * (kNW + 1) * 32;
+constexpr int kMinCtas = 2 / kGroups;   // CTAs per SM
 constexpr int kXBf16 = 100;             // internal prologue mode: x is bf16 (batched path)
-constexpr int kSmemBudget = 113 * 1024; // two CTAs per SM
+constexpr int kSmemBudget = 113 * 1024 * kGroups;  // 226 KB per SM
 constexpr int kMaxStages = 6;
 constexpr int kSlots = 8;               // row-tile reduction slots (> stages + 1)
 
@@ -323,117 +326,131 @@ __device__ __forceinline__ void load_raw8(const GemvParams& p, int k0, float v[8
   }
 }
 
-// The GEMV input from the raw values: rms_norm(x)*gamma is (gamma*x)*inv (phi4.rs:598);
-// silu(g)*u is g/(1+e^-g)*u (phi4.rs:1368-1373).
-__device__ __forceinline__ void finish8(const GemvParams& p, float v[8], const float a[8],
-                                        float inv_rms) {
+// The GEMV input from the raw values, before the RMS factor: gamma*x for RMSNORM (the
+// factor 1/rms of rms_norm(x)*gamma = (gamma*x)*inv, phi4.rs:598, is applied to the finished
+// row sums, since every output is linear in the input); silu(g)*u = g/(1+e^-g)*u for
+// SILU_GATE (phi4.rs:1368-1373). Returns sum(x^2) of the raw values for RMSNORM.
+__device__ __forceinline__ float finish8(const GemvParams& p, float v[8], const float a[8]) {
+  float ss = 0.f;
   if (p.mode == RRR_X_RMSNORM) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(a[i], v[i]), inv_rms);
+    for (int i = 0; i < 8; ++i) {
+      ss = fmaf(v[i], v[i], ss);
+      v[i] = __fmul_rn(a[i], v[i]);
+    }
   } else if (p.mode == RRR_X_SILU_GATE) {
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       v[i] = __fmul_rn(__fdiv_rn(v[i], __fadd_rn(1.0f, expf(-v[i]))), a[i]);
   }
+  return ss;
 }
 
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
+// Digits, block scales and partial sums of the GEMV input, in one pass over x: warp w
+// handles blocks w, w+8, ..., loading up to kPrepGroup blocks at once (one L2 round trip per
+// group while the weight stream loads the memory system). The digits quantise gamma*x per
+// 256-block (the RMS factor cancels in T = round(v*127*2^14/max|v|)); misc[warp] receives
+// the warp's sum of x^2 (RMSNORM) for the factor applied to the row sums.
+constexpr int kPrepGroup = 2;
+
 template <bool FRAG>
 __device__ void prepare_x(const GemvParams& p, int8_t* dig, float* xscale, float* xsum,
                           float* misc, int warp, int lane) {
-  constexpr int NT = kNW * 32;
-  const int t = warp * 32 + lane;
-  float inv_rms = 1.f;
-  if (p.mode == RRR_X_RMSNORM) {
-    const float4* x4 = reinterpret_cast<const float4*>(p.x);
-    const int K4 = p.K / 4;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    int k = t;
-    for (; k + 3 * NT < K4; k += 4 * NT) {
-      const float4 a = x4[k], b = x4[k + NT], c = x4[k + 2 * NT], d = x4[k + 3 * NT];
-      s0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
-      s1 += b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
-      s2 += c.x * c.x + c.y * c.y + c.z * c.z + c.w * c.w;
-      s3 += d.x * d.x + d.y * d.y + d.z * d.z + d.w * d.w;
-    }
-    for (; k < K4; k += NT) {
-      const float4 a = x4[k];
-      s0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
-    }
-    const float ss = warp_sum((s0 + s1) + (s2 + s3));
-    if (lane == 0) misc[warp] = ss;
-    named_barrier(1, NT);
-    float tot = 0.f;
+  constexpr int NPW = kGroups * kNW;  // every consumer warp of the CTA takes part
+  float ssq = 0.f;
+  for (int bg = warp; bg < p.nb; bg += kPrepGroup * NPW) {
+    // the group's blocks bg, bg+8, ...: loads first, then each step for all blocks at once
+    // (independent shuffle chains interleave)
+    float vg[kPrepGroup][8], ag[kPrepGroup][8];
+    const int ng = min(kPrepGroup, (p.nb - bg + NPW - 1) / NPW);
 #pragma unroll
-    for (int w = 0; w < kNW; ++w) tot += misc[w];
-    inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)p.K), p.eps)));
-  }
-  // warp w digitises blocks w, w+8, ...; the next block's loads are issued before the
-  // current block is processed
-  float v[8], a[8], vn[8], an[8];
-  int b = warp;
-  if (b < p.nb) load_raw8(p, b * 256 + lane * 8, v, a);
-  for (; b < p.nb; b += kNW) {
-    const int bn = b + kNW;
-    if (bn < p.nb) load_raw8(p, bn * 256 + lane * 8, vn, an);
-    finish8(p, v, a, inv_rms);
-    float m = 0.f, s8 = 0.f;
+    for (int g = 0; g < kPrepGroup; ++g)
+      if (g < ng) load_raw8(p, (bg + g * NPW) * 256 + lane * 8, vg[g], ag[g]);
+    float m[kPrepGroup], s8[kPrepGroup];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      m = fmaxf(m, fabsf(v[i]));
-      s8 += v[i];
+    for (int g = 0; g < kPrepGroup; ++g) {
+      m[g] = 0.f;
+      s8[g] = 0.f;
+      if (g < ng) {
+        ssq += finish8(p, vg[g], ag[g]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          m[g] = fmaxf(m[g], fabsf(vg[g][i]));
+          s8[g] += vg[g][i];
+        }
+      }
     }
-    m = warp_max(m);
-    // T = round(x * 127 * 2^14 / max) as an integer (|T| <= 127 * 2^14 < 2^22, through the
-    // 1.5 * 2^23 magic constant), split into balanced base-128 digits:
-    // T = q0 * 2^14 + q1 * 2^7 + q2 with q0 in [-127, 127], q1, q2 in [-64, 64].
-    const float inv = m > 0.f ? __fdividef(127.f * 16384.f, m) : 0.f;
-    int q0[8], q1[8], q2[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int T = __float_as_int(__fmaf_rn(v[i], inv, 12582912.0f)) - 0x4B400000;
-      q0[i] = (T + 8192) >> 14;
-      const int r = T - q0[i] * 16384;
-      q1[i] = (r + 64) >> 7;
-      q2[i] = r - q1[i] * 128;
-    }
-    if (FRAG) {
-      // per-lane B fragments: pair P = 4b + lane/8, group (lane>>2)&1, tig = lane&3;
-      // column n of the pair at n*64 + tig*16 holds (b0, b1) of MMA 1 and MMA 2
-      const int grp = (lane >> 2) & 1;
-      uint8_t* fb = reinterpret_cast<uint8_t*>(dig) + (b * 4 + (lane >> 3)) * 512 + (lane & 3) * 16;
-      const uint32_t m1[3] = {pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q1[0], q1[1], q1[2], q1[3]),
-                              pack4(q2[0], q2[1], q2[2], q2[3])};
-      const uint32_t m2[3] = {pack4(q0[4], q0[5], q0[6], q0[7]), pack4(q1[4], q1[5], q1[6], q1[7]),
-                              pack4(q2[4], q2[5], q2[6], q2[7])};
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-      for (int dgt = 0; dgt < 3; ++dgt)
-        *reinterpret_cast<uint4*>(fb + (grp * 4 + dgt) * 64) =
-            grp ? make_uint4(0u, m1[dgt], 0u, m2[dgt]) : make_uint4(m1[dgt], 0u, m2[dgt], 0u);
-      *reinterpret_cast<uint4*>(fb + (grp * 4 + 3) * 64) = make_uint4(0u, 0u, 0u, 0u);
-    } else {
-      const int k0 = b * 256 + lane * 8;
-      *reinterpret_cast<uint2*>(dig + k0) =
-          make_uint2(pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q0[4], q0[5], q0[6], q0[7]));
-      *reinterpret_cast<uint2*>(dig + p.dig_stride + k0) =
-          make_uint2(pack4(q1[0], q1[1], q1[2], q1[3]), pack4(q1[4], q1[5], q1[6], q1[7]));
-      *reinterpret_cast<uint2*>(dig + 2 * p.dig_stride + k0) =
-          make_uint2(pack4(q2[0], q2[1], q2[2], q2[3]), pack4(q2[4], q2[5], q2[6], q2[7]));
-    }
-    const float s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
-    if ((lane & 1) == 0) xsum[b * 16 + (lane >> 1)] = s16;
-    const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
-    if ((lane & 3) == 0) xsum[p.K / 16 + b * 8 + (lane >> 2)] = s32;
-    if (lane == 0) xscale[b] = m / 127.f;
+      for (int g = 0; g < kPrepGroup; ++g) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], o));
+    float s16[kPrepGroup], s32[kPrepGroup];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      v[i] = vn[i];
-      a[i] = an[i];
+    for (int g = 0; g < kPrepGroup; ++g) s16[g] = s8[g] + __shfl_xor_sync(0xffffffffu, s8[g], 1);
+#pragma unroll
+    for (int g = 0; g < kPrepGroup; ++g) s32[g] = s16[g] + __shfl_xor_sync(0xffffffffu, s16[g], 2);
+#pragma unroll
+    for (int g = 0; g < kPrepGroup; ++g) {
+      if (g >= ng) break;
+      const int b = bg + g * NPW;
+      const float* v = vg[g];
+      // T = round(x * 127 * 2^14 / max) as an integer (|T| <= 127 * 2^14 < 2^22, through
+      // the 1.5 * 2^23 magic constant), split into balanced base-128 digits:
+      // T = q0 * 2^14 + q1 * 2^7 + q2 with q0 in [-127, 127], q1, q2 in [-64, 64].
+      const float inv = m[g] > 0.f ? __fdividef(127.f * 16384.f, m[g]) : 0.f;
+      int q0[8], q1[8], q2[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int T = __float_as_int(__fmaf_rn(v[i], inv, 12582912.0f)) - 0x4B400000;
+        q0[i] = (T + 8192) >> 14;
+        const int r = T - q0[i] * 16384;
+        q1[i] = (r + 64) >> 7;
+        q2[i] = r - q1[i] * 128;
+      }
+      if (FRAG) {
+        // per-lane B fragments: pair P = 4b + lane/8, group (lane>>2)&1, tig = lane&3;
+        // column n of the pair at n*64 + tig*16 holds (b0, b1) of MMA 1 and MMA 2
+        const int grp = (lane >> 2) & 1;
+        uint8_t* fb = reinterpret_cast<uint8_t*>(dig) + (b * 4 + (lane >> 3)) * 512 + (lane & 3) * 16;
+        const uint32_t m1[3] = {pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q1[0], q1[1], q1[2], q1[3]),
+                                pack4(q2[0], q2[1], q2[2], q2[3])};
+        const uint32_t m2[3] = {pack4(q0[4], q0[5], q0[6], q0[7]), pack4(q1[4], q1[5], q1[6], q1[7]),
+                                pack4(q2[4], q2[5], q2[6], q2[7])};
+#pragma unroll
+        for (int dgt = 0; dgt < 3; ++dgt)
+          *reinterpret_cast<uint4*>(fb + (grp * 4 + dgt) * 64) =
+              grp ? make_uint4(0u, m1[dgt], 0u, m2[dgt]) : make_uint4(m1[dgt], 0u, m2[dgt], 0u);
+        *reinterpret_cast<uint4*>(fb + (grp * 4 + 3) * 64) = make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        const int k0 = b * 256 + lane * 8;
+        *reinterpret_cast<uint2*>(dig + k0) =
+            make_uint2(pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q0[4], q0[5], q0[6], q0[7]));
+        *reinterpret_cast<uint2*>(dig + p.dig_stride + k0) =
+            make_uint2(pack4(q1[0], q1[1], q1[2], q1[3]), pack4(q1[4], q1[5], q1[6], q1[7]));
+        *reinterpret_cast<uint2*>(dig + 2 * p.dig_stride + k0) =
+            make_uint2(pack4(q2[0], q2[1], q2[2], q2[3]), pack4(q2[4], q2[5], q2[6], q2[7]));
+      }
+      if ((lane & 1) == 0) xsum[b * 16 + (lane >> 1)] = s16[g];
+      if ((lane & 3) == 0) xsum[p.K / 16 + b * 8 + (lane >> 2)] = s32[g];
+      if (lane == 0) xscale[b] = m[g] / 127.f;
     }
   }
+  ssq = warp_sum(ssq);
+  if (lane == 0) misc[warp] = ssq;
+}
+
+// 1/rms of the RMSNORM input from the warps' sums of x^2 (after the barrier that follows
+// prepare_x), 1 otherwise: 1 / sqrt(mean(x^2) + eps) (phi4.rs:593-599).
+__device__ __forceinline__ float row_scale(const GemvParams& p, const float* misc) {
+  if (p.mode != RRR_X_RMSNORM) return 1.f;
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kGroups * kNW; ++w) tot += misc[w];
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)p.K), p.eps)));
 }
 
 // Row tile j (0 = gate / plain, 1 = up) of work tile wt: first weight row and row count.
@@ -447,42 +464,68 @@ __device__ __forceinline__ int tile_rows(const GemvParams& p, int wt) {
 
 // ---------------------------------------------------------------- the kernel
 template <int QT, bool FRAG>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kq_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kThreads, kMinCtas) gemv_kq_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int BB = KQ<QT>::kBlockBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // warps [0, kGroups*kNW): consumers of group warp / kNW; then one producer per group
+  const bool producer = warp >= kGroups * kNW;
+  const int grp = producer ? warp - kGroups * kNW : warp / kNW;
+  const int cw = warp % kNW;  // consumer warp index within its group
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars) + grp * 2 * p.nstages;
   uint64_t* empty = full + p.nstages;
+  uint8_t* ring = smem + (size_t)grp * p.nstages * p.stage_bytes;
   int8_t* dig = reinterpret_cast<int8_t*>(smem + p.off_dig);
   float* xscale = reinterpret_cast<float*>(smem + p.off_xscale);
   float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);
   float* xsum32 = xsum + p.K / 16;
-  float* red = reinterpret_cast<float*>(smem + p.off_red);
-  float* gate = reinterpret_cast<float*>(smem + p.off_gate);
+  float* red = reinterpret_cast<float*>(smem + p.off_red) + grp * kSlots * kNW * kTileRows;
+  float* gate = reinterpret_cast<float*>(smem + p.off_gate) + grp * kSlots * kTileRows;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.off_misc);
   float* misc = reinterpret_cast<float*>(smem + p.off_misc + 16);
+  int* cnt = reinterpret_cast<int*>(smem + p.off_misc + 16 + kGroups * kNW * 4) + grp * kSlots;
   const int n_sub = p.out_mode ? 2 : 1;  // row tiles per work tile
+  // this group's tiles: vb, vb + vstride, ...: group 0 of every CTA first, so that with
+  // fewer tiles than groups every SM still gets work
+  const int vb = grp * gridDim.x + blockIdx.x, vstride = gridDim.x * kGroups;
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.nstages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kNW);
-    }
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bars);
+    for (int g = 0; g < kGroups; ++g)
+      for (int s = 0; s < p.nstages; ++s) {
+        mbar_init(&bars[g * 2 * p.nstages + s], 1);
+        mbar_init(&bars[g * 2 * p.nstages + p.nstages + s], kNW);
+      }
     *abort_flag = 0;
-    int* cnt0 = reinterpret_cast<int*>(smem + p.off_misc + 16 + kNW * 4);
-    for (int i = 0; i < kSlots; ++i) cnt0[i] = 0;
+    int* cnt0 = reinterpret_cast<int*>(smem + p.off_misc + 16 + kGroups * kNW * 4);
+    for (int i = 0; i < kGroups * kSlots; ++i) cnt0[i] = 0;
     fence_mbarrier_init();
   }
   __syncthreads();
   pdl_launch_dependents();
 
-  if (warp == kNW) {
+  if (producer) {
     // ------------------------------------------------------------ producer warp
+    // First the GEMV input (and gamma) into L2, ahead of this CTA's weight stream: the
+    // consumers read it after the preceding grid has finished, by which time the weight
+    // copies of every CTA fill the memory queues.
+    if (lane == 0) {
+      const uint32_t xb = p.mode == kXBf16 ? (uint32_t)p.K * 2
+                          : p.mode == RRR_X_SILU_GATE ? (uint32_t)p.K * 8
+                          : p.mode == RRR_X_GQA_V ? (uint32_t)(p.n_kv * p.hd) * 4 : (uint32_t)p.K * 4;
+      const void* xs = p.mode == kXBf16 ? (const void*)p.xb
+                       : p.mode == RRR_X_GQA_V ? (const void*)(p.x + (p.n_q + p.n_kv) * p.hd)
+                       : (const void*)p.x;
+      for (uint32_t o = 0; o < xb; o += 16384) bulk_prefetch_l2((const char*)xs + o, min(16384u, xb - o));
+      if (p.mode == RRR_X_RMSNORM)
+        for (uint32_t o = 0; o < (uint32_t)p.K * 4; o += 16384)
+          bulk_prefetch_l2((const char*)p.gamma + o, min(16384u, (uint32_t)p.K * 4 - o));
+    }
     const long long floor_total = p.total_bytes & ~15ll;
     int issued = 0, s = 0;
     uint32_t ph = 0;
     bool ok = true;
-    for (int wt = blockIdx.x; wt < p.n_tiles && ok; wt += gridDim.x) {
+    for (int wt = vb; wt < p.n_tiles && ok; wt += vstride) {
       const int rows = tile_rows(p, wt);
       for (int j = 0; j < n_sub && ok; ++j) {
         const int row0 = tile_row0(p, wt, j);
@@ -499,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kq_kernel(const GemvParams p
           const int kb0 = c * p.kc;
           const int kcount = min(p.kc, p.nb - kb0);
           const long long chunk = (long long)kcount * BB;
-          uint8_t* stage = smem + (size_t)s * p.stage_bytes;
+          uint8_t* stage = ring + (size_t)s * p.stage_bytes;
           long long a0 = 0, a1 = 0;
           uint32_t tx = 0;
           if (lane < rows) {
@@ -541,17 +584,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kq_kernel(const GemvParams p
   // -------------------------------------------------------------- consumer warps
   pdl_wait();
   prepare_x<FRAG>(p, dig, xscale, xsum, misc, warp, lane);
-  named_barrier(1, kNW * 32);
+  named_barrier(1, kGroups * kNW * 32);
+  const float inv_rms = row_scale(p, misc);
 
   const Lane L = make_lane(lane, QT == RRR_Q4_K);
-  int* cnt = reinterpret_cast<int*>(smem + p.off_misc + 16 + kNW * 4);
 
   // Byte offset mod 16 of a chunk start inside its 16-byte granule (only Q6_K rows and
   // chunks can start unaligned); 32-bit arithmetic on the residues.
   const int rb16 = (int)(p.row_bytes & 15), cb16 = (p.kc * BB) & 15;
   int s = 0, ts = 0, ss = 0;  // stage index, row-tile sequence, stage sequence
   uint32_t ph = 0;    // phase parity of stage s
-  for (int wt = blockIdx.x; wt < p.n_tiles; wt += gridDim.x) {
+  for (int wt = vb; wt < p.n_tiles; wt += vstride) {
     const int rows = tile_rows(p, wt);
     for (int j = 0; j < n_sub; ++j, ++ts) {
       const int row0 = tile_row0(p, wt, j);
@@ -571,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kq_kernel(const GemvParams p
         if (!have) continue;
         const int kb0 = c * p.kc;
         const int items = min(p.kc, p.nb - kb0);
-        const uint8_t* stage = smem + cs * p.stage_bytes;
+        const uint8_t* stage = ring + cs * p.stage_bytes;
         int off0 = 0, off1 = 0;
         if (QT == RRR_Q6_K) {
           off0 = ((row0 + L.g) * rb16 + c * cb16) & 15;
@@ -581,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kq_kernel(const GemvParams p
         const uint8_t* r1 = stage + (L.g + 8) * p.row_stride + off1;
         // Whole blocks are the work items; the warp that starts the list rotates from
         // stage to stage so leftover blocks (12 per stage for K = 3072) spread over warps.
-        const int w0 = (warp + ss * items) % kNW;
+        const int w0 = (cw + ss * items) % kNW;
         ++ss;
         for (int bi = w0; bi < items; bi += kNW) {
           const uint8_t* q0 = r0 + bi * BB;
@@ -609,8 +652,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kq_kernel(const GemvParams p
       const int slot = ts % kSlots;
       float* rb = red + slot * kNW * kTileRows;
       if (L.tig == 0) {
-        rb[warp * kTileRows + L.g] = acc0;
-        rb[warp * kTileRows + L.g + 8] = acc1;
+        rb[cw * kTileRows + L.g] = acc0;
+        rb[cw * kTileRows + L.g + 8] = acc1;
       }
       __syncwarp();
       int last = 0;
@@ -625,6 +668,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kq_kernel(const GemvParams p
           float v = 0.f;
 #pragma unroll
           for (int w = 0; w < kNW; ++w) v += rb[w * kTileRows + lane];
+          v *= inv_rms;
           if (p.out_mode == 0) {
             const int row = row0 + lane;
             if (p.residual) v = p.residual[row] + v;
@@ -664,22 +708,22 @@ int plan_layout(GemvParams& p, bool frag) {
   p.stage_bytes = kTileRows * p.row_stride;
   p.dig_stride = p.K + 96;
   const int dig_bytes = frag ? p.K * 8 : 3 * p.dig_stride;
-  int fixed = 2 * kMaxStages * 8 + dig_bytes + 16;
+  int fixed = kGroups * 2 * kMaxStages * 8 + dig_bytes + 16;
   fixed += p.nb * 4 + 16 + (p.K / 16) * 4 + (p.K / 32) * 4;  // xscale, xsum16, xsum32
-  fixed += kSlots * kNW * kTileRows * 4;                     // red
-  fixed += kSlots * kTileRows * 4 + 16 + kNW * 4 + kSlots * 4 + 64;  // gate, misc
-  p.nstages = std::max(2, std::min(kMaxStages, (kSmemBudget - fixed) / p.stage_bytes));
-  int off = p.nstages * p.stage_bytes;
-  p.off_bars = off;          off += 2 * p.nstages * 8;
+  fixed += kGroups * kSlots * kNW * kTileRows * 4;            // red
+  fixed += kGroups * kSlots * kTileRows * 4 + 16 + kGroups * kNW * 4 + kGroups * kSlots * 4 + 64;
+  p.nstages = std::max(2, std::min(kMaxStages, (kSmemBudget - fixed) / (kGroups * p.stage_bytes)));
+  int off = kGroups * p.nstages * p.stage_bytes;
+  p.off_bars = off;          off += kGroups * 2 * p.nstages * 8;
   off = (off + 15) & ~15;
   p.off_dig = off;           off += dig_bytes;
   off = (off + 15) & ~15;
   p.off_xscale = off;        off += p.nb * 4;
   off = (off + 15) & ~15;
   p.off_xsum = off;          off += (p.K / 16) * 4 + (p.K / 32) * 4;  // xsum16, xsum32
-  p.off_red = off;           off += kSlots * kNW * kTileRows * 4;
-  p.off_gate = off;          off += kSlots * kTileRows * 4;
-  p.off_misc = off;          off += 16 + kNW * 4 + kSlots * 4;
+  p.off_red = off;           off += kGroups * kSlots * kNW * kTileRows * 4;
+  p.off_gate = off;          off += kGroups * kSlots * kTileRows * 4;
+  p.off_misc = off;          off += 16 + kGroups * kNW * 4 + kGroups * kSlots * 4;
   return (off + 127) & ~127;
 }
 
@@ -715,14 +759,9 @@ cudaError_t launch_k(const LaunchEnv& env, const GemvParams& p, int smem) {
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     if (n_cache < 32) cache[n_cache++] = OccEntry{(const void*)kern, dev, smem, per_sm};
   }
-  // Two CTAs per SM (two producers and 16 consumer warps per SM); RRR_GEMV_CTAS_PER_SM
-  // overrides.
-  static int ctas_per_sm = [] {
-    const char* e = getenv("RRR_GEMV_CTAS_PER_SM");
-    const int v = e ? atoi(e) : 2;
-    return v >= 1 && v <= 4 ? v : 2;
-  }();
-  const int grid = std::min(p.n_tiles, std::min(per_sm, ctas_per_sm) * env.sm_count);
+  // kMinCtas CTAs per SM (two producers and 16 consumer warps per SM); each CTA runs
+  // kGroups producer/consumer groups, so it needs at least kGroups tiles to be busy
+  const int grid = std::max(1, std::min(p.n_tiles, std::min(per_sm, kMinCtas) * env.sm_count));
   return rrr_launch_pdl(kern, dim3(grid), dim3(kThreads), smem, env.stream, env.pdl, p);
 }
 

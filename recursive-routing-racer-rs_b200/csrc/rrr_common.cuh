@@ -108,6 +108,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Prefetch of a global range into L2 (no destination, no completion tracking). src and
+// bytes must be multiples of 16. Prefetching lines that another grid is still writing is
+// harmless: L2 stays coherent with those writes.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Programmatic dependent launch: wait for the preceding grid's memory to be visible /
 // allow the next grid to start launching. No-ops when not launched with PDL.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
