@@ -276,7 +276,8 @@ int rrr_phi4_destroy(rrr_phi4* m);
  * rank creates its exchange buffer, passes its 64-byte CUDA IPC handle to the other
  * ranks (any host channel: torch.distributed, a file, MPI) and connects with all
  * world handles in rank order. The exchanges then run as one kernel over NVLink peer
- * memory (peer stores plus release/acquire flags, no NCCL), capturable in CUDA graphs:
+ * memory (peer stores of values tagged with the call's epoch in one 8-byte word, the
+ * receiver waiting on the words themselves; no NCCL), capturable in CUDA graphs:
  *   all-reduce: x[i] = sum over ranks in rank order (identical bits on every rank),
  *   all-gather: out[r*n + i] = rank r's part[i] (part may be out + rank*n).
  * Every rank must issue the same sequence of calls with the same n <= max_elems. A wait

@@ -2,16 +2,18 @@
 // NVLink peer memory, for the tensor-parallel decode step (one process per GPU).
 //
 // Every rank owns an exchange buffer, mapped into the other ranks' processes through CUDA
-// IPC handles: data[2][world][max_elems] f32 and flags[2][world][kMaxCtas] u32. A call
+// IPC handles: slots[2][world][max_elems] of 8-byte words. Each word carries one value
+// and the epoch of the call that wrote it (value bits low, epoch high), stored and loaded
+// as one naturally aligned 64-bit access (single-copy atomic), so the receiver waits on
+// the data itself: no fences and no separate flags, one NVLink trip per exchange. A call
 // of `n` elements runs C CTAs; CTA c owns elements [c*chunk, (c+1)*chunk). It
-//   1. writes its chunk of this rank's input into slot `rank` of every rank's buffer
-//      (peer stores over NVLink; the local one is an ordinary store),
-//   2. makes the stores visible system-wide and sets flags[set][rank][c] = epoch on every
-//      rank (epoch = this CTA's call counter + 1, set = epoch & 1),
-//   3. waits until flags[set][r][c] == epoch for every r in its own buffer (bounded: it
+//   1. stores its elements of this rank's input, tagged with the epoch, into slot `rank`
+//      of every rank's buffer (peer stores over NVLink; the local one is an ordinary store;
+//      epoch = this CTA's call counter + 1, set = epoch & 1),
+//   2. waits, element by element, until every rank's slot carries the epoch (bounded: it
 //      gives up after about a second, records an error in the context's device flag and
-//      returns), then
-//   4. sums the slots in rank order (all-reduce: every rank gets identical bits) or copies
+//      stops waiting), and
+//   3. sums the slots in rank order (all-reduce: every rank gets identical bits) or copies
 //      them in rank order (all-gather).
 // The two buffer sets alternate between calls: a rank can be one call ahead of another
 // but not two (it needs every rank's data of the previous call first), so a set is never
@@ -37,20 +39,38 @@ constexpr int kThreadsX = 512;
 constexpr int kDevErrCommTimeout = 5;
 
 struct Peers {
-  float* data[kMaxWorld];       // each rank's data region (this rank's own at index rank)
-  unsigned* flags[kMaxWorld];   // each rank's flag region
+  unsigned long long* slots[kMaxWorld];  // each rank's buffer (this rank's own at index rank)
 };
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+
+// The value of word p once its epoch is e; gives up (ok = false) after kWaitLimitNs.
+__device__ __forceinline__ float wait_word(const unsigned long long* p, unsigned e, bool& ok,
+                                           int* err) {
+  unsigned long long w = ld_relaxed_sys_u64(p);
+  if ((unsigned)(w >> 32) != e && ok) {
+    const uint64_t t0 = globaltimer_ns();
+    for (int i = 0;; ++i) {
+      w = ld_relaxed_sys_u64(p);
+      if ((unsigned)(w >> 32) == e) break;
+      if ((i & 63) == 63 && globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicCAS(err, 0, kDevErrCommTimeout);
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __uint_as_float((unsigned)w);
 }
 
-// mode 0: x[i] = sum over ranks (in place, `out` == `in`); mode 1: out[r*n + i] = rank r's in[i]
+// mode 0: x[i] = sum over ranks (in place allowed); mode 1: out[r*n + i] = rank r's in[i]
 __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const float* in, float* out,
                                                               int64_t n, int64_t chunk, int rank,
                                                               int world, int64_t max_elems,
@@ -58,54 +78,28 @@ __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const 
   const int c = blockIdx.x;
   const int64_t i0 = (int64_t)c * chunk, i1 = min(n, i0 + chunk);
   __shared__ unsigned s_epoch;
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) {
-    s_epoch = counters[c] + 1;
-    s_ok = 1;
-  }
+  if (threadIdx.x == 0) s_epoch = counters[c] + 1;
   __syncthreads();
   const unsigned e = s_epoch;
   const int set = e & 1;
-  // 1. this rank's chunk into slot `rank` of every buffer
+  const unsigned long long tag = (unsigned long long)e << 32;
+  // 1. this rank's elements, tagged, into slot `rank` of every buffer
   for (int r = 0; r < world; ++r) {
-    float* dst = peers.data[r] + ((int64_t)set * world + rank) * max_elems;
-    for (int64_t i = i0 + threadIdx.x; i < i1; i += kThreadsX) dst[i] = in[i];
+    unsigned long long* dst = peers.slots[r] + ((int64_t)set * world + rank) * max_elems;
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += kThreadsX)
+      st_relaxed_sys_u64(dst + i, tag | __float_as_uint(in[i]));
   }
-  // 2. stores visible to the other GPUs, then the flags
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < world) {
-    unsigned* f = peers.flags[threadIdx.x] + ((int64_t)set * world + rank) * kMaxCtas + c;
-    st_release_sys(f, e);
-  }
-  // 3. every rank's chunk has arrived in this buffer
-  if (threadIdx.x < world) {
-    const unsigned* f = peers.flags[rank] + ((int64_t)set * world + threadIdx.x) * kMaxCtas + c;
-    if (ld_acquire_sys(f) != e) {
-      const uint64_t t0 = globaltimer_ns();
-      while (ld_acquire_sys(f) != e) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          atomicCAS(err, 0, kDevErrCommTimeout);
-          s_ok = 0;
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  // 4. combine in rank order (the slots were written by other GPUs: read around L1)
-  const float* base = peers.data[rank] + (int64_t)set * world * max_elems;
-  if (s_ok) {
+  // 2.-3. every rank's element, in rank order
+  const unsigned long long* base = peers.slots[rank] + (int64_t)set * world * max_elems;
+  bool ok = true;
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += kThreadsX) {
     if (mode == 0) {
-      for (int64_t i = i0 + threadIdx.x; i < i1; i += kThreadsX) {
-        float acc = __ldcg(base + i);
-        for (int r = 1; r < world; ++r) acc += __ldcg(base + (int64_t)r * max_elems + i);
-        out[i] = acc;
-      }
+      float acc = wait_word(base + i, e, ok, err);
+      for (int r = 1; r < world; ++r) acc += wait_word(base + (int64_t)r * max_elems + i, e, ok, err);
+      out[i] = acc;
     } else {
       for (int r = 0; r < world; ++r)
-        for (int64_t i = i0 + threadIdx.x; i < i1; i += kThreadsX)
-          out[(int64_t)r * n + i] = __ldcg(base + (int64_t)r * max_elems + i);
+        out[(int64_t)r * n + i] = wait_word(base + (int64_t)r * max_elems + i, e, ok, err);
     }
   }
   __syncthreads();
@@ -130,7 +124,7 @@ struct rrr_comm {
 using namespace rrr;
 
 static size_t data_bytes(int world, int64_t max_elems) {
-  return (size_t)2 * world * max_elems * sizeof(float);
+  return (size_t)2 * world * max_elems * sizeof(unsigned long long);
 }
 
 extern "C" {
@@ -150,7 +144,7 @@ int rrr_comm_create(rrr_ctx* ctx, int rank, int world, int64_t max_elems, rrr_co
   c->rank = rank;
   c->world = world;
   c->max_elems = (max_elems + 3) / 4 * 4;
-  c->bytes = data_bytes(world, c->max_elems) + (size_t)2 * world * kMaxCtas * sizeof(unsigned);
+  c->bytes = data_bytes(world, c->max_elems);
   cudaError_t e = cudaMalloc(&c->local, c->bytes);
   if (e == cudaSuccess) e = cudaMemset(c->local, 0, c->bytes);
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, kMaxCtas * sizeof(unsigned));
@@ -194,8 +188,7 @@ int rrr_comm_connect(rrr_comm* c, const void* handles) {
       c->mapped[r] = static_cast<char*>(p);
       base = c->mapped[r];
     }
-    c->peers.data[r] = reinterpret_cast<float*>(base);
-    c->peers.flags[r] = reinterpret_cast<unsigned*>(base + data_bytes(c->world, c->max_elems));
+    c->peers.slots[r] = reinterpret_cast<unsigned long long*>(base);
   }
   c->connected = true;
   return RRR_OK;
