@@ -35,7 +35,7 @@ namespace {
 
 constexpr int kMaxCtas = 64;
 constexpr int kMaxWorld = 8;
-constexpr int kThreadsX = 512;
+constexpr int kThreadsX = 256;  // few registers: co-resident with a finishing GEMV
 constexpr int kDevErrCommTimeout = 5;
 
 struct Peers {
@@ -75,6 +75,10 @@ __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const 
                                                               int64_t n, int64_t chunk, int rank,
                                                               int world, int64_t max_elems,
                                                               unsigned* counters, int mode, int* err) {
+  // launched with programmatic dependent launch: let the next kernel (a GEMV streaming its
+  // weights) start now, and wait for the kernel that produced `in`
+  pdl_launch_dependents();
+  pdl_wait();
   const int c = blockIdx.x;
   const int64_t i0 = (int64_t)c * chunk, i1 = min(n, i0 + chunk);
   __shared__ unsigned s_epoch;
@@ -204,14 +208,15 @@ static int comm_launch(rrr_comm* c, const float* in, float* out, int64_t n, int 
                      (long long)n, (long long)c->max_elems);
   int rc = bind_device(c->ctx);
   if (rc) return rc;
-  // about 4 KB per CTA and rank, at most kMaxCtas CTAs
-  int64_t chunk = std::max<int64_t>(1024, (n + kMaxCtas - 1) / kMaxCtas);
+  // about 2 KB of values per CTA and rank, at most kMaxCtas CTAs
+  int64_t chunk = std::max<int64_t>(512, (n + kMaxCtas - 1) / kMaxCtas);
   chunk = (chunk + 3) / 4 * 4;
   const int ctas = (int)((n + chunk - 1) / chunk);
   const LaunchEnv env = make_env(c->ctx, stream);
-  exchange_kernel<<<ctas, kThreadsX, 0, env.stream>>>(c->peers, in, out, n, chunk, c->rank, c->world,
-                                                      c->max_elems, c->counters, mode, env.d_err);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = rrr_launch_pdl(exchange_kernel, dim3(ctas), dim3(kThreadsX), 0, env.stream, env.pdl,
+                                 c->peers, in, out, n, chunk, c->rank, c->world, c->max_elems,
+                                 c->counters, mode, env.d_err);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(c->ctx, e, what);
   return RRR_OK;
 }
