@@ -143,6 +143,27 @@ int rrr_dequant_kq(rrr_ctx* ctx, int qtype, const void* w_raw, float* out,
 int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16_t* x_bf16,
                         float* y, int M, int K, int N, void* stream);
 
+/* Same with an optional f32 residual [M, N] added in the epilogue (may equal y), for the
+ * residual adds of the batched decode step (phi4.rs:1393-1403, done on the CPU there). */
+int rrr_gemm_kq_batched_ex(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16_t* x_bf16,
+                           float* y, int M, int K, int N, const float* residual, void* stream);
+
+/* ---- batched decode-step glue (M tokens, each at position 0) -----------------------
+ * Producers of the bf16 GEMM inputs (phi4.rs:1198-1445 computes these per token on the
+ * CPU): rmsnorm rows -> bf16; the position-0 attention output V of each head's KV group
+ * from qkv rows [n_q*hd | n_kv*hd | n_kv*hd] into a k_window-wide bf16 row, zero outside
+ * [k_offset, k_offset + n_q*hd) (the tensor-parallel window, see RRR_X_GQA_V); SiLU(gate)*up
+ * rows ([gate | up] f32 [rows, 2F]) -> bf16 [rows, F]. The batched logits normalise the M
+ * rows (gamma != NULL, into x_norm f32 [M, K]) and multiply by the row-major [V, K] f32
+ * matrix with one cuBLAS SGEMM (a plain library GEMM): y f32 [M, V]. */
+int rrr_rmsnorm_bf16(rrr_ctx* ctx, const float* x, const float* gamma, uint16_t* y, int rows,
+                     int d, float eps, void* stream);
+int rrr_gqa_v_bf16(rrr_ctx* ctx, const float* qkv, uint16_t* y, int rows, int n_q, int n_kv,
+                   int head_dim, int k_window, int k_offset, void* stream);
+int rrr_silu_gate_bf16(rrr_ctx* ctx, const float* gu, uint16_t* y, int rows, int F, void* stream);
+int rrr_logits_f32_batched(rrr_ctx* ctx, const float* W, const float* x, float* x_norm, float* y,
+                           int M, int V, int K, const float* gamma, float eps, void* stream);
+
 /* ---- kernel (3): RMSNorm, y = gamma * x / sqrt(mean(x^2) + eps), `rows` rows of d ---
  * Replaces gpu_rmsnorm / the `rmsnorm` shader (phi4.rs:680-697, push [num_rows, d]). */
 int rrr_rmsnorm(rrr_ctx* ctx, const float* x, const float* gamma, float* y, int rows,
@@ -289,6 +310,11 @@ int rrr_comm_connect(rrr_comm* comm, const void* ipc_handles /* world x 64 bytes
 int rrr_comm_allreduce_f32(rrr_comm* comm, float* x, int64_t n, void* stream);
 int rrr_comm_allgather_f32(rrr_comm* comm, float* out, const float* part, int64_t n_per_rank,
                            void* stream);
+/* All-gather of row-split rows: part f32 [rows, n_per_row] of every rank into
+ * out f32 [rows, world * n_per_row] (rank r's row m at out[m][r*n_per_row ...]); out must
+ * not overlap part. (rows * n_per_row <= max_elems.) */
+int rrr_comm_allgather_rows_f32(rrr_comm* comm, float* out, const float* part, int rows,
+                                int64_t n_per_row, void* stream);
 /* Unmaps the other ranks' buffers (after this rank's last exchange has completed). Call
  * it on every rank and synchronise the ranks before any rank calls rrr_comm_destroy,
  * which frees this rank's buffer (and disconnects first if needed). */

@@ -153,6 +153,7 @@ int rrr_destroy(rrr_ctx* ctx) {
   bind_device(ctx);
   cudaDeviceSynchronize();
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->cublas) rrr::destroy_cublas(ctx->cublas);
   delete ctx;
   return RRR_OK;
 }
@@ -351,8 +352,8 @@ int rrr_dequant_kq(rrr_ctx* ctx, int qtype, const void* w, float* out, int64_t n
   return RRR_OK;
 }
 
-int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w, const uint16_t* x, float* y,
-                        int M, int K, int N, void* stream) {
+int rrr_gemm_kq_batched_ex(rrr_ctx* ctx, int qtype, const void* w, const uint16_t* x, float* y,
+                           int M, int K, int N, const float* residual, void* stream) {
   RRR_CHECK_CTX(ctx);
   int rc = check_qtype(ctx, qtype, "rrr_gemm_kq_batched");
   if (rc) return rc;
@@ -360,22 +361,30 @@ int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w, const uint16_t* 
   if (M < 1 || N < 1 || K < 256 || K % 256 != 0 || K > kGemvMaxK)
     return set_error(ctx, RRR_ERR_BAD_SHAPE,
                      "rrr_gemm_kq_batched: need M, N >= 1, K %% 256 == 0, 256 <= K <= %d", kGemvMaxK);
-  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(y, 16))
-    return set_error(ctx, RRR_ERR_MISALIGNED, "rrr_gemm_kq_batched: W, X, Y must be 16-byte aligned");
+  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(y, 16) || (residual && !aligned(residual, 16)))
+    return set_error(ctx, RRR_ERR_MISALIGNED, "rrr_gemm_kq_batched: W, X, Y, residual must be 16-byte aligned");
   if (overlap(y, (size_t)M * N * 4, x, (size_t)M * K * 2))
     return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemm_kq_batched: Y must not overlap X");
+  if (residual && residual != y && overlap(y, (size_t)M * N * 4, residual, (size_t)M * N * 4))
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemm_kq_batched: residual must equal Y or not overlap it");
   RRR_BIND(ctx);
   const LaunchEnv env = make_env(ctx, stream);
   TcPlan plan;
   if (M >= 16 && plan_gemm_kq_tc(qtype, M, K, N, ctx->sm_count, &plan)) {
-    RRR_LAUNCH_CHECK(ctx, launch_gemm_kq_tc(env, qtype, w, x, y, M, K, N, plan),
+    RRR_LAUNCH_CHECK(ctx, launch_gemm_kq_tc(env, qtype, w, x, y, M, K, N, plan, residual),
                      "rrr_gemm_kq_batched (tensor cores) launch");
     return RRR_OK;
   }
   for (int m = 0; m < M; ++m)
-    RRR_LAUNCH_CHECK(ctx, launch_gemv_kq_bf16(env, qtype, w, x + (size_t)m * K, y + (size_t)m * N, K, N),
+    RRR_LAUNCH_CHECK(ctx, launch_gemv_kq_bf16(env, qtype, w, x + (size_t)m * K, y + (size_t)m * N, K, N,
+                                              residual ? residual + (size_t)m * N : nullptr),
                      "rrr_gemm_kq_batched (per-token) launch");
   return RRR_OK;
+}
+
+int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w, const uint16_t* x, float* y,
+                        int M, int K, int N, void* stream) {
+  return rrr_gemm_kq_batched_ex(ctx, qtype, w, x, y, M, K, N, nullptr, stream);
 }
 
 int rrr_rmsnorm(rrr_ctx* ctx, const float* x, const float* gamma, float* y, int rows, int d,

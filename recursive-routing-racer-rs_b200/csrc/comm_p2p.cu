@@ -70,11 +70,14 @@ __device__ __forceinline__ float wait_word(const unsigned long long* p, unsigned
   return __uint_as_float((unsigned)w);
 }
 
-// mode 0: x[i] = sum over ranks (in place allowed); mode 1: out[r*n + i] = rank r's in[i]
+// mode 0: x[i] = sum over ranks (in place allowed); mode 1: all-gather, element i of rank
+// r's input to out[(i / npr) * world * npr + r * npr + i % npr] (npr = n: concatenation;
+// npr < n: rows of npr elements interleaved by rank, the layout of row-split logits)
 __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const float* in, float* out,
                                                               int64_t n, int64_t chunk, int rank,
                                                               int world, int64_t max_elems,
-                                                              unsigned* counters, int mode, int* err) {
+                                                              unsigned* counters, int mode,
+                                                              int64_t npr, int* err) {
   // launched with programmatic dependent launch: let the next kernel (a GEMV streaming its
   // weights) start now, and wait for the kernel that produced `in`
   pdl_launch_dependents();
@@ -102,8 +105,9 @@ __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const 
       for (int r = 1; r < world; ++r) acc += wait_word(base + (int64_t)r * max_elems + i, e, ok, err);
       out[i] = acc;
     } else {
+      float* o = out + (i / npr) * world * npr + i % npr;
       for (int r = 0; r < world; ++r)
-        out[(int64_t)r * n + i] = wait_word(base + (int64_t)r * max_elems + i, e, ok, err);
+        o[(int64_t)r * npr] = wait_word(base + (int64_t)r * max_elems + i, e, ok, err);
     }
   }
   __syncthreads();
@@ -198,8 +202,8 @@ int rrr_comm_connect(rrr_comm* c, const void* handles) {
   return RRR_OK;
 }
 
-static int comm_launch(rrr_comm* c, const float* in, float* out, int64_t n, int mode, void* stream,
-                       const char* what) {
+static int comm_launch(rrr_comm* c, const float* in, float* out, int64_t n, int mode, int64_t npr,
+                       void* stream, const char* what) {
   if (!c) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null communicator");
   if (!c->connected) return set_error(c->ctx, RRR_ERR_INVALID_ARG, "%s: not connected", what);
   if (!in || !out) return set_error(c->ctx, RRR_ERR_INVALID_ARG, "%s: null pointer", what);
@@ -215,14 +219,14 @@ static int comm_launch(rrr_comm* c, const float* in, float* out, int64_t n, int 
   const LaunchEnv env = make_env(c->ctx, stream);
   cudaError_t e = rrr_launch_pdl(exchange_kernel, dim3(ctas), dim3(kThreadsX), 0, env.stream, env.pdl,
                                  c->peers, in, out, n, chunk, c->rank, c->world, c->max_elems,
-                                 c->counters, mode, env.d_err);
+                                 c->counters, mode, npr, env.d_err);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(c->ctx, e, what);
   return RRR_OK;
 }
 
 int rrr_comm_allreduce_f32(rrr_comm* c, float* x, int64_t n, void* stream) {
-  return comm_launch(c, x, x, n, 0, stream, "rrr_comm_allreduce_f32");
+  return comm_launch(c, x, x, n, 0, n, stream, "rrr_comm_allreduce_f32");
 }
 
 int rrr_comm_allgather_f32(rrr_comm* c, float* out, const float* part, int64_t n_per_rank,
@@ -232,7 +236,18 @@ int rrr_comm_allgather_f32(rrr_comm* c, float* out, const float* part, int64_t n
       !((const char*)out + (size_t)c->world * n_per_rank * 4 <= (const char*)part ||
         (const char*)part + (size_t)n_per_rank * 4 <= (const char*)out))
     return set_error(c->ctx, RRR_ERR_INVALID_ARG, "rrr_comm_allgather_f32: out overlaps part");
-  return comm_launch(c, part, out, n_per_rank, 1, stream, "rrr_comm_allgather_f32");
+  return comm_launch(c, part, out, n_per_rank, 1, n_per_rank, stream, "rrr_comm_allgather_f32");
+}
+
+int rrr_comm_allgather_rows_f32(rrr_comm* c, float* out, const float* part, int rows,
+                                int64_t n_per_row, void* stream) {
+  if (c && (rows < 1 || n_per_row < 1))
+    return set_error(c->ctx, RRR_ERR_BAD_SHAPE, "rrr_comm_allgather_rows_f32: rows, n_per_row >= 1");
+  if (c && out && part && !((const char*)out + (size_t)c->world * rows * n_per_row * 4 <= (const char*)part ||
+                            (const char*)part + (size_t)rows * n_per_row * 4 <= (const char*)out))
+    return set_error(c->ctx, RRR_ERR_INVALID_ARG, "rrr_comm_allgather_rows_f32: out overlaps part");
+  return comm_launch(c, part, out, (int64_t)rows * n_per_row, 1, n_per_row, stream,
+                     "rrr_comm_allgather_rows_f32");
 }
 
 int rrr_comm_disconnect(rrr_comm* c) {

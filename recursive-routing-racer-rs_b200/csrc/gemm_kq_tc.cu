@@ -60,6 +60,7 @@ struct TcParams {
   const uint8_t* w;
   const uint8_t* w_end;
   float* y;
+  const float* residual;  // optional [M, N] f32 added in the epilogue (may equal y)
   long long row_bytes;
   int M, K, N, nb, bb;  // nb super-blocks per row, bb bytes per super-block
   int tn, splits, stages, slot, tmem_cols, n_tiles;
@@ -581,7 +582,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int m = m0 + c + i;
-            if (m < p.M && n < p.N) p.y[(size_t)m * p.N + n] = __uint_as_float(v[i]);
+            if (m < p.M && n < p.N) {
+              const size_t o = (size_t)m * p.N + n;
+              const float r = p.residual ? p.residual[o] : 0.f;
+              p.y[o] = __uint_as_float(v[i]) + r;
+            }
           }
         } else {
 #pragma unroll
@@ -618,11 +623,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m = m0 + j, nn = n0 + r4;
         if (m < p.M) {
           float* dst = p.y + (size_t)m * p.N + nn;
+          const float* res = p.residual ? p.residual + (size_t)m * p.N + nn : nullptr;
           if ((p.N & 3) == 0 && nn + 3 < p.N) {
+            if (res) {
+              const float4 r4 = *reinterpret_cast<const float4*>(res);
+              acc.x += r4.x;
+              acc.y += r4.y;
+              acc.z += r4.z;
+              acc.w += r4.w;
+            }
             *reinterpret_cast<float4*>(dst) = acc;
           } else {
             const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-            for (int e = 0; e < 4 && nn + e < p.N; ++e) dst[e] = a4[e];
+            for (int e = 0; e < 4 && nn + e < p.N; ++e) dst[e] = a4[e] + (res ? res[e] : 0.f);
           }
         }
       }
@@ -688,7 +701,7 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint6
 
 template <int QT>
 cudaError_t launch_t(const LaunchEnv& env, const TcPlan& pl, const void* w, const uint16_t* x,
-                     float* y, int M, int K, int N) {
+                     float* y, int M, int K, int N, const float* residual) {
   CUtensorMap map, wmap;
   if (!encode_2d(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M,
                  (uint64_t)K * 2, (uint32_t)kBK, (uint32_t)pl.tn, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -708,6 +721,7 @@ cudaError_t launch_t(const LaunchEnv& env, const TcPlan& pl, const void* w, cons
   p.row_bytes = (long long)p.nb * p.bb;
   p.w_end = p.w + p.row_bytes * N;
   p.y = y;
+  p.residual = residual;
   p.M = M;
   p.K = K;
   p.N = N;
@@ -806,11 +820,11 @@ bool plan_gemm_kq_tc(int qtype, int M, int K, int N, int sm_count, TcPlan* pl) {
 
 cudaError_t launch_gemm_kq_tc(const LaunchEnv& env, int qtype, const void* w,
                               const uint16_t* x_bf16, float* y, int M, int K, int N,
-                              const TcPlan& pl) {
+                              const TcPlan& pl, const float* residual) {
   switch (qtype) {
-    case RRR_Q4_K: return launch_t<RRR_Q4_K>(env, pl, w, x_bf16, y, M, K, N);
-    case RRR_Q5_K: return launch_t<RRR_Q5_K>(env, pl, w, x_bf16, y, M, K, N);
-    case RRR_Q6_K: return launch_t<RRR_Q6_K>(env, pl, w, x_bf16, y, M, K, N);
+    case RRR_Q4_K: return launch_t<RRR_Q4_K>(env, pl, w, x_bf16, y, M, K, N, residual);
+    case RRR_Q5_K: return launch_t<RRR_Q5_K>(env, pl, w, x_bf16, y, M, K, N, residual);
+    case RRR_Q6_K: return launch_t<RRR_Q6_K>(env, pl, w, x_bf16, y, M, K, N, residual);
     default: return cudaErrorNotSupported;
   }
 }

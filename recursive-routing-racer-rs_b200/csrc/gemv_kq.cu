@@ -872,11 +872,13 @@ cudaError_t launch_gemv_kq_swiglu(const LaunchEnv& env, int qtype, const void* w
 }
 
 cudaError_t launch_gemv_kq_bf16(const LaunchEnv& env, int qtype, const void* w,
-                                const uint16_t* x, float* y, int K, int N) {
+                                const uint16_t* x, float* y, int K, int N,
+                                const float* residual) {
   GemvParams p = {};
   p.w = static_cast<const uint8_t*>(w);
   p.xb = x;
   p.y = y;
+  p.residual = residual;
   p.mode = kXBf16;
   p.K = K;
   p.N = N;

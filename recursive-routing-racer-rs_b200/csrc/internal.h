@@ -23,7 +23,8 @@ cudaError_t launch_gemv_kq(const LaunchEnv& env, int qtype, const void* w, const
                            const rrr_gemv_prologue* pro);
 // GEMV with a bf16 input vector (one token of the batched path when M < 16).
 cudaError_t launch_gemv_kq_bf16(const LaunchEnv& env, int qtype, const void* w,
-                                const uint16_t* x, float* y, int K, int N);
+                                const uint16_t* x, float* y, int K, int N,
+                                const float* residual);
 cudaError_t launch_dequant_kq(const LaunchEnv& env, int qtype, const void* w, float* out,
                               int64_t n_blocks);
 cudaError_t launch_rmsnorm(const LaunchEnv& env, const float* x, const float* gamma, float* y,
@@ -64,7 +65,7 @@ struct TcPlan {
 bool plan_gemm_kq_tc(int qtype, int M, int K, int N, int sm_count, TcPlan* plan);
 cudaError_t launch_gemm_kq_tc(const LaunchEnv& env, int qtype, const void* w,
                               const uint16_t* x_bf16, float* y, int M, int K, int N,
-                              const TcPlan& plan);
+                              const TcPlan& plan, const float* residual);
 // Self-test of the integer tensor-core fragment layout used by the GEMV (writes 1 to
 // *d_ok when the device result matches the expected product).
 cudaError_t launch_mma_selftest(const LaunchEnv& env, int* d_ok);

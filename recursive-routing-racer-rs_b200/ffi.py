@@ -80,6 +80,11 @@ PROTOS = {
     "rrr_dequant_kq": (c_int, [vp, c_int, vp, vp, c_int64, vp]),
     "rrr_gemm_kq_batched": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, c_int, vp]),
     "rrr_rmsnorm": (c_int, [vp, vp, vp, vp, c_int, c_int, c_float, vp]),
+    "rrr_gemm_kq_batched_ex": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, c_int, vp, vp]),
+    "rrr_rmsnorm_bf16": (c_int, [vp, vp, vp, vp, c_int, c_int, c_float, vp]),
+    "rrr_gqa_v_bf16": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, c_int, c_int, vp]),
+    "rrr_silu_gate_bf16": (c_int, [vp, vp, vp, c_int, c_int, vp]),
+    "rrr_logits_f32_batched": (c_int, [vp, vp, vp, vp, vp, c_int, c_int, c_int, vp, c_float, vp]),
     "rrr_logits_f32": (c_int, [vp, vp, vp, vp, c_int, c_int, c_int, vp, c_float, vp]),
     "rrr_silu_gate": (c_int, [vp, vp, vp, c_int, vp]),
     "rrr_residual_add": (c_int, [vp, vp, vp, vp, c_int, vp]),
@@ -114,6 +119,7 @@ PROTOS = {
     "rrr_comm_connect": (c_int, [vp, vp]),
     "rrr_comm_allreduce_f32": (c_int, [vp, vp, c_int64, vp]),
     "rrr_comm_allgather_f32": (c_int, [vp, vp, vp, c_int64, vp]),
+    "rrr_comm_allgather_rows_f32": (c_int, [vp, vp, vp, c_int, c_int64, vp]),
     "rrr_comm_disconnect": (c_int, [vp]),
     "rrr_comm_destroy": (c_int, [vp]),
     "rrr_fill_kquant_random_2d": (c_int, [vp, c_int, vp, c_int64, c_int64, c_int64, c_int64, c_uint64, vp]),

@@ -188,9 +188,10 @@ class TPDecoder:
     shards, with torch.distributed all-reduce / all-gather (NCCL) between them. The step
     can be captured into a CUDA graph (kernels and collectives) and replayed."""
 
-    def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4TP, group=None, comm: str = "nccl"):
+    def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4TP, group=None, comm: str = "nccl",
+                 max_batch: int = 1):
         """comm: "nccl" (torch.distributed collectives) or "p2p" (rrr_comm_* kernels over
-        NVLink peer memory)."""
+        NVLink peer memory); max_batch: the largest M of forward_batched."""
         import torch
         import torch.distributed as dist
         self.torch, self.dist = torch, dist
@@ -198,7 +199,7 @@ class TPDecoder:
         self.p2p = None
         if comm == "p2p" and weights.shard.G > 1:
             self.p2p = P2PComm(ctx, weights.shard.g, weights.shard.G,
-                               max(weights.cfg.d_model, weights.shard.vocab_rows), group)
+                               max_batch * max(weights.cfg.d_model, weights.shard.vocab_rows), group)
         elif comm not in ("nccl", "p2p"):
             raise ValueError(f"unknown comm {comm!r}")
         cfg, sh = weights.cfg, weights.shard
@@ -208,6 +209,7 @@ class TPDecoder:
         self.logits_loc = torch.empty(sh.vocab_rows, device=dev)
         self.graph = None
         self._graph_key = None
+        self._bm = 0  # batch size of the batched buffers
 
     def steps(self, hidden, logits, argmax, stream=None):
         """The step as a generator: launches the kernels on `stream` (default: the current
@@ -251,24 +253,119 @@ class TPDecoder:
     def _issue(self, hidden, logits, argmax):
         """The step with its exchanges as torch.distributed collectives (NCCL) or as the
         peer-memory kernels."""
-        dist = self.dist
         st = c_void_p(self.torch.cuda.current_stream().cuda_stream)
         for op in self.steps(hidden, logits, argmax):
-            if self.p2p is not None:
-                if op[0] == "all_reduce":
-                    self.p2p.all_reduce(op[1], st)
-                else:
-                    self.p2p.all_gather(op[1], op[2], st)
-            elif op[0] == "all_reduce":
-                dist.all_reduce(op[1], group=self.group)
-            else:
-                dist.all_gather_into_tensor(op[1], op[2], group=self.group)
+            self._exchange(op, st)
 
     def close(self) -> None:
         self.release_graph()
         if self.p2p is not None:
             self.p2p.close()
             self.p2p = None
+
+    def _ensure_batch(self, M: int) -> None:
+        if self._bm >= M:
+            return
+        torch = self.torch
+        cfg, sh = self.w.cfg, self.w.shard
+        dev = torch.device("cuda", self.ctx.device)
+        self.b_xn = torch.empty(M, cfg.d_model, dtype=torch.int16, device=dev)       # bf16 bits
+        self.b_qkv = torch.empty(M, sh.qkv_dim, device=dev)
+        self.b_a = torch.empty(M, sh.o_k, dtype=torch.int16, device=dev)             # bf16 bits
+        self.b_gu = torch.empty(M, 2 * sh.ffn_dim, device=dev)
+        self.b_mid = torch.empty(M, sh.ffn_dim, dtype=torch.int16, device=dev)       # bf16 bits
+        self.b_xnorm = torch.empty(M, cfg.d_model, device=dev)
+        self.b_logits_loc = torch.empty(M, sh.vocab_rows, device=dev)
+        self._bm = M
+
+    def steps_batched(self, hidden, logits, M: int, stream=None):
+        """M tokens at position 0 (the batched-prefill call sites, phi4.rs:1198-1445, with
+        every GEMM on the tensor cores): hidden f32 [M, d] (in/out), logits f32 [M, vocab].
+        Yields at each exchange like steps(); the logits exchange is ("all_gather_rows",
+        out [M, vocab], part [M, vocab/G], M)."""
+        L, ctx, cfg, sh, w = ffi.lib(), self.ctx, self.w.cfg, self.w.shard, self.w
+        torch = self.torch
+        self._ensure_batch(M)
+        st = c_void_p(stream if stream is not None else torch.cuda.current_stream().cuda_stream)
+        d, hd = cfg.d_model, cfg.head_dim
+        hp = c_void_p(hidden.data_ptr())
+        res = hp if sh.g == 0 else None
+        nq_loc = sh.q_heads[1] - sh.q_heads[0]
+        nkv_loc = sh.kv_heads[1] - sh.kv_heads[0]
+        xn, qkv, a = c_void_p(self.b_xn.data_ptr()), c_void_p(self.b_qkv.data_ptr()), c_void_p(self.b_a.data_ptr())
+        gu, mid = c_void_p(self.b_gu.data_ptr()), c_void_p(self.b_mid.data_ptr())
+        for l, e in enumerate(w.layers):
+            ctx.check(L.rrr_rmsnorm_bf16(ctx.h, hp, c_void_p(e["attn_norm"]), xn, M, d, cfg.rms_eps, st))
+            ctx.check(L.rrr_gemm_kq_batched(ctx.h, cfg.qkv_type, c_void_p(e["qkv"]), xn, qkv, M, d,
+                                            sh.qkv_dim, st))
+            ctx.check(L.rrr_gqa_v_bf16(ctx.h, qkv, a, M, nq_loc, nkv_loc, hd, sh.o_k, sh.o_k_offset, st))
+            ctx.check(L.rrr_gemm_kq_batched_ex(ctx.h, cfg.o_type, c_void_p(e["o_proj"]), a, hp, M, sh.o_k,
+                                               d, res, st))
+            if sh.G > 1:
+                yield ("all_reduce", hidden)
+            ctx.check(L.rrr_rmsnorm_bf16(ctx.h, hp, c_void_p(e["ffn_norm"]), xn, M, d, cfg.rms_eps, st))
+            ctx.check(L.rrr_gemm_kq_batched(ctx.h, cfg.gate_up_type, c_void_p(e["gate_up"]), xn, gu, M, d,
+                                            2 * sh.ffn_dim, st))
+            ctx.check(L.rrr_silu_gate_bf16(ctx.h, gu, mid, M, sh.ffn_dim, st))
+            ctx.check(L.rrr_gemm_kq_batched_ex(ctx.h, cfg.down_type, c_void_p(e["down"]), mid, hp, M,
+                                               sh.ffn_dim, d, res, st))
+            if sh.G > 1:
+                yield ("all_reduce", hidden)
+        lp = self.b_logits_loc if sh.G > 1 else logits
+        ctx.check(L.rrr_logits_f32_batched(ctx.h, c_void_p(w.w_out), hp, c_void_p(self.b_xnorm.data_ptr()),
+                                           c_void_p(lp.data_ptr()), M, sh.vocab_rows, d,
+                                           c_void_p(w.output_norm), cfg.rms_eps, st))
+        if sh.G > 1:
+            yield ("all_gather_rows", logits, self.b_logits_loc, M)
+
+    def _exchange(self, op, st) -> None:
+        dist = self.dist
+        if self.p2p is not None:
+            if op[0] == "all_reduce":
+                self.p2p.all_reduce(op[1], st)
+            elif op[0] == "all_gather":
+                self.p2p.all_gather(op[1], op[2], st)
+            else:
+                self.ctx.check(ffi.lib().rrr_comm_allgather_rows_f32(
+                    self.p2p.h, c_void_p(op[1].data_ptr()), c_void_p(op[2].data_ptr()), op[3],
+                    op[2].numel() // op[3], st))
+        elif op[0] == "all_reduce":
+            dist.all_reduce(op[1], group=self.group)
+        elif op[0] == "all_gather":
+            dist.all_gather_into_tensor(op[1], op[2], group=self.group)
+        else:
+            G, M = self.w.shard.G, op[3]
+            tmp = self.torch.empty(G * op[2].numel(), device=op[2].device)
+            dist.all_gather_into_tensor(tmp, op[2].reshape(-1), group=self.group)
+            op[1].view(M, G, -1).copy_(tmp.view(G, M, -1).permute(1, 0, 2))
+
+    def forward_batched(self, hidden, logits, M: int, use_graph: bool = False) -> None:
+        """One batched step of M tokens on the current stream (see steps_batched); with
+        use_graph the step is captured on the first call for these tensors and M."""
+        torch = self.torch
+        if not use_graph:
+            st = c_void_p(torch.cuda.current_stream().cuda_stream)
+            for op in self.steps_batched(hidden, logits, M):
+                self._exchange(op, st)
+            return
+        key = ("b", hidden.data_ptr(), logits.data_ptr(), M)
+        if self.graph is None or self._graph_key != key:
+            self.release_graph()
+            saved = hidden.clone()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for op in self.steps_batched(hidden, logits, M):
+                    self._exchange(op, c_void_p(s.cuda_stream))
+            torch.cuda.current_stream().wait_stream(s)
+            hidden.copy_(saved)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="relaxed"):
+                st = c_void_p(torch.cuda.current_stream().cuda_stream)
+                for op in self.steps_batched(hidden, logits, M):
+                    self._exchange(op, st)
+            self.graph, self._graph_key = g, key
+        self.graph.replay()
 
     def launches_per_step(self) -> int:
         """Kernels of this library per step (NCCL collectives not counted; the peer-memory
@@ -313,13 +410,17 @@ class TPDecoder:
             self._graph_key = None
 
 
-def emulate_step(decoders, hiddens, logits_list, argmaxes=None) -> None:
+def emulate_step(decoders, hiddens, logits_list, argmaxes=None, batch: int = 0) -> None:
     """Runs the ranks' steps of one process (all shards on the current device) in lockstep,
     doing each exchange with torch ops: the sum of the ranks' tensors for an all-reduce,
-    the concatenation for an all-gather. For checking the split on one GPU."""
+    the concatenation for an all-gather. batch > 0: the batched step of that many tokens.
+    For checking the split on one GPU."""
     import torch
-    gens = [dec.steps(h, lg, None if argmaxes is None else argmaxes[i])
-            for i, (dec, h, lg) in enumerate(zip(decoders, hiddens, logits_list))]
+    if batch:
+        gens = [dec.steps_batched(h, lg, batch) for dec, h, lg in zip(decoders, hiddens, logits_list)]
+    else:
+        gens = [dec.steps(h, lg, None if argmaxes is None else argmaxes[i])
+                for i, (dec, h, lg) in enumerate(zip(decoders, hiddens, logits_list))]
     while True:
         ops = []
         for gi in gens:
@@ -335,7 +436,12 @@ def emulate_step(decoders, hiddens, logits_list, argmaxes=None) -> None:
             total = torch.stack([o[1] for o in ops]).sum(0)
             for o in ops:
                 o[1].copy_(total)
-        else:
+        elif ops[0][0] == "all_gather":
             full = torch.cat([o[2] for o in ops])
             for o in ops:
                 o[1].copy_(full)
+        else:
+            M = ops[0][3]
+            full = torch.cat([o[2].reshape(M, -1) for o in ops], dim=1)
+            for o in ops:
+                o[1].view(M, -1).copy_(full)

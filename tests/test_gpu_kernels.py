@@ -422,6 +422,32 @@ def test_gemm_tc_repeat_deterministic(rrr, ctx, oracle, G, qt):
         assert np.array_equal(o, outs[0])
 
 
+@pytest.mark.parametrize("qt", QTYPES)
+@pytest.mark.parametrize("M,K,N,inplace", [(16, 1024, 768, True), (40, 1024, 768, True),
+                                            (40, 768, 2048, False), (3, 512, 256, True),
+                                            (300, 512, 256, True)])
+def test_gemm_tc_residual(rrr, ctx, oracle, G, qt, M, K, N, inplace):
+    """rrr_gemm_kq_batched_ex: Y = X W^T + R with R == Y (in place) or separate, on the
+    split-K cluster path, the single-split path and the per-token path (M < 16)."""
+    import torch
+    rng = np.random.default_rng(M + K + N + qt)
+    raw = oracle.random_blocks(qt, N * (K // 256), rng)
+    X = torch.randn(M, K, dtype=torch.bfloat16)
+    R = torch.randn(M, N) * 10
+    W = oracle.dequant(qt, raw, N * K).reshape(N, K).astype(np.float64)
+    ref = (X.float().numpy().astype(np.float64) @ W.T + R.numpy()).astype(np.float32)
+    wd, xd = G.dev(raw), X.cuda()
+    Y = R.clone().cuda()
+    Rd = Y if inplace else R.clone().cuda()
+    if not inplace:
+        Y = torch.full((M, N), float("nan"), device="cuda")
+    ctx.check(rrr.ffi.lib().rrr_gemm_kq_batched_ex(ctx.h, qt, vp(wd), vp(xd), vp(Y), M, K, N, vp(Rd), None))
+    got = G.host(Y).reshape(M, N)
+    assert ctx.device_error() == 0
+    for m in range(M):
+        assert rel_l2(got[m], ref[m]) < 1e-2, (m, rel_l2(got[m], ref[m]))
+
+
 def test_decode_step_small(rrr, ctx, oracle, G):
     """A small Phi-4-shaped model (numpy weights): eager and graph decode steps against
     the oracle's position-0 decode step."""
