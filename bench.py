@@ -319,6 +319,30 @@ def run_ours(args, rank, world, local_rank):
               "frac_of_peak": round(dec_bytes / dms / 1e6 / peak, 4),
               "launches_per_token": dec.launches_per_step() + 1, "graph": True}
     dec.close()
+    # ---------------- batched decode step, 64 tokens at position 0 (configs[4] batch 64 on
+    # one GPU / one rank's replica): tcgen05 GEMMs for every layer GEMM, batched logits
+    tpm = importlib.import_module("recursive-routing-racer-rs_b200.tp")
+    BM = 64
+    bw = tpm.SyntheticPhi4TP(ctx, cfg, tpm.plan(cfg, 1, 0), seed=9, stream=sp)
+    bdec = tpm.TPDecoder(ctx, bw, max_batch=BM)
+    bh = torch.randn(BM, cfg.d_model, device="cuda")
+    blg = torch.empty(BM, cfg.vocab_size, device="cuda")
+    for _ in range(max(3, args.warmup)):
+        bdec.forward_batched(bh, blg, BM, use_graph=True)
+    barrier()
+    b0e, b1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    bsteps = max(5, args.steps // 2)
+    b0e.record(stream)
+    for _ in range(bsteps):
+        bdec.forward_batched(bh, blg, BM, use_graph=True)
+    b1e.record(stream)
+    barrier()
+    bms = max_over_ranks(b0e.elapsed_time(b1e) / bsteps)
+    decode_batch = {"batch": BM, "tok_s": round(BM * 1e3 / bms, 1), "ms_per_step": round(bms, 4),
+                    "graph": True, "path": "per layer: rmsnorm->bf16, 4 tcgen05 GEMMs (residual in "
+                                           "the epilogue), GQA-V / SiLU glue; logits f32 SGEMM"}
+    bdec.close()
+    bw.close()
     # ---------------- tensor-parallel decode step (configs[4], batch 1) over all ranks
     tp_decode = None
     if world > 1:
@@ -347,10 +371,26 @@ def run_ours(args, rank, world, local_rank):
 
         tms, tl_p2p = time_tp("p2p")
         tms_nccl, _ = time_tp("nccl")
+        # batch 64 over the ranks (peer-memory exchanges of [64, 3072] and [64, V/G])
+        tb = tpm.TPDecoder(ctx, tw, comm="p2p", max_batch=BM)
+        tbh = torch.randn(BM, cfg.d_model, device="cuda")
+        tblg = torch.empty(BM, cfg.vocab_size, device="cuda")
+        for _ in range(max(3, args.warmup)):
+            tb.forward_batched(tbh, tblg, BM, use_graph=True)
+        barrier()
+        t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0e.record(stream)
+        for _ in range(bsteps):
+            tb.forward_batched(tbh, tblg, BM, use_graph=True)
+        t1e.record(stream)
+        barrier()
+        tbms = max_over_ranks(t0e.elapsed_time(t1e) / bsteps)
+        tb.close()
         tp_decode = {"tok_s": round(1e3 / tms, 2), "ms_per_token": round(tms, 4), "n_gpus": world,
                      "exchange": "rrr_comm peer-memory kernels over NVLink (all-reduce x2 per layer "
                                  "+ logits all-gather)",
                      "tok_s_nccl": round(1e3 / tms_nccl, 2),
+                     "batch64_tok_s": round(BM * 1e3 / tbms, 1), "batch64_ms_per_step": round(tbms, 4),
                      "bytes_per_rank": tw.shard_bytes(),
                      "GBps_per_rank": round(tw.shard_bytes() / tms / 1e6, 1),
                      "exchanges_per_token": 2 * cfg.n_layers + 1,
@@ -409,6 +449,7 @@ def run_ours(args, rank, world, local_rank):
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one gate_up "
                                            "launch (profiles/gemv_kq_phi4_layer_shapes.md)"},
             "decode": decode,
+            "decode_batch64": decode_batch,
             "tp_decode": tp_decode,
             "batched_gemm": {"note": "configs[3]: rrr_gemm_kq_batched (tcgen05, bf16 x bf16 -> f32); "
                                      "tensor_frac against the measured dense bf16 burst peak",
