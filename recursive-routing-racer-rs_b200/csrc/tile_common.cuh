@@ -1,0 +1,175 @@
+// tile_common.cuh — pieces shared by the batched-token GEMM kernels (gemm_kq_tc.cu on the
+// tcgen05 tensor cores, gemm_kq_mma.cu on register-level mma.sync): TMA tile loads, the
+// 128-byte swizzle, cluster barriers and distributed shared memory, warp-uniform bounded
+// waits, the packed exact-offset dequantisation of K-quant runs to bf16, and the host-side
+// tensor-map encoding and raw-stage pitch. Only sm_100a is targeted.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kquant.cuh"
+#include "rrr_common.cuh"
+
+namespace rrr {
+
+// Device error code of a tile kernel's bounded wait (kDevErr* of rrr_common.cuh are 1..3).
+constexpr int kDevErrTileWait = 4;
+
+// Generic-proxy shared-memory writes become visible to the async proxy (tensor core).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 2-D TMA tile load (plain, no multicast) of box {64, TN} at (c0 = k, c1 = token).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Barrier over every thread of every CTA of the cluster (release / acquire).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+// 16-byte load from the shared memory of cluster CTA `rank` at this CTA's shared address.
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local_addr, uint32_t rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(local_addr), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(ra)
+               : "memory");
+  return v;
+}
+
+// Byte offset of 16-byte chunk c (0..7) of row r inside a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Bounded wait by every lane of a warp; the warp agrees on the outcome.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          int code = kDevErrTileWait) {
+  const bool ok = mbar_wait_bounded(bar, parity, err, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// The CTA's abort flag as one value for the whole warp (warp-collective code below must
+// not diverge on it).
+__device__ __forceinline__ bool warp_aborted(volatile int* flag) {
+  return __any_sync(0xffffffffu, *flag != 0);
+}
+
+// Scale pair of one run of weights v*a - b (v a small integer) in the form the packed
+// FMA uses: the integer is placed in bits 16-22 of an f32 with exponent 23, which is the
+// exact value f = 2^23 + 65536 v; then f * (a / 65536) + c with c = -(128 a + b) equals
+// v*a - b up to one rounding of the FMA and the rounding of c (about 2^-17 a).
+struct RunScale {
+  float2 a, c;
+};
+__device__ __forceinline__ RunScale run_scale(float a, float b) {
+  const float ap = a * (1.0f / 65536.0f);
+  const float c = -fmaf(128.f, a, b);
+  return {make_float2(ap, ap), make_float2(c, c)};
+}
+
+// Four values (bytes of w, each < 128) -> two bf16x2 words (round to nearest).
+__device__ __forceinline__ void emit4(uint32_t w, const RunScale& sc, uint32_t* o) {
+  const float2 f01 = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7044)),
+                                 __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7144)));
+  const float2 f23 = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7244)),
+                                 __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7344)));
+  const __nv_bfloat162 b01 = __float22bfloat162_rn(__ffma2_rn(f01, sc.a, sc.c));
+  const __nv_bfloat162 b23 = __float22bfloat162_rn(__ffma2_rn(f23, sc.a, sc.c));
+  o[0] = *reinterpret_cast<const uint32_t*>(&b01);
+  o[1] = *reinterpret_cast<const uint32_t*>(&b23);
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
+
+// 6-bit scale / min of sub-block s from the 12 scale bytes held as words s0 (bytes 0-3),
+// s1 (4-7), s2 (8-11) (phi4.rs:492-498).
+__device__ __forceinline__ void scale_min_w(uint32_t s0, uint32_t s1, uint32_t s2, int s,
+                                            float& sv, float& mv) {
+  uint32_t a, b;
+  if (s < 4) {
+    a = byte_of(s0, s) & 63u;
+    b = byte_of(s1, s) & 63u;
+  } else {
+    const int i = s - 4;
+    a = (byte_of(s2, i) & 15u) | ((byte_of(s0, i) >> 6) << 4);
+    b = (byte_of(s2, i) >> 4) | ((byte_of(s1, i) >> 6) << 4);
+  }
+  sv = (float)a;
+  mv = (float)b;
+}
+
+// 16 bytes at a 2-byte-aligned shared address, via aligned 32-bit loads and funnel shifts.
+__device__ __forceinline__ void ld16_a2(const uint8_t* p, uint32_t* o) {
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~(uintptr_t)3);
+  const uint32_t sh = (uint32_t)(reinterpret_cast<uintptr_t>(p) & 3) * 8;
+  uint32_t w[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) w[i] = q[i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = __funnelshift_r(w[i], w[i + 1], sh);
+}
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// Row pitch of a raw stage of `kbs` super-blocks: the blocks plus room for the 16-byte
+// envelope of a block run that does not start 16-byte aligned (Q6_K), rounded to an odd
+// number of 16-byte units so that 8 consecutive rows read 16-byte words from distinct
+// bank groups.
+inline int raw_slot_bytes(int qtype, int kbs) {
+  const int bytes = kq_block_bytes(qtype) * kbs + (qtype == RRR_Q6_K ? 14 : 0);
+  int units = (bytes + 15) / 16;
+  if ((units & 1) == 0) ++units;
+  return units * 16;
+}
+
+inline int next_pow2_cols(int tn) {
+  int c = 32;
+  while (c < tn) c <<= 1;
+  return c;
+}
+
+// Tensor map of a 2-D row-major array: `inner` elements of `elem_bytes` per row (row
+// pitch `pitch_bytes`, a multiple of 16), `rows` rows; box = box_inner x box_rows.
+inline bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+               uint64_t rows, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_rows,
+               CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)pitch_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+
+}  // namespace rrr
