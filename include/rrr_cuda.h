@@ -75,8 +75,14 @@ int rrr_d2d(rrr_ctx* ctx, void* dst_dev, const void* src_dev, size_t bytes, void
 int rrr_memset(rrr_ctx* ctx, void* dst_dev, int value, size_t bytes, void* stream);
 int rrr_sync(rrr_ctx* ctx, void* stream);
 /* Reads and clears the context's device error flag, which kernels set when a bounded
- * wait gives up. Synchronises the device. *code = 0 if no kernel reported an error. */
+ * wait gives up (codes 1-5: RRR_ERR_TIMEOUT) or meet a position outside the KV cache /
+ * a token id outside the embedding table (code 6: RRR_ERR_BAD_SHAPE). Synchronises the
+ * device. *code = 0 if no kernel reported an error. */
 int rrr_check_device_error(rrr_ctx* ctx, int* code);
+/* Programmatic dependent launch (default on): each kernel of the library may start while
+ * the previous kernel on its stream finishes (weights stream early; inputs are read after
+ * the grid dependency wait). enable = 0 serialises every launch (a debugging aid). */
+int rrr_set_pdl(rrr_ctx* ctx, int enable);
 /* Number of streaming multiprocessors of the context's device. */
 int rrr_device_sm_count(rrr_ctx* ctx, int* sms);
 /* Diagnostic: runs the integer tensor-core fragment-layout check the GEMV relies on
@@ -260,10 +266,55 @@ int rrr_gguf_data_offset(rrr_gguf* g, uint64_t* off);
 int rrr_gguf_upload(rrr_ctx* ctx, rrr_gguf* g, const char* name, void** dptr,
                     uint64_t* n_bytes);
 
+/* ---- decode attention at real positions (per-layer glue between the QKV and the
+ *      O-projection GEMVs of forward_gpu / forward_dynamic: phi4.rs:1115-1121,
+ *      1284-1309, 1656-1690) ------------------------------------------------------
+ * RoPE as apply_rope_cfg (phi4.rs:238-256), the f16 KV cache of max_seq rows per layer
+ * (MAX_SEQ = 2048, phi4.rs:181, 897-904) and GQA decode attention. */
+typedef struct rrr_attn_desc {
+  int n_heads, n_kv_heads, head_dim;  /* head_dim 64/128/256; n_heads / n_kv_heads <= 8 */
+  int rope_dim;                       /* rotated values per head: even, <= head_dim, <= 128 */
+  float rope_theta;                   /* rope.freq_base (10000 for Phi-4-mini) */
+  float rope_attn_factor;             /* rope.scaling.attn_factor (1.190238; 1 = standard) */
+  const float* rope_factors;          /* device f32[n_rope_factors] (rope_factors_short) or NULL */
+  int n_rope_factors;                 /* pair i uses factor i, 1 past the table */
+  int max_seq;                        /* rows of each cache */
+} rrr_attn_desc;
+/* Row t of qkv (f32 [rows][row_stride]: Q | K | V of n_q + 2 n_kv heads) is the token at
+ * position p + t, p = *d_pos (a device int read when the kernel runs, so that a captured
+ * step replays at any position) or pos0 when d_pos is NULL. RoPE on its Q and K heads in
+ * place (pair (2i, 2i+1), i < rope_dim/2, same operations as apply_rope_cfg); K and V
+ * rounded to f16 (nearest even) into row p + t of k_cache / v_cache (f16
+ * [max_seq][n_kv*head_dim], 16-byte aligned). Positions outside [0, max_seq): rejected
+ * (pos0) or recorded in the device error flag with nothing written (d_pos). */
+int rrr_rope_kv_store(rrr_ctx* ctx, const rrr_attn_desc* a, float* qkv, int64_t row_stride,
+                      int rows, int pos0, const int* d_pos, uint16_t* k_cache,
+                      uint16_t* v_cache, void* stream);
+/* out[t][h*hd + e] = sum over s in [0, p + t] of softmax_s(q[t]_h . k[s]_g / sqrt(hd)) *
+ * v[s]_g[e], g = h / (n_q / n_kv) (causal: row t sees the rows stored up to its own
+ * position). q: rows of q_stride floats whose first n_q*hd values are the query heads
+ * (the Q part of QKV rows: q = qkv, q_stride = the QKV row stride). out f32 [rows][n_q*hd]. */
+int rrr_attention_f16kv(rrr_ctx* ctx, const rrr_attn_desc* a, const float* q, int64_t q_stride,
+                        int rows, int pos0, const int* d_pos, const uint16_t* k_cache,
+                        const uint16_t* v_cache, float* out, void* stream);
+/* Embedding rows (Phi4Model::embed on the table dequantised by dequant_tensor_f32,
+ * phi4.rs:709, 572-587, 2085-2089): out[t] = row tokens[t] of an [n_rows, d] table stored
+ * as GGUF type ggml_type (0 F32, 1 F16, 6 Q5_0, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K; d a
+ * multiple of the type's block), dequantised bit-exactly on the fly. tokens: device
+ * int32[n_tokens]; an id outside [0, n_rows) gives a zero row and sets the device error
+ * flag (the reference panics on the slice). */
+int rrr_embed_rows(rrr_ctx* ctx, int ggml_type, const void* table, int64_t n_rows, int d,
+                   const int32_t* tokens, int n_tokens, float* out, void* stream);
+
 /* ---- Phi-4-mini-shape decode step (replaces forward_gpu, phi4.rs:1099-1196) --------
- * One token at position 0 (attention output = V, see RRR_X_GQA_V): per layer
+ * max_seq == 0: one token at position 0 (attention output = V, see RRR_X_GQA_V): per layer
  *   h += Wo . expand(V(Wqkv . rms(h)*g_attn)); h += Wdown . (silu(g) * u),
  *   [g; u] = Wgate_up . rms(h)*g_ffn; then logits = Wout . rms(h)*g_out.
+ * max_seq > 0: one token at the model's current position p (forward_dynamic,
+ * phi4.rs:1593-1760): after the QKV GEMV, RoPE + the f16 KV store at row p
+ * (rrr_rope_kv_store) and attention over rows 0..p (rrr_attention_f16kv) give the
+ * O-projection's input; the model owns the caches (2 x n_layers x max_seq x n_kv*hd f16)
+ * and a device position that starts at 0 and advances by one per forward.
  * All pointers are device pointers that the caller owns and keeps alive. */
 typedef struct rrr_phi4_layer {
   const void* w_qkv;      int qkv_type;      /* [n_q*hd + 2*n_kv*hd, d] */
@@ -280,6 +331,11 @@ typedef struct rrr_phi4_desc {
   const rrr_phi4_layer* layers; /* n_layers entries (copied) */
   const float* output_norm;     /* f32[d] */
   const float* w_out;           /* f32 [vocab, d] row-major */
+  int max_seq;                  /* 0: position-0 step; > 0: KV-cache decode */
+  int rope_dim;                 /* KV-cache decode: RoPE of rrr_attn_desc */
+  float rope_theta, rope_attn_factor;
+  const float* rope_factors;    /* device f32[n_rope_factors] or NULL */
+  int n_rope_factors;
 } rrr_phi4_desc;
 typedef struct rrr_phi4 rrr_phi4;
 int rrr_phi4_create(rrr_ctx* ctx, const rrr_phi4_desc* desc, rrr_phi4** out);
@@ -290,6 +346,13 @@ int rrr_phi4_forward(rrr_phi4* m, float* hidden, float* logits, int* argmax_out,
                      int use_graph, void* stream);
 /* Number of kernel launches one forward issues. */
 int rrr_phi4_launches_per_step(rrr_phi4* m, int* n);
+/* KV-cache decode: the position of the next forward (the KVCache.len of the reference;
+ * 0 after create). set_position moves it (0 <= pos < max_seq; cache rows >= pos are
+ * overwritten as decoding proceeds); position reads the host-side copy. */
+int rrr_phi4_set_position(rrr_phi4* m, int pos, void* stream);
+int rrr_phi4_position(rrr_phi4* m, int* pos);
+/* KV-cache decode: the device caches of one layer (f16 [max_seq][n_kv*hd]). */
+int rrr_phi4_kv_cache(rrr_phi4* m, int layer, uint16_t** k_cache, uint16_t** v_cache);
 int rrr_phi4_destroy(rrr_phi4* m);
 
 /* ---- exchanges between the GPUs of one box (tensor-parallel decode step) ------------

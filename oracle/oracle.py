@@ -213,6 +213,84 @@ def decode_step(cfg: dict, layers: list, output_norm: np.ndarray, w_out: np.ndar
     return h, logits
 
 
+def rope(x: np.ndarray, pos: int, n_heads: int, head_dim: int, rope_dim: int, theta: float,
+         attn_factor: float, factors=None) -> np.ndarray:
+    """apply_rope_cfg (phi4.rs:238-256) on a copy of x (f32[n_heads*head_dim])."""
+    y = np.array(x, dtype=np.float32, copy=True)
+    f = np.ascontiguousarray(factors if factors is not None else np.zeros(0), np.float32)
+    L = lib()
+    L.rrro_rope.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                            ctypes.c_float, ctypes.c_float, ctypes.c_void_p, ctypes.c_int]
+    L.rrro_rope(y.ctypes.data, pos, n_heads, head_dim, rope_dim, theta, attn_factor,
+                f.ctypes.data, len(f))
+    return y
+
+
+def f32_to_f16_bits(a: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f16 bit patterns (the KV-cache store)."""
+    return np.asarray(a, np.float32).astype(np.float16).view(np.uint16)
+
+
+def attention_f16kv(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, seq_len: int,
+                    n_heads: int, n_kv_heads: int, head_dim: int) -> np.ndarray:
+    """Decode attention over rows 0..seq_len-1 of the f16 caches (uint16 bit patterns,
+    [rows, n_kv_heads*head_dim])."""
+    qq = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(k_cache, np.uint16)
+    vc = np.ascontiguousarray(v_cache, np.uint16)
+    out = np.empty(n_heads * head_dim, np.float32)
+    L = lib()
+    L.rrro_attention_f16kv.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4
+    L.rrro_attention_f16kv(qq.ctypes.data, kc.ctypes.data, vc.ctypes.data, out.ctypes.data,
+                           seq_len, n_heads, n_kv_heads, head_dim)
+    return out
+
+
+def decode_step_kv(cfg: dict, layers: list, output_norm: np.ndarray, w_out: np.ndarray,
+                   hidden: np.ndarray, pos: int, k_caches: np.ndarray, v_caches: np.ndarray,
+                   rope_dim: int, theta: float, attn_factor: float, factors=None,
+                   threads: int = 1):
+    """Decode step at position `pos` with RoPE and f16 KV caches (forward_dynamic,
+    phi4.rs:1593-1760). k_caches / v_caches: uint16 [n_layers, max_seq, n_kv*hd], updated
+    in place. Returns (hidden_out, logits)."""
+    arr = (_Layer * len(layers))()
+    keep = []
+    for i, Ly in enumerate(layers):
+        for k in ("w_qkv", "w_o", "w_gate_up", "w_down"):
+            a = np.ascontiguousarray(Ly[k], np.uint8)
+            keep.append(a)
+            setattr(arr[i], k, a.ctypes.data)
+        for k in ("attn_norm", "ffn_norm"):
+            a = np.ascontiguousarray(Ly[k], np.float32)
+            keep.append(a)
+            setattr(arr[i], k, a.ctypes.data)
+        for k in ("qkv_type", "o_type", "gate_up_type", "down_type"):
+            setattr(arr[i], k, int(Ly[k]))
+    assert k_caches.dtype == np.uint16 and k_caches.flags.c_contiguous
+    assert v_caches.dtype == np.uint16 and v_caches.flags.c_contiguous
+    on = np.ascontiguousarray(output_norm, np.float32)
+    wo = np.ascontiguousarray(w_out, np.float32)
+    f = np.ascontiguousarray(factors if factors is not None else np.zeros(0), np.float32)
+    h = np.array(hidden, dtype=np.float32, copy=True)
+    logits = np.empty(cfg["vocab"], np.float32)
+    L = lib()
+    L.rrro_decode_step_kv.argtypes = ([ctypes.c_int] * 7 + [ctypes.c_float, ctypes.c_int,
+                                      ctypes.c_float, ctypes.c_float, ctypes.c_void_p,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                      ctypes.c_void_p, ctypes.POINTER(_Layer)]
+                                      + [ctypes.c_void_p] * 4 + [ctypes.c_int])
+    L.rrro_decode_step_kv.restype = ctypes.c_int
+    rc = L.rrro_decode_step_kv(cfg["d_model"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
+                               cfg["ffn_dim"], cfg["n_layers"], cfg["vocab"], cfg.get("eps", 1e-5),
+                               rope_dim, theta, attn_factor, f.ctypes.data, len(f), pos,
+                               k_caches.shape[1], k_caches.ctypes.data, v_caches.ctypes.data, arr,
+                               on.ctypes.data, wo.ctypes.data, h.ctypes.data, logits.ctypes.data,
+                               threads)
+    if rc != 0:
+        raise ValueError("bad decode_step_kv config")
+    return h, logits
+
+
 # ---------------------------------------------------------------- synthetic data (numpy)
 def _f16_bits_uniform(rng: np.random.Generator, n: int, lo=1e-4, hi=1e-2) -> np.ndarray:
     return rng.uniform(lo, hi, n).astype(np.float32).astype(np.float16).view(np.uint16)

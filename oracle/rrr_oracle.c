@@ -439,3 +439,102 @@ int rrro_decode_step(int d, int nh, int nkv, int hd, int ffn, int nl, int vocab,
   free(normed); free(qkv); free(attn); free(tmp); free(gu); free(mid);
   return 0;
 }
+
+/* ---------------------------------------------------------------- RoPE / KV / attention */
+void rrro_rope(float* x, int pos, int n_heads, int head_dim, int rope_dim, float theta,
+               float attn_factor, const float* factors, int n_factors) {
+  for (int h = 0; h < n_heads; ++h) {
+    const int base = h * head_dim;
+    for (int i = 0; i < rope_dim / 2; ++i) {
+      const float base_freq = 1.0f / powf(theta, (2.0f * (float)i) / (float)rope_dim);
+      const float factor = i < n_factors ? factors[i] : 1.0f;
+      const float freq = base_freq / factor;
+      const float angle = (float)pos * freq;
+      const float sin_t = sinf(angle), cos_t = cosf(angle);
+      const float cs = cos_t * attn_factor, ss = sin_t * attn_factor;
+      const float x0 = x[base + 2 * i], x1 = x[base + 2 * i + 1];
+      x[base + 2 * i] = x0 * cs - x1 * ss;
+      x[base + 2 * i + 1] = x0 * ss + x1 * cs;
+    }
+  }
+}
+
+void rrro_kv_store(const float* k, const float* v, uint16_t* k_cache, uint16_t* v_cache,
+                   int pos, int kv_stride) {
+  for (int i = 0; i < kv_stride; ++i) {
+    k_cache[(size_t)pos * kv_stride + i] = rrro_f32_to_f16_rne(k[i]);
+    v_cache[(size_t)pos * kv_stride + i] = rrro_f32_to_f16_rne(v[i]);
+  }
+}
+
+void rrro_attention_f16kv(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                          float* out, int seq_len, int n_heads, int n_kv_heads, int head_dim) {
+  const int hpk = n_heads / n_kv_heads, kv_stride = n_kv_heads * head_dim;
+  double* s = (double*)malloc(sizeof(double) * (size_t)(seq_len > 0 ? seq_len : 1));
+  double* acc = (double*)malloc(sizeof(double) * (size_t)head_dim);
+  const double scale = 1.0 / sqrt((double)head_dim);
+  for (int h = 0; h < n_heads; ++h) {
+    const int g = h / hpk;
+    const float* qh = q + (size_t)h * head_dim;
+    double m = -INFINITY;
+    for (int t = 0; t < seq_len; ++t) {
+      const uint16_t* kr = k_cache + (size_t)t * kv_stride + (size_t)g * head_dim;
+      double dot = 0.0;
+      for (int e = 0; e < head_dim; ++e) dot += (double)qh[e] * (double)rrro_f16_to_f32(kr[e]);
+      s[t] = dot * scale;
+      if (s[t] > m) m = s[t];
+    }
+    double l = 0.0;
+    for (int e = 0; e < head_dim; ++e) acc[e] = 0.0;
+    for (int t = 0; t < seq_len; ++t) {
+      const double p = exp(s[t] - m);
+      l += p;
+      const uint16_t* vr = v_cache + (size_t)t * kv_stride + (size_t)g * head_dim;
+      for (int e = 0; e < head_dim; ++e) acc[e] += p * (double)rrro_f16_to_f32(vr[e]);
+    }
+    for (int e = 0; e < head_dim; ++e) out[(size_t)h * head_dim + e] = (float)(acc[e] / l);
+  }
+  free(s);
+  free(acc);
+}
+
+int rrro_decode_step_kv(int d, int nh, int nkv, int hd, int ffn, int nl, int vocab, float eps,
+                        int rope_dim, float theta, float attn_factor, const float* factors,
+                        int n_factors, int pos, int max_seq, uint16_t* k_caches,
+                        uint16_t* v_caches, const rrro_layer* L, const float* out_norm,
+                        const float* w_out, float* h, float* logits, int threads) {
+  if (d <= 0 || nh <= 0 || nkv <= 0 || nh % nkv || hd <= 0 || nh * hd != d || pos < 0 ||
+      pos >= max_seq || rope_dim < 0 || rope_dim > hd || rope_dim % 2)
+    return -1;
+  const int qkv_dim = nh * hd + 2 * nkv * hd, kv_stride = nkv * hd;
+  float* normed = (float*)malloc(sizeof(float) * (size_t)d);
+  float* qkv = (float*)malloc(sizeof(float) * (size_t)qkv_dim);
+  float* attn = (float*)malloc(sizeof(float) * (size_t)d);
+  float* tmp = (float*)malloc(sizeof(float) * (size_t)d);
+  float* gu = (float*)malloc(sizeof(float) * (size_t)2 * ffn);
+  float* mid = (float*)malloc(sizeof(float) * (size_t)ffn);
+  for (int l = 0; l < nl; ++l) {
+    uint16_t* kc = k_caches + (size_t)l * max_seq * kv_stride;
+    uint16_t* vc = v_caches + (size_t)l * max_seq * kv_stride;
+    rrro_rms_norm(h, L[l].attn_norm, normed, d, eps);
+    rrro_gemv_kq(L[l].qkv_type, L[l].w_qkv, normed, qkv, d, qkv_dim, threads);
+    float* q = qkv;
+    float* k = qkv + nh * hd;
+    float* v = k + kv_stride;
+    rrro_rope(q, pos, nh, hd, rope_dim, theta, attn_factor, factors, n_factors);
+    rrro_rope(k, pos, nkv, hd, rope_dim, theta, attn_factor, factors, n_factors);
+    rrro_kv_store(k, v, kc, vc, pos, kv_stride);
+    rrro_attention_f16kv(q, kc, vc, attn, pos + 1, nh, nkv, hd);
+    rrro_gemv_kq(L[l].o_type, L[l].w_o, attn, tmp, d, d, threads);
+    rrro_add(h, tmp, h, d);
+    rrro_rms_norm(h, L[l].ffn_norm, normed, d, eps);
+    rrro_gemv_kq(L[l].gate_up_type, L[l].w_gate_up, normed, gu, d, 2 * ffn, threads);
+    rrro_silu_gate(gu, mid, ffn);
+    rrro_gemv_kq(L[l].down_type, L[l].w_down, mid, tmp, ffn, d, threads);
+    rrro_add(h, tmp, h, d);
+  }
+  rrro_rms_norm(h, out_norm, normed, d, eps);
+  rrro_gemv_f32(w_out, normed, logits, vocab, d, threads);
+  free(normed); free(qkv); free(attn); free(tmp); free(gu); free(mid);
+  return 0;
+}

@@ -76,6 +76,36 @@ int rrro_decode_step(int d_model, int n_heads, int n_kv_heads, int head_dim, int
                      const float* output_norm, const float* w_out, float* hidden,
                      float* logits, int threads);
 
+/* RoPE exactly as apply_rope_cfg (phi4.rs:238-256): for each of n_heads heads of
+ * head_dim values and i < rope_dim/2: base = 1 / theta^((2i)/rope_dim) (f32 powf),
+ * freq = base / factor_i (factor 1 past the table), angle = pos * freq, (sin, cos) of the
+ * angle times attn_factor, then (x0, x1) = (x0 c - x1 s, x0 s + x1 c) on the pair
+ * (2i, 2i+1). In place. */
+void rrro_rope(float* x, int pos, int n_heads, int head_dim, int rope_dim, float theta,
+               float attn_factor, const float* factors, int n_factors);
+/* The f16 KV store of the `kv_store` dispatch (phi4.rs:1660-1677): row `pos` of the
+ * caches (kv_stride f16 per row) = k, v rounded to nearest even. */
+void rrro_kv_store(const float* k, const float* v, uint16_t* k_cache, uint16_t* v_cache,
+                   int pos, int kv_stride);
+/* Decode attention of the `attention` dispatch (push [seq_len, n_kv, heads_per_kv,
+ * head_dim], phi4.rs:1680-1688). The shader is not part of the reference (un-vendored
+ * torch-vulkan), so this is the standard definition it implements: query head h uses KV
+ * head h / (n_heads / n_kv_heads); scores q.k / sqrt(head_dim) over positions
+ * 0..seq_len-1 of the f16 caches, softmax (max subtracted), weighted sum of V. Dot
+ * products and sums in double. out f32[n_heads*head_dim]. */
+void rrro_attention_f16kv(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                          float* out, int seq_len, int n_heads, int n_kv_heads, int head_dim);
+/* Decode step at position `pos` with RoPE and the f16 KV caches (forward_dynamic,
+ * phi4.rs:1593-1760): per layer rms -> QKV -> RoPE(Q), RoPE(K) -> store K, V at row pos
+ * -> attention over pos+1 rows -> O -> residual -> FFN as rrro_decode_step.
+ * k_caches / v_caches: n_layers x max_seq x (n_kv_heads*head_dim) f16, updated. */
+int rrro_decode_step_kv(int d_model, int n_heads, int n_kv_heads, int head_dim, int ffn_dim,
+                        int n_layers, int vocab, float eps, int rope_dim, float theta,
+                        float attn_factor, const float* factors, int n_factors, int pos,
+                        int max_seq, uint16_t* k_caches, uint16_t* v_caches,
+                        const rrro_layer* layers, const float* output_norm,
+                        const float* w_out, float* hidden, float* logits, int threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -241,8 +241,18 @@ int rrr_check_device_error(rrr_ctx* ctx, int* code) {
                    "rrr_check_device_error: read");
   RRR_LAUNCH_CHECK(ctx, cudaMemset(ctx->d_err, 0, sizeof v), "rrr_check_device_error: clear");
   *code = v;
+  if (v == 6)
+    return set_error(ctx, RRR_ERR_BAD_SHAPE,
+                     "a kernel met a position outside the KV cache or a token id outside the "
+                     "embedding table (device code 6)");
   if (v != 0)
     return set_error(ctx, RRR_ERR_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", v);
+  return RRR_OK;
+}
+
+int rrr_set_pdl(rrr_ctx* ctx, int enable) {
+  RRR_CHECK_CTX(ctx);
+  ctx->pdl = enable != 0;
   return RRR_OK;
 }
 

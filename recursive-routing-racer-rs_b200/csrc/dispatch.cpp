@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "capi_internal.h"
+#include "internal.h"
 
 using namespace rrr;
 
@@ -128,8 +129,74 @@ int run_named(rrr_ctx* ctx, const char* cname, void* const* b, const uint64_t* s
     return set_error(ctx, RRR_ERR_UNSUPPORTED,
                      "%s: repacked / fused-norm shader layouts are not provided; upload raw GGUF "
                      "blocks and use matmul_q{4,5,6}k (or rrr_gemv_kq_ex with RRR_X_RMSNORM)", cname);
-  if (name == "attention" || name == "rope" || name == "rope_kv_store" || name == "kv_store" ||
-      name == "layer_norm" || name == "gelu" || name == "add")
+  if (name == "rope_kv_store") {
+    // push [pos, n_heads, n_kv_heads, head_dim, rope_dim, q_dim, kv_stride], bindings
+    // [qkv, rope_factors, kbuf, vbuf] (phi4.rs:1115-1117, 1016-1017). The push carries no
+    // theta / attention factor: the reference's constants ROPE_THETA and ROPE_ATTN_FACTOR
+    // (phi4.rs:115-116) apply, and the factor table is the whole rope_factors binding.
+    if ((rc = need(4, 7))) return rc;
+    rrr_attn_desc a{};
+    const uint32_t pos = push_u32(push, 0);
+    a.n_heads = (int)push_u32(push, 1);
+    a.n_kv_heads = (int)push_u32(push, 2);
+    a.head_dim = (int)push_u32(push, 3);
+    a.rope_dim = (int)push_u32(push, 4);
+    const uint32_t q_dim = push_u32(push, 5), kv_stride = push_u32(push, 6);
+    if (q_dim != (uint32_t)(a.n_heads * a.head_dim) || kv_stride != (uint32_t)(a.n_kv_heads * a.head_dim) ||
+        kv_stride == 0)
+      return set_error(ctx, RRR_ERR_BAD_SHAPE, "rope_kv_store: q_dim / kv_stride disagree with the heads");
+    a.rope_theta = 10000.0f;
+    a.rope_attn_factor = 1.190238f;
+    a.rope_factors = static_cast<const float*>(b[1]);
+    a.n_rope_factors = (int)(sz[1] / 4);
+    a.max_seq = (int)(sz[2] / (2ull * kv_stride));
+    if (small(0, 4ull * (q_dim + 2ull * kv_stride)) || sz[3] < sz[2] || pos >= (uint32_t)a.max_seq)
+      return set_error(ctx, RRR_ERR_BUFFER_TOO_SMALL, "rope_kv_store: binding smaller than the push needs");
+    if (!run) return RRR_OK;
+    return rrr_rope_kv_store(ctx, &a, static_cast<float*>(b[0]), q_dim + 2ll * kv_stride, 1, (int)pos,
+                             nullptr, static_cast<uint16_t*>(b[2]), static_cast<uint16_t*>(b[3]), stream);
+  }
+  if (name == "kv_store") {
+    // push [pos, q_dim, kv_stride], bindings [qkv, kbuf, vbuf] (phi4.rs:1663-1677): K and
+    // V of the QKV row (after RoPE) rounded to f16 into cache row pos
+    if ((rc = need(3, 3))) return rc;
+    const uint32_t pos = push_u32(push, 0), q_dim = push_u32(push, 1), kv_stride = push_u32(push, 2);
+    if (kv_stride == 0 || kv_stride % 2)
+      return set_error(ctx, RRR_ERR_BAD_SHAPE, "kv_store: kv_stride must be even and > 0");
+    if (small(0, 4ull * (q_dim + 2ull * kv_stride)) || small(1, 2ull * (pos + 1) * kv_stride) ||
+        small(2, 2ull * (pos + 1) * kv_stride))
+      return set_error(ctx, RRR_ERR_BUFFER_TOO_SMALL, "kv_store: binding smaller than the push needs");
+    if ((reinterpret_cast<uintptr_t>(b[1]) | reinterpret_cast<uintptr_t>(b[2])) & 3)
+      return set_error(ctx, RRR_ERR_MISALIGNED, "kv_store: caches must be 4-byte aligned");
+    if (!run) return RRR_OK;
+    if ((rc = bind_device(ctx))) return rc;
+    // one "head" of kv_stride values, no rotation
+    cudaError_t e = launch_rope_kv_store(make_env(ctx, stream), static_cast<float*>(b[0]) + q_dim,
+                                         q_dim + 2ll * kv_stride, 1, (int)pos, nullptr, 0, 1,
+                                         (int)kv_stride, 0, 1.f, 1.f, nullptr, 0,
+                                         static_cast<uint16_t*>(b[1]), static_cast<uint16_t*>(b[2]),
+                                         (int)pos + 1);
+    return e == cudaSuccess ? RRR_OK : cuda_error(ctx, e, "kv_store launch");
+  }
+  if (name == "attention") {
+    // push [seq_len, n_kv_heads, heads_per_kv, head_dim], bindings [q, kbuf, vbuf, out],
+    // one query row (phi4.rs:1118-1121, 1680-1688)
+    if ((rc = need(4, 4))) return rc;
+    rrr_attn_desc a{};
+    const uint32_t seq = push_u32(push, 0);
+    a.n_kv_heads = (int)push_u32(push, 1);
+    a.n_heads = (int)(push_u32(push, 1) * push_u32(push, 2));
+    a.head_dim = (int)push_u32(push, 3);
+    a.max_seq = (int)seq;
+    const uint64_t qn = (uint64_t)a.n_heads * a.head_dim, kvn = (uint64_t)seq * a.n_kv_heads * a.head_dim;
+    if (seq == 0 || small(0, 4 * qn) || small(1, 2 * kvn) || small(2, 2 * kvn) || small(3, 4 * qn))
+      return set_error(ctx, RRR_ERR_BUFFER_TOO_SMALL, "attention: binding smaller than the push needs");
+    if (!run) return RRR_OK;
+    return rrr_attention_f16kv(ctx, &a, static_cast<const float*>(b[0]), (int64_t)qn, 1, (int)seq - 1,
+                               nullptr, static_cast<const uint16_t*>(b[1]),
+                               static_cast<const uint16_t*>(b[2]), static_cast<float*>(b[3]), stream);
+  }
+  if (name == "rope" || name == "layer_norm" || name == "gelu" || name == "add")
     return set_error(ctx, RRR_ERR_UNSUPPORTED, "%s: outside the weight path; not provided", cname);
   return set_error(ctx, RRR_ERR_INVALID_ARG, "unknown dispatch name '%s'", cname);
 }

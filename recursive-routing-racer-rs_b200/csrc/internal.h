@@ -70,4 +70,20 @@ cudaError_t launch_gemm_kq_tc(const LaunchEnv& env, int qtype, const void* w,
 // *d_ok when the device result matches the expected product).
 cudaError_t launch_mma_selftest(const LaunchEnv& env, int* d_ok);
 
+// Decode attention at real positions (attention.cu).
+cudaError_t launch_rope_kv_store(const LaunchEnv& env, float* qkv, long long row_stride, int rows,
+                                 int pos0, const int* d_pos, int nh, int nkv, int hd, int rope_dim,
+                                 float theta, float attn_factor, const float* factors,
+                                 int n_factors, uint16_t* kc, uint16_t* vc, int max_seq);
+cudaError_t launch_attention_f16kv(const LaunchEnv& env, const float* q, long long q_stride,
+                                   int rows, int pos0, const int* d_pos, const uint16_t* kc,
+                                   const uint16_t* vc, float* out, int nh, int nkv, int hd,
+                                   int max_seq, int seq_max);
+int attention_smem_for(int hd, int hpk, int seq_max);
+cudaError_t launch_embed_rows(const LaunchEnv& env, int type, const void* table, long long n_rows,
+                              long long row_bytes, int d, const int* tokens, int n_tokens,
+                              float* out);
+// *d_pos += delta after the preceding kernels of the stream have completed.
+cudaError_t launch_pos_advance(const LaunchEnv& env, int* d_pos, int delta);
+
 }  // namespace rrr

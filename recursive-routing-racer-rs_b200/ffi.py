@@ -52,7 +52,15 @@ class Phi4Desc(ctypes.Structure):
     _fields_ = [("d_model", c_int), ("n_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int),
                 ("ffn_dim", c_int), ("n_layers", c_int), ("vocab", c_int), ("rms_eps", c_float),
                 ("logits_chunk_rows", c_int), ("layers", POINTER(Phi4Layer)),
-                ("output_norm", c_void_p), ("w_out", c_void_p)]
+                ("output_norm", c_void_p), ("w_out", c_void_p), ("max_seq", c_int),
+                ("rope_dim", c_int), ("rope_theta", c_float), ("rope_attn_factor", c_float),
+                ("rope_factors", c_void_p), ("n_rope_factors", c_int)]
+
+
+class AttnDesc(ctypes.Structure):
+    _fields_ = [("n_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int), ("rope_dim", c_int),
+                ("rope_theta", c_float), ("rope_attn_factor", c_float), ("rope_factors", c_void_p),
+                ("n_rope_factors", c_int), ("max_seq", c_int)]
 
 
 vp = c_void_p
@@ -112,6 +120,13 @@ PROTOS = {
     "rrr_phi4_forward": (c_int, [vp, vp, vp, vp, c_int, vp]),
     "rrr_phi4_launches_per_step": (c_int, [vp, POINTER(c_int)]),
     "rrr_phi4_destroy": (c_int, [vp]),
+    "rrr_set_pdl": (c_int, [vp, c_int]),
+    "rrr_phi4_set_position": (c_int, [vp, c_int, vp]),
+    "rrr_phi4_position": (c_int, [vp, POINTER(c_int)]),
+    "rrr_phi4_kv_cache": (c_int, [vp, c_int, POINTER(vp), POINTER(vp)]),
+    "rrr_rope_kv_store": (c_int, [vp, POINTER(AttnDesc), vp, c_int64, c_int, c_int, vp, vp, vp, vp]),
+    "rrr_attention_f16kv": (c_int, [vp, POINTER(AttnDesc), vp, c_int64, c_int, c_int, vp, vp, vp, vp, vp]),
+    "rrr_embed_rows": (c_int, [vp, c_int, vp, c_int64, c_int, vp, c_int, vp, vp]),
     "rrr_fill_kquant_random": (c_int, [vp, c_int, vp, c_int64, c_uint64, vp]),
     "rrr_fill_f32_normal": (c_int, [vp, vp, c_int64, c_float, c_float, c_uint64, vp]),
     "rrr_fill_f32_uniform": (c_int, [vp, vp, c_int64, c_float, c_float, c_uint64, vp]),
@@ -186,6 +201,6 @@ class Context:
     def device_error(self) -> int:
         code = c_int()
         rc = lib().rrr_check_device_error(self.h, ctypes.byref(code))
-        if rc not in (RRR_OK, -7):
+        if rc not in (RRR_OK, -7, -3):
             self.check(rc)
         return code.value

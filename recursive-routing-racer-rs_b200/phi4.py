@@ -25,6 +25,9 @@ class ModelConfig:
     n_layers: int = 32
     vocab_size: int = 200064
     rms_eps: float = 1e-5
+    rope_dim: int = 96            # ROPE_DIM, phi4.rs:114
+    rope_theta: float = 10000.0   # ROPE_THETA, phi4.rs:115
+    rope_attn_factor: float = 1.190238  # ROPE_ATTN_FACTOR, phi4.rs:116
     qkv_type: int = 13      # Q5_K (Q4_K_M assignment in the benchmark configs)
     o_type: int = 12        # Q4_K
     gate_up_type: int = 12  # Q4_K
@@ -46,9 +49,15 @@ class ModelConfig:
         nh = g("attention.head_count")
         eps = gguf.meta_f32(f"{arch}.attention.layer_norm_rms_epsilon")
         vocab = next((t.shape[1] for t in gguf.tensor_infos if t.name == "token_embd.weight"), 0)
+        hd = d // nh if nh else 128
+        rd = g("rope.dimension_count")
+        theta = gguf.meta_f32(f"{arch}.rope.freq_base")
+        af = gguf.meta_f32(f"{arch}.rope.scaling.attn_factor")
         return cls(d_model=d, n_heads=nh, n_kv_heads=g("attention.head_count_kv"),
-                   head_dim=d // nh if nh else 128, ffn_dim=g("feed_forward_length"),
-                   n_layers=g("block_count"), vocab_size=vocab, rms_eps=eps if eps > 0 else 1e-5)
+                   head_dim=hd, ffn_dim=g("feed_forward_length"),
+                   n_layers=g("block_count"), vocab_size=vocab, rms_eps=eps if eps > 0 else 1e-5,
+                   rope_dim=rd if rd > 0 else hd, rope_theta=theta if theta > 0 else 10000.0,
+                   rope_attn_factor=af if af > 0 else 1.0)
 
     def layer_gemvs(self):
         """(name, qtype, K, N) of the four per-layer GEMVs (benchmark config 1)."""
@@ -124,9 +133,16 @@ class SyntheticPhi4:
         self.w_out = self.arena.alloc(cfg.vocab_size * cfg.d_model * 4)
         ctx.check(L.rrr_fill_f32_normal(ctx.h, self.w_out, cfg.vocab_size * cfg.d_model, 0.0, 0.02,
                                         tensor_seed(seed, -1, "output"), s))
+        # LongRoPE short factors (rope_factors_short.weight, one per rotated pair) ~ U[1, 1.5]
+        self.n_rope_factors = cfg.rope_dim // 2
+        self.rope_factors = self.arena.alloc(max(1, self.n_rope_factors) * 4)
+        if self.n_rope_factors:
+            ctx.check(L.rrr_fill_f32_uniform(ctx.h, self.rope_factors, self.n_rope_factors, 1.0, 1.5,
+                                             tensor_seed(seed, -1, "rope_factors"), s))
         ctx.check(L.rrr_sync(ctx.h, s))
 
-    def desc(self):
+    def desc(self, max_seq: int = 0):
+        """rrr_phi4_desc; max_seq > 0 selects KV-cache decode with RoPE."""
         cfg = self.cfg
         arr = (ffi.Phi4Layer * cfg.n_layers)()
         for i, e in enumerate(self.layers):
@@ -137,7 +153,9 @@ class SyntheticPhi4:
             arr[i].attn_norm, arr[i].ffn_norm = e["attn_norm"], e["ffn_norm"]
         d = ffi.Phi4Desc(cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim,
                          cfg.n_layers, cfg.vocab_size, cfg.rms_eps, cfg.logits_chunk_rows,
-                         ctypes.cast(arr, ctypes.POINTER(ffi.Phi4Layer)), self.output_norm, self.w_out)
+                         ctypes.cast(arr, ctypes.POINTER(ffi.Phi4Layer)), self.output_norm, self.w_out,
+                         max_seq, cfg.rope_dim, cfg.rope_theta, cfg.rope_attn_factor,
+                         self.rope_factors, self.n_rope_factors)
         return d, arr
 
     def close(self) -> None:
@@ -147,9 +165,10 @@ class SyntheticPhi4:
 class Phi4Decoder:
     """The decode step (rrr_phi4_*), a drop-in for Phi4Model::forward_gpu's GPU chain."""
 
-    def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4):
+    def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4, max_seq: int = 0):
         self.ctx = ctx
-        d, self._keep = weights.desc()
+        self.max_seq = max_seq
+        d, self._keep = weights.desc(max_seq)
         h = c_void_p()
         ctx.check(ffi.lib().rrr_phi4_create(ctx.h, ctypes.byref(d), ctypes.byref(h)))
         self.h = h
@@ -165,6 +184,23 @@ class Phi4Decoder:
         n = c_int()
         self.ctx.check(ffi.lib().rrr_phi4_launches_per_step(self.h, ctypes.byref(n)))
         return n.value
+
+    def set_position(self, pos: int, stream=None) -> None:
+        """KV-cache decode: position of the next forward (KVCache.len)."""
+        s = None if stream is None else c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+        self.ctx.check(ffi.lib().rrr_phi4_set_position(self.h, pos, s))
+
+    @property
+    def position(self) -> int:
+        n = c_int()
+        self.ctx.check(ffi.lib().rrr_phi4_position(self.h, ctypes.byref(n)))
+        return n.value
+
+    def kv_cache(self, layer: int):
+        """Device pointers (k, v) of one layer's f16 [max_seq, n_kv*hd] caches."""
+        k, v = c_void_p(), c_void_p()
+        self.ctx.check(ffi.lib().rrr_phi4_kv_cache(self.h, layer, ctypes.byref(k), ctypes.byref(v)))
+        return k.value, v.value
 
     def close(self) -> None:
         if self.h:

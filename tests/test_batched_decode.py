@@ -105,6 +105,7 @@ def test_batched_step_single_gpu(rrr, ctx, oracle, M):
     cfg = _cfg()
     w = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, 1, 0), seed=21)
     dec = tp.TPDecoder(ctx, w, max_batch=M)
+    torch.manual_seed(M)
     hidden0 = torch.randn(M, cfg.d_model, device="cuda")
     h = hidden0.clone()
     lg = torch.empty(M, cfg.vocab_size, device="cuda")
@@ -129,6 +130,7 @@ def test_batched_step_tp2_emulated(rrr, ctx, oracle):
     layers, on, wo = _host_model(oracle, w1, torch)
     ws = [tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, G, g), seed=22) for g in range(G)]
     decs = [tp.TPDecoder(ctx, w, max_batch=M) for w in ws]
+    torch.manual_seed(1000 + M)
     hidden0 = torch.randn(M, cfg.d_model, device="cuda")
     hs = [hidden0.clone() for _ in range(G)]
     lgs = [torch.empty(M, cfg.vocab_size, device="cuda") for _ in range(G)]
