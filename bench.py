@@ -319,6 +319,28 @@ def run_ours(args, rank, world, local_rank):
               "frac_of_peak": round(dec_bytes / dms / 1e6 / peak, 4),
               "launches_per_token": dec.launches_per_step() + 1, "graph": True}
     dec.close()
+    # ---------------- decode at real positions (KV cache of 2048 rows, RoPE, attention):
+    # graph replays at positions 1024 .. 1024 + steps (the position advances on the device)
+    kdec = phi4.Phi4Decoder(ctx, model, max_seq=2048)
+    P0 = 1024
+    kdec.set_position(P0 - max(3, args.warmup), stream)
+    for _ in range(max(3, args.warmup)):
+        kdec.forward(hidden.data_ptr(), logits.data_ptr(), am.data_ptr(), True, stream)
+    barrier()
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ksteps = max(args.steps, 10)
+    k0.record(stream)
+    for _ in range(ksteps):
+        kdec.forward(hidden.data_ptr(), logits.data_ptr(), am.data_ptr(), True, stream)
+    k1.record(stream)
+    barrier()
+    kms = max_over_ranks(k0.elapsed_time(k1) / ksteps)
+    kv_bytes = 2 * 2 * cfg.n_kv_heads * cfg.head_dim * cfg.n_layers * (P0 + ksteps / 2)
+    decode_kv = {"positions": [P0, P0 + ksteps], "tok_s": round(1e3 / kms, 2),
+                 "ms_per_token": round(kms, 4),
+                 "GBps": round((dec_bytes + kv_bytes) / kms / 1e6, 1),
+                 "launches_per_token": kdec.launches_per_step() + 1, "graph": True}
+    kdec.close()
     # ---------------- batched decode step, 64 tokens at position 0 (configs[4] batch 64 on
     # one GPU / one rank's replica): tcgen05 GEMMs for every layer GEMM, batched logits
     tpm = importlib.import_module("recursive-routing-racer-rs_b200.tp")
@@ -449,6 +471,7 @@ def run_ours(args, rank, world, local_rank):
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one gate_up "
                                            "launch (profiles/gemv_kq_phi4_layer_shapes.md)"},
             "decode": decode,
+            "decode_kv": decode_kv,
             "decode_batch64": decode_batch,
             "tp_decode": tp_decode,
             "batched_gemm": {"note": "configs[3]: rrr_gemm_kq_batched (tcgen05, bf16 x bf16 -> f32); "

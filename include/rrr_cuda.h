@@ -297,6 +297,13 @@ int rrr_rope_kv_store(rrr_ctx* ctx, const rrr_attn_desc* a, float* qkv, int64_t 
 int rrr_attention_f16kv(rrr_ctx* ctx, const rrr_attn_desc* a, const float* q, int64_t q_stride,
                         int rows, int pos0, const int* d_pos, const uint16_t* k_cache,
                         const uint16_t* v_cache, float* out, void* stream);
+/* One token, fused: RoPE of its query heads (in shared memory; qkv is not modified), its
+ * K (rotated) and V rows stored into the caches at position p, then attention over rows
+ * 0..p. Same results as rrr_rope_kv_store followed by rrr_attention_f16kv for rows = 1,
+ * in one launch (the decode step's path). qkv: one f32 QKV row. */
+int rrr_rope_attention_f16kv(rrr_ctx* ctx, const rrr_attn_desc* a, const float* qkv, int pos0,
+                             const int* d_pos, uint16_t* k_cache, uint16_t* v_cache, float* out,
+                             void* stream);
 /* Embedding rows (Phi4Model::embed on the table dequantised by dequant_tensor_f32,
  * phi4.rs:709, 572-587, 2085-2089): out[t] = row tokens[t] of an [n_rows, d] table stored
  * as GGUF type ggml_type (0 F32, 1 F16, 6 Q5_0, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K; d a
@@ -311,8 +318,8 @@ int rrr_embed_rows(rrr_ctx* ctx, int ggml_type, const void* table, int64_t n_row
  *   h += Wo . expand(V(Wqkv . rms(h)*g_attn)); h += Wdown . (silu(g) * u),
  *   [g; u] = Wgate_up . rms(h)*g_ffn; then logits = Wout . rms(h)*g_out.
  * max_seq > 0: one token at the model's current position p (forward_dynamic,
- * phi4.rs:1593-1760): after the QKV GEMV, RoPE + the f16 KV store at row p
- * (rrr_rope_kv_store) and attention over rows 0..p (rrr_attention_f16kv) give the
+ * phi4.rs:1593-1760): after the QKV GEMV, RoPE + the f16 KV store at row p and
+ * attention over rows 0..p (rrr_rope_attention_f16kv, one launch) give the
  * O-projection's input; the model owns the caches (2 x n_layers x max_seq x n_kv*hd f16)
  * and a device position that starts at 0 and advances by one per forward.
  * All pointers are device pointers that the caller owns and keeps alive. */

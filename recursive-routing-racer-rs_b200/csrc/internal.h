@@ -75,10 +75,19 @@ cudaError_t launch_rope_kv_store(const LaunchEnv& env, float* qkv, long long row
                                  int pos0, const int* d_pos, int nh, int nkv, int hd, int rope_dim,
                                  float theta, float attn_factor, const float* factors,
                                  int n_factors, uint16_t* kc, uint16_t* vc, int max_seq);
+// RoPE parameters of the fused one-token path (rope != null in launch_attention_f16kv):
+// q is the token's QKV row; its query heads are rotated in shared memory and its K
+// (rotated) and V rows are stored into the caches at the token's position first.
+struct AttnRope {
+  int rope_dim;
+  float theta, attn_factor;
+  const float* factors;
+  int n_factors;
+};
 cudaError_t launch_attention_f16kv(const LaunchEnv& env, const float* q, long long q_stride,
                                    int rows, int pos0, const int* d_pos, const uint16_t* kc,
                                    const uint16_t* vc, float* out, int nh, int nkv, int hd,
-                                   int max_seq, int seq_max);
+                                   int max_seq, int seq_max, const AttnRope* rope);
 int attention_smem_for(int hd, int hpk, int seq_max);
 cudaError_t launch_embed_rows(const LaunchEnv& env, int type, const void* table, long long n_rows,
                               long long row_bytes, int d, const int* tokens, int n_tokens,

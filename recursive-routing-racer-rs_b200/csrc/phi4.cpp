@@ -9,11 +9,11 @@
 // epilogue (rrr_gemv_kq_swiglu), so a layer is 4 launches and the step is
 // 4*L + logits chunks (+ argmax). The whole step can be captured once into a CUDA graph.
 //
-// With a KV cache (max_seq > 0, forward_dynamic, phi4.rs:1593-1760) a layer is 6 launches:
-// QKV (RMSNorm prologue), RoPE + f16 KV store, attention over rows 0..pos, O-proj (residual
-// epilogue), gate_up (SwiGLU), down (residual); the position lives on the device and a
-// one-thread kernel advances it at the end of the step, so one captured graph serves
-// every position.
+// With a KV cache (max_seq > 0, forward_dynamic, phi4.rs:1593-1760) a layer is 5 launches:
+// QKV (RMSNorm prologue), RoPE + f16 KV store + attention over rows 0..pos (one fused
+// kernel), O-proj (residual epilogue), gate_up (SwiGLU), down (residual); the position
+// lives on the device and a one-thread kernel advances it at the end of the step, so one
+// captured graph serves every position.
 #include <cuda_runtime.h>
 
 #include <vector>
@@ -60,9 +60,8 @@ static int phi4_issue(rrr_phi4* m, float* hidden, float* logits, int* argmax, vo
     if (d.max_seq > 0) {
       uint16_t* kc = m->kv + 2 * cache * l;
       uint16_t* vc = kc + cache;
-      if ((rc = rrr_rope_kv_store(ctx, &m->attn_desc, m->qkv, qkv_dim, 1, 0, m->d_pos, kc, vc, stream)) ||
-          (rc = rrr_attention_f16kv(ctx, &m->attn_desc, m->qkv, qkv_dim, 1, 0, m->d_pos, kc, vc,
-                                    m->attn, stream)) ||
+      if ((rc = rrr_rope_attention_f16kv(ctx, &m->attn_desc, m->qkv, 0, m->d_pos, kc, vc, m->attn,
+                                         stream)) ||
           (rc = rrr_gemv_kq_ex(ctx, L.o_type, L.w_o, m->attn, hidden, d.n_heads * d.head_dim,
                                d.d_model, hidden, nullptr, stream)))
         return rc;
@@ -223,7 +222,7 @@ int rrr_phi4_forward(rrr_phi4* m, float* hidden, float* logits, int* argmax_out,
 int rrr_phi4_launches_per_step(rrr_phi4* m, int* n) {
   if (!m || !n) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null argument");
   const int chunk = m->d.logits_chunk_rows > 0 ? m->d.logits_chunk_rows : m->d.vocab;
-  *n = (m->d.max_seq > 0 ? 6 : 4) * m->d.n_layers + (m->d.vocab + chunk - 1) / chunk +
+  *n = (m->d.max_seq > 0 ? 5 : 4) * m->d.n_layers + (m->d.vocab + chunk - 1) / chunk +
        (m->d.max_seq > 0 ? 1 : 0);
   return RRR_OK;
 }

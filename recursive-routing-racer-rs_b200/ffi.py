@@ -126,6 +126,7 @@ PROTOS = {
     "rrr_phi4_kv_cache": (c_int, [vp, c_int, POINTER(vp), POINTER(vp)]),
     "rrr_rope_kv_store": (c_int, [vp, POINTER(AttnDesc), vp, c_int64, c_int, c_int, vp, vp, vp, vp]),
     "rrr_attention_f16kv": (c_int, [vp, POINTER(AttnDesc), vp, c_int64, c_int, c_int, vp, vp, vp, vp, vp]),
+    "rrr_rope_attention_f16kv": (c_int, [vp, POINTER(AttnDesc), vp, c_int, vp, vp, vp, vp, vp]),
     "rrr_embed_rows": (c_int, [vp, c_int, vp, c_int64, c_int, vp, c_int, vp, vp]),
     "rrr_fill_kquant_random": (c_int, [vp, c_int, vp, c_int64, c_uint64, vp]),
     "rrr_fill_f32_normal": (c_int, [vp, vp, c_int64, c_float, c_float, c_uint64, vp]),

@@ -8,6 +8,7 @@ DRAM figures of a capture are those of the bench's per-GEMV lines.
     python -m recursive-routing-racer-rs_b200.profcases gemv            # 3 GEMV shapes x 6
     python -m recursive-routing-racer-rs_b200.profcases decode --layers 32
     python -m recursive-routing-racer-rs_b200.profcases gemm --m 256    # batched tcgen05 GEMM
+    python -m recursive-routing-racer-rs_b200.profcases attn --pos 1024 # RoPE + KV + attention
 """
 import argparse
 import importlib
@@ -66,7 +67,28 @@ def case_gemm(ctx, L, torch, args):
                                             c_void_p(y.data_ptr()), args.m, K, N, None))
 
 
-CASES = {"gemv": case_gemv, "decode": case_decode, "gemm": case_gemm}
+def case_attn(ctx, L, torch, args):
+    """Fused RoPE + f16 KV store + decode attention (Phi-4-mini heads: 24 query, 8 KV, 128)
+    at position --pos of 8 layers' 2048-row caches, the position read from the device."""
+    import ctypes
+    ffi = importlib.import_module(_PKG + ".ffi")
+    nh, nkv, hd, max_seq = 24, 8, 128, 2048
+    kvs = nkv * hd
+    a = ffi.AttnDesc(nh, nkv, hd, 96, 10000.0, 1.190238, None, 0, max_seq)
+    caches = [(torch.randn(max_seq * kvs, device="cuda").half(), torch.randn(max_seq * kvs, device="cuda").half())
+              for _ in range(8)]
+    qkv = torch.randn((nh + 2 * nkv) * hd, device="cuda")
+    out = torch.empty(nh * hd, device="cuda")
+    dpos = torch.tensor([args.pos], dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    for _ in range(args.rounds):
+        for kc, vc in caches:
+            ctx.check(L.rrr_rope_attention_f16kv(ctx.h, ctypes.byref(a), c_void_p(qkv.data_ptr()), 0,
+                                                 c_void_p(dpos.data_ptr()), c_void_p(kc.data_ptr()),
+                                                 c_void_p(vc.data_ptr()), c_void_p(out.data_ptr()), None))
+
+
+CASES = {"gemv": case_gemv, "decode": case_decode, "gemm": case_gemm, "attn": case_attn}
 
 
 def main(argv=None):
@@ -75,6 +97,7 @@ def main(argv=None):
     ap.add_argument("--rounds", type=int, default=6)
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--m", type=int, default=256)
+    ap.add_argument("--pos", type=int, default=1024)
     args = ap.parse_args(argv)
     import torch
     rrr = importlib.import_module(_PKG)
