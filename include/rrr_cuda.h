@@ -153,6 +153,14 @@ int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16
  * residual adds of the batched decode step (phi4.rs:1393-1403, done on the CPU there). */
 int rrr_gemm_kq_batched_ex(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16_t* x_bf16,
                            float* y, int M, int K, int N, const float* residual, void* stream);
+/* The same GEMM with the kernel chosen explicitly (tests, benchmarks): RRR_GEMM_AUTO is
+ * rrr_gemm_kq_batched_ex's choice (mma.sync for 16 <= M <= 64 when every weight row is a
+ * multiple of 16 bytes, tcgen05 for larger M, one GEMV per token below 16); the others force
+ * one kernel and fail with RRR_ERR_BAD_SHAPE where it does not apply. */
+enum { RRR_GEMM_AUTO = 0, RRR_GEMM_TCGEN05 = 1, RRR_GEMM_MMA = 2, RRR_GEMM_PER_TOKEN = 3 };
+int rrr_gemm_kq_batched_path(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16_t* x_bf16,
+                             float* y, int M, int K, int N, const float* residual, int path,
+                             void* stream);
 
 /* ---- batched decode-step glue (M tokens, each at position 0) -----------------------
  * Producers of the bf16 GEMM inputs (phi4.rs:1198-1445 computes these per token on the

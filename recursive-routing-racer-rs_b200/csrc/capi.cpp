@@ -364,7 +364,14 @@ int rrr_dequant_kq(rrr_ctx* ctx, int qtype, const void* w, float* out, int64_t n
 
 int rrr_gemm_kq_batched_ex(rrr_ctx* ctx, int qtype, const void* w, const uint16_t* x, float* y,
                            int M, int K, int N, const float* residual, void* stream) {
+  return rrr_gemm_kq_batched_path(ctx, qtype, w, x, y, M, K, N, residual, RRR_GEMM_AUTO, stream);
+}
+
+int rrr_gemm_kq_batched_path(rrr_ctx* ctx, int qtype, const void* w, const uint16_t* x, float* y,
+                             int M, int K, int N, const float* residual, int path, void* stream) {
   RRR_CHECK_CTX(ctx);
+  if (path < RRR_GEMM_AUTO || path > RRR_GEMM_PER_TOKEN)
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemm_kq_batched_path: unknown path %d", path);
   int rc = check_qtype(ctx, qtype, "rrr_gemm_kq_batched");
   if (rc) return rc;
   if (!w || !x || !y) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemm_kq_batched: null pointer");
@@ -379,12 +386,26 @@ int rrr_gemm_kq_batched_ex(rrr_ctx* ctx, int qtype, const void* w, const uint16_
     return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemm_kq_batched: residual must equal Y or not overlap it");
   RRR_BIND(ctx);
   const LaunchEnv env = make_env(ctx, stream);
+  MmaPlan mplan;
+  if ((path == RRR_GEMM_AUTO || path == RRR_GEMM_MMA) &&
+      plan_gemm_kq_mma(qtype, M, K, N, ctx->sm_count, &mplan)) {
+    RRR_LAUNCH_CHECK(ctx, launch_gemm_kq_mma(env, qtype, w, x, y, M, K, N, mplan, residual),
+                     "rrr_gemm_kq_batched (mma.sync) launch");
+    return RRR_OK;
+  }
+  if (path == RRR_GEMM_MMA)
+    return set_error(ctx, RRR_ERR_BAD_SHAPE,
+                     "rrr_gemm_kq_batched_path: the mma.sync kernel takes 16 <= M <= 64 and rows "
+                     "of a multiple of 16 bytes");
   TcPlan plan;
-  if (M >= 16 && plan_gemm_kq_tc(qtype, M, K, N, ctx->sm_count, &plan)) {
+  if ((path == RRR_GEMM_AUTO || path == RRR_GEMM_TCGEN05) && M >= 16 &&
+      plan_gemm_kq_tc(qtype, M, K, N, ctx->sm_count, &plan)) {
     RRR_LAUNCH_CHECK(ctx, launch_gemm_kq_tc(env, qtype, w, x, y, M, K, N, plan, residual),
                      "rrr_gemm_kq_batched (tensor cores) launch");
     return RRR_OK;
   }
+  if (path == RRR_GEMM_TCGEN05)
+    return set_error(ctx, RRR_ERR_BAD_SHAPE, "rrr_gemm_kq_batched_path: the tcgen05 kernel takes M >= 16");
   for (int m = 0; m < M; ++m)
     RRR_LAUNCH_CHECK(ctx, launch_gemv_kq_bf16(env, qtype, w, x + (size_t)m * K, y + (size_t)m * N, K, N,
                                               residual ? residual + (size_t)m * N : nullptr),

@@ -70,6 +70,21 @@ cudaError_t launch_gemm_kq_tc(const LaunchEnv& env, int qtype, const void* w,
 // *d_ok when the device result matches the expected product).
 cudaError_t launch_mma_selftest(const LaunchEnv& env, int* d_ok);
 
+// Batched-token GEMM for 16 <= M <= 64 on mma.sync (gemm_kq_mma.cu): 256-row tiles, the
+// weights dequantised into A fragments in registers. plan_gemm_kq_mma returns false for
+// shapes it does not handle (M outside [16, 64], rows not 16-byte aligned).
+struct MmaPlan {
+  int tn;          // tokens per tile: M rounded up to 16
+  int m_tiles, n_tiles;
+  int splits;      // K splits = CTAs per cluster (1..8)
+  int stages, smem;
+  int kbs;         // super-blocks per stage
+};
+bool plan_gemm_kq_mma(int qtype, int M, int K, int N, int sm_count, MmaPlan* plan);
+cudaError_t launch_gemm_kq_mma(const LaunchEnv& env, int qtype, const void* w,
+                               const uint16_t* x_bf16, float* y, int M, int K, int N,
+                               const MmaPlan& plan, const float* residual);
+
 // Decode attention at real positions (attention.cu).
 cudaError_t launch_rope_kv_store(const LaunchEnv& env, float* qkv, long long row_stride, int rows,
                                  int pos0, const int* d_pos, int nh, int nkv, int hd, int rope_dim,

@@ -368,8 +368,11 @@ def test_gemm_batched(rrr, ctx, oracle, G, qt, M):
         assert rel_l2(got[m], oracle.gemv_kq(qt, raw, Xf[m], K, N)) < 1e-2
 
 
-def _gemm_tc_case(rrr, ctx, oracle, G, qt, M, K, N, seed, repeats=1):
-    """Runs rrr_gemm_kq_batched `repeats` times; returns (outputs, f32 reference)."""
+GEMM_TCGEN05, GEMM_MMA = 1, 2   # RRR_GEMM_* of rrr_gemm_kq_batched_path
+
+
+def _gemm_tc_case(rrr, ctx, oracle, G, qt, M, K, N, seed, repeats=1, path=GEMM_TCGEN05):
+    """Runs the batched GEMM kernel `path` `repeats` times; returns (outputs, f32 reference)."""
     import torch
     rng = np.random.default_rng(seed)
     raw = oracle.random_blocks(qt, N * (K // 256), rng)
@@ -381,7 +384,8 @@ def _gemm_tc_case(rrr, ctx, oracle, G, qt, M, K, N, seed, repeats=1):
     for _ in range(repeats):
         Y = G.empty_f32(M * N)
         Y.fill_(float("nan"))
-        ctx.check(rrr.ffi.lib().rrr_gemm_kq_batched(ctx.h, qt, vp(wd), vp(xd), vp(Y), M, K, N, None))
+        ctx.check(rrr.ffi.lib().rrr_gemm_kq_batched_path(ctx.h, qt, vp(wd), vp(xd), vp(Y), M, K, N, None,
+                                                         path, None))
         outs.append(G.host(Y).reshape(M, N))
     assert ctx.device_error() == 0
     return outs, ref
@@ -422,6 +426,53 @@ def test_gemm_tc_repeat_deterministic(rrr, ctx, oracle, G, qt):
         assert np.array_equal(o, outs[0])
 
 
+# mma.sync path (16 <= M <= 64): split-K clusters of up to 8, one tile, ragged rows and
+# tokens, many row tiles (no split), the down-projection shape.
+MMA_SHAPES = [
+    (16, 2048, 96),      # 1 row tile, split-K 4
+    (64, 3072, 200),     # ragged row tile, split-K 6
+    (37, 1024, 530),     # ragged token tile (TN 48), 3 row tiles
+    (48, 512, 19000),    # 75 row tiles: split-K 1
+    (20, 8192, 3072),    # down-projection shape, 12 tiles x split-K 8
+]
+
+
+@pytest.mark.parametrize("qt", QTYPES)
+@pytest.mark.parametrize("M,K,N", MMA_SHAPES)
+def test_gemm_mma(rrr, ctx, oracle, G, qt, M, K, N):
+    """mma.sync batched GEMM (weights dequantised into A fragments in registers) vs the f32
+    product of the oracle's dequantised weights and the bf16 activations: within 1e-2
+    relative L2 per token row (north star), repeat calls bit-identical."""
+    if (K // 256) * {12: 144, 13: 176, 14: 210}[qt] % 16:
+        pytest.skip("rows not a multiple of 16 bytes: the tcgen05 kernel serves this shape")
+    outs, ref = _gemm_tc_case(rrr, ctx, oracle, G, qt, M, K, N, seed=M * 5 + K + N + qt, repeats=2,
+                              path=GEMM_MMA)
+    got = outs[0]
+    assert np.isfinite(got).all()
+    for m in range(M):
+        assert rel_l2(got[m], ref[m]) < 1e-2, (m, rel_l2(got[m], ref[m]))
+    assert rel_l2(got.ravel(), ref.ravel()) < 5e-3
+    assert np.array_equal(outs[1], got)
+
+
+def test_gemm_path_selection(rrr, ctx, oracle, G):
+    """The mma.sync kernel rejects what it does not handle (M > 64, rows that are not a
+    multiple of 16 bytes: Q6_K with K/256 not a multiple of 8); the tcgen05 kernel M < 16."""
+    import torch
+    L = rrr.ffi.lib()
+    w = G.dev(oracle.random_blocks(14, 64 * 3, np.random.default_rng(1)))
+    x = torch.zeros(128, 768, dtype=torch.bfloat16, device="cuda")
+    y = G.empty_f32(128 * 64)
+    assert L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 32, 768, 64, None, GEMM_MMA, None) == -3
+    assert L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 128, 768, 64, None, GEMM_MMA, None) == -3
+    assert L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 8, 768, 64, None, GEMM_TCGEN05, None) == -3
+    assert L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 8, 768, 64, None, 7, None) == -1
+    # automatic choice still serves the Q6_K shape (tcgen05 with per-row copies)
+    ctx.check(L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 32, 768, 64, None, 0, None))
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+
+
 @pytest.mark.parametrize("qt", QTYPES)
 @pytest.mark.parametrize("M,K,N,inplace", [(16, 1024, 768, True), (40, 1024, 768, True),
                                             (40, 768, 2048, False), (3, 512, 256, True),
@@ -441,11 +492,19 @@ def test_gemm_tc_residual(rrr, ctx, oracle, G, qt, M, K, N, inplace):
     Rd = Y if inplace else R.clone().cuda()
     if not inplace:
         Y = torch.full((M, N), float("nan"), device="cuda")
-    ctx.check(rrr.ffi.lib().rrr_gemm_kq_batched_ex(ctx.h, qt, vp(wd), vp(xd), vp(Y), M, K, N, vp(Rd), None))
-    got = G.host(Y).reshape(M, N)
-    assert ctx.device_error() == 0
-    for m in range(M):
-        assert rel_l2(got[m], ref[m]) < 1e-2, (m, rel_l2(got[m], ref[m]))
+    Y0 = Y.clone()
+    R0 = Rd.clone()
+    aligned_rows = (K // 256) * {12: 144, 13: 176, 14: 210}[qt] % 16 == 0
+    paths = [0] + ([GEMM_TCGEN05] if M >= 16 else []) + ([GEMM_MMA] if 16 <= M <= 64 and aligned_rows else [])
+    for path in paths:
+        Y.copy_(Y0)
+        Rd.copy_(R0)
+        ctx.check(rrr.ffi.lib().rrr_gemm_kq_batched_path(ctx.h, qt, vp(wd), vp(xd), vp(Y), M, K, N, vp(Rd),
+                                                         path, None))
+        got = G.host(Y).reshape(M, N)
+        assert ctx.device_error() == 0
+        for m in range(M):
+            assert rel_l2(got[m], ref[m]) < 1e-2, (path, m, rel_l2(got[m], ref[m]))
 
 
 def test_decode_step_small(rrr, ctx, oracle, G):
