@@ -47,9 +47,11 @@
 namespace rrr {
 namespace {
 
-constexpr int kRows = 256;            // weight rows per tile (8 warps x 32)
-constexpr int kCWarps = 8;            // consumer warps
-constexpr int kThreads = (kCWarps + 1) * 32;
+constexpr int kRows = 256;            // weight rows per tile
+// MT m16 tiles per consumer warp: 16 / MT consumer warps cover the 256 rows (MT = 1 for
+// TN <= 32: twice the warps to hide latency; MT = 2 for larger TN: half the X reads)
+template <int MT> constexpr int cwarps() { return 16 / MT; }
+template <int MT> constexpr int threads_for() { return (cwarps<MT>() + 1) * 32; }
 constexpr int kMaxTn = 64;
 constexpr int kMaxSplits = 8;         // portable cluster size
 constexpr int kPartStride = kRows + 4;  // floats per token row of the partial tile
@@ -196,11 +198,13 @@ template <> struct MmaDq<RRR_Q6_K> {
 
 // ---- the kernel ---------------------------------------------------------------------
 
-template <int QT, int TN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int QT, int TN, int MT>
+__global__ void __launch_bounds__(threads_for<MT>(), 1)
     gemm_kq_mma_kernel(const __grid_constant__ CUtensorMap xmap,
                        const __grid_constant__ CUtensorMap wmap, const MmaParams p) {
   constexpr int NF = TN / 8;  // n fragments of 8 tokens
+  constexpr int kCWarps = cwarps<MT>();
+  constexpr int WR = 16 * MT;  // rows per consumer warp
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = smem_dyn + ((1024u - (smem_addr(smem_dyn) & 1023u)) & 1023u);
   constexpr int TS = MmaDq<QT>::kSubs + 1;  // table row stride (float2): conflict-free
@@ -209,7 +213,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_tab + (size_t)p.kbs * kRows * TS * 8);
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
-  volatile int* cons_abort = abort_flag + 1;  // written by consumers before a barrier only
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kRows, m0 = blockIdx.y * TN, z = blockIdx.z;
@@ -225,7 +228,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], kCWarps);
     }
     *abort_flag = 0;
-    *cons_abort = 0;
     fence_mbarrier_init();
   }
   __syncthreads();
@@ -261,9 +263,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- consumers: warp cw owns rows 32cw .. 32cw+31
     const int cw = warp - 1;
     const int g = lane >> 2, t = lane & 3;
-    float acc[2][NF][4];
+    float acc[MT][NF][4];
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int nf = 0; nf < NF; ++nf)
 #pragma unroll
@@ -272,41 +274,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lm_tok = 8 * ((lane >> 3) >> 1) + (lane & 7);
     const int lm_chk = (lane >> 3) & 1;
 
-    const int trow = threadIdx.x - 32;  // this thread's row of the scale table
+    // this warp's scale table: its WR rows x the stage's blocks (lane l computes row l)
+    float2* wtab = tab + cw * (p.kbs * WR * TS);
     for (int st = 0; st < n_st; ++st) {
+      if (warp_aborted(abort_flag)) break;
       const int s = st % S;
-      if (!warp_wait(&full[s], (uint32_t)(st / S) & 1u, p.err)) *cons_abort = 1;
+      if (!warp_wait(&full[s], (uint32_t)(st / S) & 1u, p.err)) {
+        *abort_flag = 1;
+        break;
+      }
       const uint8_t* raw = smem + (size_t)s * p.stage_bytes;
       const uint32_t xs = smem_addr(raw + p.raw_bytes);
       const int kb = kb0 + st * p.kbs;
       const int nk = min(p.kbs, kb1 - kb);
       const int env = (int)(((long long)kb * p.bb) & 15);
-      // the stage's scale table, one row per consumer thread (harmless on a failed wait)
-      for (int kk = 0; kk < nk; ++kk)
-        MmaDq<QT>::table_row(raw + trow * p.pitch + env + kk * p.bb, tab + (kk * kRows + trow) * TS);
-      named_barrier(1, kCWarps * 32);
-      if (*cons_abort) {  // same value for every consumer: written before the barrier only
-        *abort_flag = 1;
-        break;
-      }
+      if (lane < WR)
+        for (int kk = 0; kk < nk; ++kk)
+          MmaDq<QT>::table_row(raw + (WR * cw + lane) * p.pitch + env + kk * p.bb,
+                               wtab + (kk * WR + lane) * TS);
+      __syncwarp();
       for (int kk = 0; kk < nk; ++kk) {
-        const uint8_t* b[2][2];
-        const float2* tr[2][2];
-        typename MmaDq<QT>::Row rr[2][2];
+        const uint8_t* b[MT][2];
+        const float2* tr[MT][2];
+        typename MmaDq<QT>::Row rr[MT][2];
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int r = 32 * cw + 16 * mt + 8 * h + g;
-            b[mt][h] = raw + r * p.pitch + env + kk * p.bb;
-            tr[mt][h] = tab + (kk * kRows + r) * TS;
+            const int rl = 16 * mt + 8 * h + g;
+            b[mt][h] = raw + (WR * cw + rl) * p.pitch + env + kk * p.bb;
+            tr[mt][h] = wtab + (kk * WR + rl) * TS;
             rr[mt][h] = MmaDq<QT>::row(b[mt][h], t);
           }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t a[2][4][4];
+          uint32_t a[MT][4][4];
 #pragma unroll
-          for (int mt = 0; mt < 2; ++mt) {
+          for (int mt = 0; mt < MT; ++mt) {
             uint32_t lo[4][2], hi[4][2];
             MmaDq<QT>::chunk(b[mt][0], rr[mt][0], tr[mt][0], c, t, lo);
             MmaDq<QT>::chunk(b[mt][1], rr[mt][1], tr[mt][1], c, t, hi);
@@ -327,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t b0, b1, b2, b3;
               ldmatrix_x4(box + sw128_off(16 * np + lm_tok, 2 * ks + lm_chk), b0, b1, b2, b3);
 #pragma unroll
-              for (int mt = 0; mt < 2; ++mt) {
+              for (int mt = 0; mt < MT; ++mt) {
                 mma_bf16(acc[mt][2 * np], a[mt][ks], b0, b1);
                 mma_bf16(acc[mt][2 * np + 1], a[mt][ks], b2, b3);
               }
@@ -335,20 +339,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // every consumer is done with the stage (and its scale table) before it is refilled
-      named_barrier(1, kCWarps * 32);
+      __syncwarp();  // the warp's table rows are rewritten next stage
       if (lane == 0) mbar_arrive(&empty[s]);
     }
     // all stages consumed by every consumer before the ring is reused for the partial tile
     named_barrier(1, kCWarps * 32);
     float* part = reinterpret_cast<float*>(smem);  // [TN][kPartStride]
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int nf = 0; nf < NF; ++nf)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int row = 32 * cw + 16 * mt + g + 8 * (i >> 1);
+          const int row = WR * cw + 16 * mt + g + 8 * (i >> 1);
           const int tok = 8 * nf + 2 * t + (i & 1);
           part[tok * kPartStride + row] = acc[mt][nf][i];
         }
@@ -409,7 +412,7 @@ int table_bytes_for(int qtype, int kbs) {
   return kbs * kRows * ((qtype == RRR_Q6_K ? 16 : 8) + 1) * 8;
 }
 
-template <int QT, int TN>
+template <int QT, int TN, int MT>
 cudaError_t launch_t(const LaunchEnv& env, const MmaPlan& pl, const void* w, const uint16_t* x,
                      float* y, int M, int K, int N, const float* residual) {
   CUtensorMap xmap, wmap;
@@ -437,12 +440,12 @@ cudaError_t launch_t(const LaunchEnv& env, const MmaPlan& pl, const void* w, con
   p.stage_bytes = (uint32_t)stage_bytes_for(QT, pl.kbs, TN);
   p.off_tab = (uint32_t)pl.stages * p.stage_bytes;
   p.err = env.d_err;
-  auto kern = gemm_kq_mma_kernel<QT, TN>;
+  auto kern = gemm_kq_mma_kernel<QT, TN, MT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.n_tiles, pl.m_tiles, pl.splits);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads_for<MT>());
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = env.stream;
   cudaLaunchAttribute attr[1];
@@ -469,10 +472,10 @@ template <int QT>
 cudaError_t launch_q(const LaunchEnv& env, const MmaPlan& pl, const void* w, const uint16_t* x,
                      float* y, int M, int K, int N, const float* residual) {
   switch (pl.tn) {
-    case 16: return launch_t<QT, 16>(env, pl, w, x, y, M, K, N, residual);
-    case 32: return launch_t<QT, 32>(env, pl, w, x, y, M, K, N, residual);
-    case 48: return launch_t<QT, 48>(env, pl, w, x, y, M, K, N, residual);
-    case 64: return launch_t<QT, 64>(env, pl, w, x, y, M, K, N, residual);
+    case 16: return launch_t<QT, 16, 1>(env, pl, w, x, y, M, K, N, residual);
+    case 32: return launch_t<QT, 32, 1>(env, pl, w, x, y, M, K, N, residual);
+    case 48: return launch_t<QT, 48, 2>(env, pl, w, x, y, M, K, N, residual);
+    case 64: return launch_t<QT, 64, 2>(env, pl, w, x, y, M, K, N, residual);
     default: return cudaErrorInvalidValue;
   }
 }
