@@ -175,6 +175,10 @@ int rrr_rmsnorm_bf16(rrr_ctx* ctx, const float* x, const float* gamma, uint16_t*
 int rrr_gqa_v_bf16(rrr_ctx* ctx, const float* qkv, uint16_t* y, int rows, int n_q, int n_kv,
                    int head_dim, int k_window, int k_offset, void* stream);
 int rrr_silu_gate_bf16(rrr_ctx* ctx, const float* gu, uint16_t* y, int rows, int F, void* stream);
+/* y[m][k] = bf16(x[m][k - k_offset]) for k - k_offset in [0, n), 0 elsewhere in
+ * [0, k_window): a rank's attention output [rows, n] placed in its O-projection window. */
+int rrr_window_bf16(rrr_ctx* ctx, const float* x, uint16_t* y, int rows, int n, int k_window,
+                    int k_offset, void* stream);
 int rrr_logits_f32_batched(rrr_ctx* ctx, const float* W, const float* x, float* x_norm, float* y,
                            int M, int V, int K, const float* gamma, float eps, void* stream);
 
@@ -312,6 +316,9 @@ int rrr_attention_f16kv(rrr_ctx* ctx, const rrr_attn_desc* a, const float* q, in
 int rrr_rope_attention_f16kv(rrr_ctx* ctx, const rrr_attn_desc* a, const float* qkv, int pos0,
                              const int* d_pos, uint16_t* k_cache, uint16_t* v_cache, float* out,
                              void* stream);
+/* *d_pos += delta on the stream, after the kernels before it (the KVCache.len += 1 of the
+ * reference's decode loop for a device-resident position; capturable in a CUDA graph). */
+int rrr_position_advance(rrr_ctx* ctx, int* d_pos, int delta, void* stream);
 /* Embedding rows (Phi4Model::embed on the table dequantised by dequant_tensor_f32,
  * phi4.rs:709, 572-587, 2085-2089): out[t] = row tokens[t] of an [n_rows, d] table stored
  * as GGUF type ggml_type (0 F32, 1 F16, 6 Q5_0, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K; d a

@@ -753,6 +753,15 @@ int rrr_rope_attention_f16kv(rrr_ctx* ctx, const rrr_attn_desc* a, const float* 
   return e == cudaSuccess ? RRR_OK : cuda_error(ctx, e, "rrr_rope_attention_f16kv launch");
 }
 
+int rrr_position_advance(rrr_ctx* ctx, int* d_pos, int delta, void* stream) {
+  if (!ctx) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null context");
+  if (!d_pos) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_position_advance: null position");
+  int rc = bind_device(ctx);
+  if (rc) return rc;
+  cudaError_t e = launch_pos_advance(make_env(ctx, stream), d_pos, delta);
+  return e == cudaSuccess ? RRR_OK : cuda_error(ctx, e, "rrr_position_advance launch");
+}
+
 int rrr_embed_rows(rrr_ctx* ctx, int ggml_type, const void* table, int64_t n_rows, int d,
                    const int32_t* tokens, int n_tokens, float* out, void* stream) {
   if (!ctx) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null context");

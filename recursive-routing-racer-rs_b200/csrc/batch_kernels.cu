@@ -6,6 +6,9 @@
 //   gqa_v_bf16     y[m][k] = bf16(V of head (k - k_offset)/hd's KV group) in the head
 //                  window, 0 elsewhere (position-0 attention output, phi4.rs:1120)
 //   silu_gate_bf16 y[m][i] = bf16(silu(gate[m][i]) * up[m][i])      (phi4.rs:1359-1378)
+//   window_bf16    y[m][k] = bf16(x[m][k - k_offset]) inside the window, 0 outside (the
+//                  attention output of a tensor-parallel rank's heads placed in its
+//                  O-projection column window)
 //   logits         rows normalised in f32, then one f32 GEMM (cuBLAS SGEMM, a plain
 //                  library GEMM: W row-major [V, K] times the normalised rows)
 #include <cublas_v2.h>
@@ -76,6 +79,17 @@ __global__ void silu_gate_bf16_kernel(const float* __restrict__ gu, __nv_bfloat1
   }
 }
 
+__global__ void window_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int n,
+                                   int kwin, int koff) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int m = blockIdx.y;
+  for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < kwin; k += gridDim.x * blockDim.x) {
+    const int i = k - koff;
+    y[(int64_t)m * kwin + k] = __float2bfloat16_rn(i >= 0 && i < n ? x[(int64_t)m * n + i] : 0.f);
+  }
+}
+
 }  // namespace
 
 void destroy_cublas(void* handle) { cublasDestroy(static_cast<cublasHandle_t>(handle)); }
@@ -131,6 +145,22 @@ int rrr_silu_gate_bf16(rrr_ctx* ctx, const float* gu, uint16_t* y, int rows, int
   cudaError_t e = rrr_launch_pdl(silu_gate_bf16_kernel, dim3(grid_x(F), rows), dim3(256), 0,
                                  env.stream, env.pdl, gu, reinterpret_cast<__nv_bfloat16*>(y), F);
   return e == cudaSuccess ? RRR_OK : cuda_error(ctx, e, "rrr_silu_gate_bf16 launch");
+}
+
+int rrr_window_bf16(rrr_ctx* ctx, const float* x, uint16_t* y, int rows, int n, int k_window,
+                    int k_offset, void* stream) {
+  if (!ctx) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null context");
+  if (!x || !y) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_window_bf16: null pointer");
+  if (rows < 0 || n < 1 || k_offset < 0 || k_offset + n > k_window)
+    return set_error(ctx, RRR_ERR_BAD_SHAPE, "rrr_window_bf16: need k_offset + n <= k_window");
+  int rc = bind_device(ctx);
+  if (rc) return rc;
+  if (rows == 0) return RRR_OK;
+  const LaunchEnv env = make_env(ctx, stream);
+  cudaError_t e = rrr_launch_pdl(window_bf16_kernel, dim3(grid_x(k_window), rows), dim3(256), 0,
+                                 env.stream, env.pdl, x, reinterpret_cast<__nv_bfloat16*>(y), n,
+                                 k_window, k_offset);
+  return e == cudaSuccess ? RRR_OK : cuda_error(ctx, e, "rrr_window_bf16 launch");
 }
 
 int rrr_logits_f32_batched(rrr_ctx* ctx, const float* W, const float* x, float* x_norm, float* y,

@@ -121,6 +121,8 @@ PROTOS = {
     "rrr_phi4_launches_per_step": (c_int, [vp, POINTER(c_int)]),
     "rrr_phi4_destroy": (c_int, [vp]),
     "rrr_set_pdl": (c_int, [vp, c_int]),
+    "rrr_position_advance": (c_int, [vp, vp, c_int, vp]),
+    "rrr_window_bf16": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, vp]),
     "rrr_gemm_kq_batched_path": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, c_int, vp, c_int, vp]),
     "rrr_phi4_set_position": (c_int, [vp, c_int, vp]),
     "rrr_phi4_position": (c_int, [vp, POINTER(c_int)]),

@@ -132,6 +132,12 @@ class SyntheticPhi4TP:
         self.w_out = self.arena.alloc((v1 - v0) * d * 4)
         ctx.check(L.rrr_fill_f32_range(ctx.h, self.w_out, (v1 - v0) * d, v0 * d, 1, 0.0, 0.02,
                                        tensor_seed(seed, -1, "output"), s))
+        # LongRoPE factors, replicated (the same stream as SyntheticPhi4's)
+        self.n_rope_factors = cfg.rope_dim // 2
+        self.rope_factors = self.arena.alloc(max(1, self.n_rope_factors) * 4)
+        if self.n_rope_factors:
+            ctx.check(L.rrr_fill_f32_uniform(ctx.h, self.rope_factors, self.n_rope_factors, 1.0, 1.5,
+                                             tensor_seed(seed, -1, "rope_factors"), s))
         ctx.check(L.rrr_sync(ctx.h, s))
 
     def shard_bytes(self) -> int:
@@ -184,14 +190,23 @@ class P2PComm:
 
 
 class TPDecoder:
-    """One rank's position-0 decode step: the kernels of the 1-GPU step on the rank's
-    shards, with torch.distributed all-reduce / all-gather (NCCL) between them. The step
-    can be captured into a CUDA graph (kernels and collectives) and replayed."""
+    """One rank's decode step: the kernels of the 1-GPU step on the rank's shards, with
+    torch.distributed all-reduce / all-gather (NCCL) or the peer-memory kernels between
+    them. The step can be captured into a CUDA graph (kernels and collectives) and
+    replayed.
+
+    max_seq = 0: every token at position 0 (attention output = V; forward_batched runs M
+    independent sequences). max_seq > 0: a KV cache of the rank's KV heads (f16, max_seq
+    rows per layer) and a device position: forward decodes one token at the position and
+    advances it (RoPE, KV store and attention fused in one launch per layer);
+    forward_batched is a prefill of M consecutive tokens of one sequence (RoPE + KV store
+    of the M rows, causal attention, phi4.rs:1270-1309) and advances the position by M."""
 
     def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4TP, group=None, comm: str = "nccl",
-                 max_batch: int = 1):
+                 max_batch: int = 1, max_seq: int = 0):
         """comm: "nccl" (torch.distributed collectives) or "p2p" (rrr_comm_* kernels over
-        NVLink peer memory); max_batch: the largest M of forward_batched."""
+        NVLink peer memory); max_batch: the largest M of forward_batched; max_seq: KV-cache
+        rows (0: position-0 steps)."""
         import torch
         import torch.distributed as dist
         self.torch, self.dist = torch, dist
@@ -210,6 +225,30 @@ class TPDecoder:
         self.graph = None
         self._graph_key = None
         self._bm = 0  # batch size of the batched buffers
+        self.max_seq = max_seq
+        self.pos = 0  # host copy of the device position
+        if max_seq:
+            nq_loc = sh.q_heads[1] - sh.q_heads[0]
+            nkv_loc = sh.kv_heads[1] - sh.kv_heads[0]
+            self.kc = torch.zeros(cfg.n_layers, max_seq, nkv_loc * cfg.head_dim, dtype=torch.int16, device=dev)
+            self.vc = torch.zeros_like(self.kc)
+            self.d_pos = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.attn_desc = ffi.AttnDesc(nq_loc, nkv_loc, cfg.head_dim, cfg.rope_dim, cfg.rope_theta,
+                                          cfg.rope_attn_factor, c_void_p(weights.rope_factors),
+                                          weights.n_rope_factors, max_seq)
+            # O-projection input: the heads' attention output inside the window, zeros around
+            self.attn_in = torch.zeros(sh.o_k, device=dev)
+
+    def set_position(self, pos: int) -> None:
+        """KV-cache decode: position of the next token (KVCache.len)."""
+        if not 0 <= pos < self.max_seq:
+            raise ValueError(f"position {pos} outside the cache of {self.max_seq} rows")
+        self.d_pos.fill_(pos)
+        self.pos = pos
+
+    def _cache(self, l):
+        kv = self.kc[l].data_ptr(), self.vc[l].data_ptr()
+        return c_void_p(kv[0]), c_void_p(kv[1])
 
     def steps(self, hidden, logits, argmax, stream=None):
         """The step as a generator: launches the kernels on `stream` (default: the current
@@ -225,13 +264,24 @@ class TPDecoder:
         nq_loc = sh.q_heads[1] - sh.q_heads[0]
         nkv_loc = sh.kv_heads[1] - sh.kv_heads[0]
         qkv_p, mid_p = c_void_p(self.qkv.data_ptr()), c_void_p(self.mid.data_ptr())
+        if self.max_seq:
+            if self.pos >= self.max_seq:
+                raise ValueError(f"position {self.pos} is past the cache of {self.max_seq} rows")
+            ad, dpos = ctypes.byref(self.attn_desc), c_void_p(self.d_pos.data_ptr())
+            attn_out = c_void_p(self.attn_in.data_ptr() + 4 * sh.o_k_offset)
         for l, e in enumerate(w.layers):
             pn = ffi.GemvPrologue(1, e["attn_norm"], cfg.rms_eps, 0, 0, 0, 0)
             ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.qkv_type, c_void_p(e["qkv"]), hp, qkv_p, d,
                                        sh.qkv_dim, None, ctypes.byref(pn), st))
-            pv = ffi.GemvPrologue(3, None, 0.0, nq_loc, nkv_loc, hd, sh.o_k_offset)
-            ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.o_type, c_void_p(e["o_proj"]), qkv_p, hp, sh.o_k,
-                                       d, res, ctypes.byref(pv), st))
+            if self.max_seq:
+                kc, vc = self._cache(l)
+                ctx.check(L.rrr_rope_attention_f16kv(ctx.h, ad, qkv_p, 0, dpos, kc, vc, attn_out, st))
+                ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.o_type, c_void_p(e["o_proj"]),
+                                           c_void_p(self.attn_in.data_ptr()), hp, sh.o_k, d, res, None, st))
+            else:
+                pv = ffi.GemvPrologue(3, None, 0.0, nq_loc, nkv_loc, hd, sh.o_k_offset)
+                ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.o_type, c_void_p(e["o_proj"]), qkv_p, hp, sh.o_k,
+                                           d, res, ctypes.byref(pv), st))
             if sh.G > 1:
                 yield ("all_reduce", hidden)
             pf = ffi.GemvPrologue(1, e["ffn_norm"], cfg.rms_eps, 0, 0, 0, 0)
@@ -249,6 +299,9 @@ class TPDecoder:
         if argmax is not None:
             ctx.check(L.rrr_argmax_f32(ctx.h, c_void_p(logits.data_ptr()), cfg.vocab_size,
                                        c_void_p(argmax.data_ptr()), st))
+        if self.max_seq:
+            ctx.check(L.rrr_position_advance(ctx.h, c_void_p(self.d_pos.data_ptr()), 1, st))
+            self.pos += 1
 
     def _issue(self, hidden, logits, argmax):
         """The step with its exchanges as torch.distributed collectives (NCCL) or as the
@@ -276,13 +329,16 @@ class TPDecoder:
         self.b_mid = torch.empty(M, sh.ffn_dim, dtype=torch.int16, device=dev)       # bf16 bits
         self.b_xnorm = torch.empty(M, cfg.d_model, device=dev)
         self.b_logits_loc = torch.empty(M, sh.vocab_rows, device=dev)
+        if self.max_seq:
+            self.b_attn = torch.empty(M, (sh.q_heads[1] - sh.q_heads[0]) * cfg.head_dim, device=dev)
         self._bm = M
 
     def steps_batched(self, hidden, logits, M: int, stream=None):
-        """M tokens at position 0 (the batched-prefill call sites, phi4.rs:1198-1445, with
-        every GEMM on the tensor cores): hidden f32 [M, d] (in/out), logits f32 [M, vocab].
-        Yields at each exchange like steps(); the logits exchange is ("all_gather_rows",
-        out [M, vocab], part [M, vocab/G], M)."""
+        """M tokens (the batched-prefill call sites, phi4.rs:1198-1445, with every GEMM on
+        the tensor cores): at position 0 each (max_seq = 0), or a prefill of M consecutive
+        positions from the current one (max_seq > 0). hidden f32 [M, d] (in/out), logits
+        f32 [M, vocab]. Yields at each exchange like steps(); the logits exchange is
+        ("all_gather_rows", out [M, vocab], part [M, vocab/G], M)."""
         L, ctx, cfg, sh, w = ffi.lib(), self.ctx, self.w.cfg, self.w.shard, self.w
         torch = self.torch
         self._ensure_batch(M)
@@ -294,11 +350,23 @@ class TPDecoder:
         nkv_loc = sh.kv_heads[1] - sh.kv_heads[0]
         xn, qkv, a = c_void_p(self.b_xn.data_ptr()), c_void_p(self.b_qkv.data_ptr()), c_void_p(self.b_a.data_ptr())
         gu, mid = c_void_p(self.b_gu.data_ptr()), c_void_p(self.b_mid.data_ptr())
+        if self.max_seq:
+            if self.pos + M > self.max_seq:
+                raise ValueError(f"positions {self.pos}..{self.pos + M - 1} exceed the cache of "
+                                 f"{self.max_seq} rows")
+            ad, dpos = ctypes.byref(self.attn_desc), c_void_p(self.d_pos.data_ptr())
+            att = c_void_p(self.b_attn.data_ptr())
         for l, e in enumerate(w.layers):
             ctx.check(L.rrr_rmsnorm_bf16(ctx.h, hp, c_void_p(e["attn_norm"]), xn, M, d, cfg.rms_eps, st))
             ctx.check(L.rrr_gemm_kq_batched(ctx.h, cfg.qkv_type, c_void_p(e["qkv"]), xn, qkv, M, d,
                                             sh.qkv_dim, st))
-            ctx.check(L.rrr_gqa_v_bf16(ctx.h, qkv, a, M, nq_loc, nkv_loc, hd, sh.o_k, sh.o_k_offset, st))
+            if self.max_seq:
+                kc, vc = self._cache(l)
+                ctx.check(L.rrr_rope_kv_store(ctx.h, ad, qkv, sh.qkv_dim, M, 0, dpos, kc, vc, st))
+                ctx.check(L.rrr_attention_f16kv(ctx.h, ad, qkv, sh.qkv_dim, M, 0, dpos, kc, vc, att, st))
+                ctx.check(L.rrr_window_bf16(ctx.h, att, a, M, nq_loc * hd, sh.o_k, sh.o_k_offset, st))
+            else:
+                ctx.check(L.rrr_gqa_v_bf16(ctx.h, qkv, a, M, nq_loc, nkv_loc, hd, sh.o_k, sh.o_k_offset, st))
             ctx.check(L.rrr_gemm_kq_batched_ex(ctx.h, cfg.o_type, c_void_p(e["o_proj"]), a, hp, M, sh.o_k,
                                                d, res, st))
             if sh.G > 1:
@@ -316,7 +384,10 @@ class TPDecoder:
                                            c_void_p(lp.data_ptr()), M, sh.vocab_rows, d,
                                            c_void_p(w.output_norm), cfg.rms_eps, st))
         if sh.G > 1:
-            yield ("all_gather_rows", logits, self.b_logits_loc, M)
+            yield ("all_gather_rows", logits, self.b_logits_loc[:M], M)
+        if self.max_seq:
+            ctx.check(L.rrr_position_advance(ctx.h, dpos, M, st))
+            self.pos += M
 
     def _exchange(self, op, st) -> None:
         dist = self.dist
@@ -349,9 +420,13 @@ class TPDecoder:
                 self._exchange(op, st)
             return
         key = ("b", hidden.data_ptr(), logits.data_ptr(), M)
+        if self.max_seq and self.pos + M > self.max_seq:
+            raise ValueError(f"positions {self.pos}..{self.pos + M - 1} exceed the cache of "
+                             f"{self.max_seq} rows")
         if self.graph is None or self._graph_key != key:
             self.release_graph()
             saved = hidden.clone()
+            p0 = self.pos
             s = torch.cuda.Stream()
             s.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(s):
@@ -359,19 +434,26 @@ class TPDecoder:
                     self._exchange(op, c_void_p(s.cuda_stream))
             torch.cuda.current_stream().wait_stream(s)
             hidden.copy_(saved)
+            if self.max_seq:  # the warm-up wrote these positions' cache rows: run them again
+                self.set_position(p0)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, capture_error_mode="relaxed"):
                 st = c_void_p(torch.cuda.current_stream().cuda_stream)
                 for op in self.steps_batched(hidden, logits, M):
                     self._exchange(op, st)
+            self.pos = p0
             self.graph, self._graph_key = g, key
         self.graph.replay()
+        if self.max_seq:
+            self.pos += M
 
     def launches_per_step(self) -> int:
         """Kernels of this library per step (NCCL collectives not counted; the peer-memory
         exchanges are)."""
         cfg = self.w.cfg
         n = 4 * cfg.n_layers + -(-self.w.shard.vocab_rows // cfg.logits_chunk_rows) + 1
+        if self.max_seq:
+            n += cfg.n_layers + 1  # fused RoPE + KV + attention per layer, position advance
         if self.p2p is not None:
             n += 2 * cfg.n_layers + 1
         return n
@@ -385,9 +467,12 @@ class TPDecoder:
             return
         torch = self.torch
         key = (hidden.data_ptr(), logits.data_ptr(), None if argmax is None else argmax.data_ptr())
+        if self.max_seq and self.pos >= self.max_seq:
+            raise ValueError(f"position {self.pos} is past the cache of {self.max_seq} rows")
         if self.graph is None or self._graph_key != key:
             self.release_graph()
             saved = hidden.clone()
+            p0 = self.pos
             s = torch.cuda.Stream()
             s.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(s):
@@ -395,11 +480,16 @@ class TPDecoder:
                 self._issue(hidden, logits, argmax)
             torch.cuda.current_stream().wait_stream(s)
             hidden.copy_(saved)
+            if self.max_seq:  # the warm-up wrote this position's cache row: decode it again
+                self.set_position(p0)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, capture_error_mode="relaxed"):
                 self._issue(hidden, logits, argmax)
+            self.pos = p0
             self.graph, self._graph_key = g, key
         self.graph.replay()
+        if self.max_seq:
+            self.pos += 1
 
     def release_graph(self) -> None:
         """Drop the captured graph (it holds NCCL calls: release it before the process

@@ -145,3 +145,91 @@ def test_batched_step_tp2_emulated(rrr, ctx, oracle):
             assert _rel(H[m], Hr[m]) < BF16_TOL and _rel(LG[m], LGr[m]) < BF16_TOL
     for w in ws + [w1]:
         w.close()
+
+
+ROPE = dict(rope_dim=96, theta=10000.0, attn_factor=1.190238)
+
+
+def _bf16_reference_kv(oracle, layers, on, wo, H0, torch, pos0, kc, vc, fac):
+    """Prefill of M consecutive tokens at positions pos0.. with the step's bf16 roundings
+    made explicit (GEMM inputs rounded to bf16, exact weights: M < 16 runs one GEMV per
+    token): per layer the QKV rows, RoPE + f16 KV store of every row, causal attention of
+    each row over the cache, then O / FFN as _bf16_reference. kc / vc (uint16 [L, S, kvs])
+    are updated."""
+    c = SMALL
+    d, F, hd, nq, nkv = c["d_model"], c["ffn_dim"], c["head_dim"], c["n_heads"], c["n_kv_heads"]
+    qkv_dim, kvs = (nq + 2 * nkv) * hd, nkv * hd
+    H = H0.astype(np.float32).copy()
+    M = H.shape[0]
+
+    def rms(x, g):
+        return np.stack([oracle.rms_norm(r, g, c["eps"]) for r in x])
+
+    def W(L, key, qt, K, N):
+        return oracle.dequant(qt, L[key], N * K).reshape(N, K).astype(np.float64)
+
+    for li, L in enumerate(layers):
+        xn = _bf16(rms(H, L["attn_norm"]), torch).astype(np.float64)
+        qkv = (xn @ W(L, "w_qkv", L["qkv_type"], d, qkv_dim).T).astype(np.float32)
+        A = np.empty((M, nq * hd), np.float32)
+        qs = []
+        for t in range(M):
+            q = oracle.rope(qkv[t, :nq * hd], pos0 + t, nq, hd, ROPE["rope_dim"], ROPE["theta"],
+                            ROPE["attn_factor"], fac)
+            k = oracle.rope(qkv[t, nq * hd:nq * hd + kvs], pos0 + t, nkv, hd, ROPE["rope_dim"],
+                            ROPE["theta"], ROPE["attn_factor"], fac)
+            kc[li, pos0 + t] = oracle.f32_to_f16_bits(k)
+            vc[li, pos0 + t] = oracle.f32_to_f16_bits(qkv[t, nq * hd + kvs:])
+            qs.append(q)
+        for t in range(M):
+            A[t] = oracle.attention_f16kv(qs[t], kc[li], vc[li], pos0 + t + 1, nq, nkv, hd)
+        H = (H + _bf16(A, torch).astype(np.float64) @ W(L, "w_o", L["o_type"], nq * hd, d).T).astype(np.float32)
+        xn = _bf16(rms(H, L["ffn_norm"]), torch).astype(np.float64)
+        gu = (xn @ W(L, "w_gate_up", L["gate_up_type"], d, 2 * F).T).astype(np.float32)
+        mid = np.stack([oracle.silu_gate(r) for r in gu])
+        H = (H + _bf16(mid, torch).astype(np.float64) @ W(L, "w_down", L["down_type"], F, d).T).astype(np.float32)
+    LG = (rms(H, on).astype(np.float64) @ wo.astype(np.float64).T).astype(np.float32)
+    return H, LG
+
+
+@pytest.mark.parametrize("G", [1, 2])
+def test_prefill_with_positions(rrr, ctx, oracle, G):
+    """Prefill of 5 tokens at positions 0-4, then 3 more at 5-7 (KV cache, RoPE, causal
+    attention over the cache), one GPU (G = 1, graph for the second chunk) and an emulated
+    G = 2 split, against the bf16-aware reference with the oracle's RoPE / attention."""
+    import torch
+    cfg = _cfg()
+    max_seq = 16
+    w1 = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, 1, 0), seed=23)
+    layers, on, wo = _host_model(oracle, w1, torch)
+    fac = np.empty(w1.n_rope_factors, np.float32)
+    ctx.check(tp.ffi.lib().rrr_d2h(ctx.h, c_void_p(fac.ctypes.data), c_void_p(w1.rope_factors), fac.nbytes, None))
+    ws = [tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, G, g), seed=23) for g in range(G)]
+    decs = [tp.TPDecoder(ctx, w, max_batch=8, max_seq=max_seq) for w in ws]
+    kvs = SMALL["n_kv_heads"] * SMALL["head_dim"]
+    kc = np.zeros((SMALL["n_layers"], max_seq, kvs), np.uint16)
+    vc = np.zeros_like(kc)
+    torch.manual_seed(31 + G)
+    pos0 = 0
+    for M in (5, 3):
+        hidden0 = torch.randn(M, cfg.d_model, device="cuda")
+        hs = [hidden0.clone() for _ in range(G)]
+        lgs = [torch.empty(M, cfg.vocab_size, device="cuda") for _ in range(G)]
+        if G == 1:
+            decs[0].forward_batched(hs[0], lgs[0], M, use_graph=(M == 3))
+        else:
+            tp.emulate_step(decs, hs, lgs, batch=M)
+        torch.cuda.synchronize()
+        assert ctx.device_error() == 0
+        Hr, LGr = _bf16_reference_kv(oracle, layers, on, wo, hidden0.cpu().numpy(), torch, pos0, kc, vc, fac)
+        for g in range(G):
+            H, LG = hs[g].cpu().numpy(), lgs[g].cpu().numpy()
+            for m in range(M):
+                assert _rel(H[m], Hr[m]) < BF16_TOL, (G, g, pos0 + m, _rel(H[m], Hr[m]))
+                assert _rel(LG[m], LGr[m]) < BF16_TOL
+            assert decs[g].pos == pos0 + M
+        pos0 += M
+    for dec in decs:
+        dec.close()
+    for w in ws + [w1]:
+        w.close()

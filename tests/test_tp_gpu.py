@@ -85,6 +85,42 @@ def test_tp_split_emulated_matches_single_gpu(rrr, ctx, G):
         w.close()
 
 
+@pytest.mark.parametrize("G", [2, 8])
+def test_tp_kv_decode_emulated_matches_single_gpu(rrr, ctx, G):
+    """KV-cache decode at positions 0..3 (RoPE, f16 caches of the rank's KV heads, fused
+    attention; the O-projection input is the heads' attention output in the rank's column
+    window): the emulated G-rank split equals the 1-GPU rrr_phi4_forward KV step."""
+    import torch
+    cfg = phi4.ModelConfig(n_layers=2)
+    seed, max_seq = 13, 32
+    m = phi4.SyntheticPhi4(ctx, cfg, seed=seed)
+    dec1 = phi4.Phi4Decoder(ctx, m, max_seq=max_seq)
+    ws = [tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, G, g), seed=seed) for g in range(G)]
+    decs = [tp.TPDecoder(ctx, w, max_seq=max_seq) for w in ws]
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    lg1 = torch.empty(cfg.vocab_size, device="cuda")
+    am1 = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for pos in range(4):
+        hidden0 = torch.randn(cfg.d_model, device="cuda", generator=gen)
+        h1 = hidden0.clone()
+        dec1.forward(h1.data_ptr(), lg1.data_ptr(), am1.data_ptr(), False)
+        hs = [hidden0.clone() for _ in range(G)]
+        lgs = [torch.empty(cfg.vocab_size, device="cuda") for _ in range(G)]
+        ams = [torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(G)]
+        tp.emulate_step(decs, hs, lgs, ams)
+        torch.cuda.synchronize()
+        assert ctx.device_error() == 0
+        for g in range(G):
+            assert _rel(hs[g].cpu().numpy(), h1.cpu().numpy()) < 1e-4, (pos, g)
+            assert _rel(lgs[g].cpu().numpy(), lg1.cpu().numpy()) < 1e-4
+            assert int(ams[g].item()) == int(am1.item())
+            assert decs[g].pos == pos + 1
+    dec1.close()
+    m.close()
+    for w in ws:
+        w.close()
+
+
 # ------------------------------------------------------------------ NCCL, 2 GPUs
 def _free_port():
     with socket.socket() as s:
