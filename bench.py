@@ -393,6 +393,20 @@ def run_ours(args, rank, world, local_rank):
 
         tms, tl_p2p = time_tp("p2p")
         tms_nccl, _ = time_tp("nccl")
+        # at real positions: KV caches of the rank's heads, positions 1024 .. 1024 + steps
+        kdec = tpm.TPDecoder(ctx, tw, comm="p2p", max_seq=2048)
+        kdec.set_position(1024 - max(3, args.warmup))
+        for _ in range(max(3, args.warmup)):
+            kdec.forward(th, tl, ta, use_graph=True)
+        barrier()
+        t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0e.record(stream)
+        for _ in range(dsteps):
+            kdec.forward(th, tl, ta, use_graph=True)
+        t1e.record(stream)
+        barrier()
+        tkms = max_over_ranks(t0e.elapsed_time(t1e) / dsteps)
+        kdec.close()
         # batch 64 over the ranks (peer-memory exchanges of [64, 3072] and [64, V/G])
         tb = tpm.TPDecoder(ctx, tw, comm="p2p", max_batch=BM)
         tbh = torch.randn(BM, cfg.d_model, device="cuda")
@@ -412,6 +426,7 @@ def run_ours(args, rank, world, local_rank):
                      "exchange": "rrr_comm peer-memory kernels over NVLink (all-reduce x2 per layer "
                                  "+ logits all-gather)",
                      "tok_s_nccl": round(1e3 / tms_nccl, 2),
+                     "kv_tok_s": round(1e3 / tkms, 2), "kv_positions": [1024, 1024 + dsteps],
                      "batch64_tok_s": round(BM * 1e3 / tbms, 1), "batch64_ms_per_step": round(tbms, 4),
                      "bytes_per_rank": tw.shard_bytes(),
                      "GBps_per_rank": round(tw.shard_bytes() / tms / 1e6, 1),

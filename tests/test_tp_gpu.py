@@ -128,7 +128,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_rank(rank, world, port, q, comm):
+def _nccl_rank(rank, world, port, q, comm, max_seq=0):
     import datetime
     import torch
     import torch.distributed as dist
@@ -145,7 +145,7 @@ def _nccl_rank(rank, world, port, q, comm):
         gen = torch.Generator(device="cuda").manual_seed(5)
         hidden0 = torch.randn(cfg.d_model, device="cuda", generator=gen)
         w = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, world, rank), seed=seed)
-        dec = tp.TPDecoder(ctx, w, comm=comm)
+        dec = tp.TPDecoder(ctx, w, comm=comm, max_seq=max_seq)
         lg = torch.empty(cfg.vocab_size, device="cuda")
         am = torch.zeros(1, dtype=torch.int32, device="cuda")
         results = []
@@ -156,8 +156,23 @@ def _nccl_rank(rank, world, port, q, comm):
             results.append((h.cpu().numpy(), lg.cpu().numpy(), int(am.item())))
         dec.close()
         if rank == 0:
-            h1, lg1, am1 = _single_gpu(ctx, cfg, seed, hidden0)
-            q.put([(_rel(h, h1), _rel(lgr, lg1), a == am1) for h, lgr, a in results]
+            if max_seq:
+                # the same three tokens (positions 0, 1, 2) through the 1-GPU KV step
+                m = phi4.SyntheticPhi4(ctx, cfg, seed=seed)
+                d1 = phi4.Phi4Decoder(ctx, m, max_seq=max_seq)
+                refs = []
+                for _ in range(3):
+                    h = hidden0.clone()
+                    lg1 = torch.empty(cfg.vocab_size, device="cuda")
+                    am1 = torch.zeros(1, dtype=torch.int32, device="cuda")
+                    d1.forward(h.data_ptr(), lg1.data_ptr(), am1.data_ptr(), False)
+                    torch.cuda.synchronize()
+                    refs.append((h.cpu().numpy(), lg1.cpu().numpy(), int(am1.item())))
+                d1.close()
+                m.close()
+            else:
+                refs = [_single_gpu(ctx, cfg, seed, hidden0)] * 3
+            q.put([(_rel(h, r[0]), _rel(lgr, r[1]), a == r[2]) for (h, lgr, a), r in zip(results, refs)]
                   + [ctx.device_error()])
         w.close()
     finally:
@@ -166,9 +181,11 @@ def _nccl_rank(rank, world, port, q, comm):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("comm", ["nccl", "p2p"])
-def test_tp_nccl_two_gpus(comm):
-    """comm = nccl: torch.distributed collectives; p2p: the rrr_comm_* peer-memory kernels."""
+@pytest.mark.parametrize("comm,max_seq", [("nccl", 0), ("p2p", 0), ("nccl", 16), ("p2p", 16)])
+def test_tp_nccl_two_gpus(comm, max_seq):
+    """comm = nccl: torch.distributed collectives; p2p: the rrr_comm_* peer-memory kernels.
+    max_seq > 0: three decode steps at positions 0, 1, 2 with the KV caches (eager, then
+    captured and replayed), against the 1-GPU KV step."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -176,7 +193,7 @@ def test_tp_nccl_two_gpus(comm):
     mpc = mp.get_context("spawn")
     q = mpc.Queue()
     port = _free_port()
-    procs = [mpc.Process(target=_nccl_rank, args=(r, 2, port, q, comm)) for r in range(2)]
+    procs = [mpc.Process(target=_nccl_rank, args=(r, 2, port, q, comm, max_seq)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
