@@ -362,7 +362,7 @@ def run_ours(args, rank, world, local_rank):
     bms = max_over_ranks(b0e.elapsed_time(b1e) / bsteps)
     decode_batch = {"batch": BM, "tok_s": round(BM * 1e3 / bms, 1), "ms_per_step": round(bms, 4),
                     "graph": True, "path": "per layer: rmsnorm->bf16, 4 tcgen05 GEMMs (residual in "
-                                           "the epilogue), GQA-V / SiLU glue; logits f32 SGEMM"}
+                                           "the epilogue), GQA-V / SiLU glue; logits on TF32 tensor cores (cuBLAS)"}
     bdec.close()
     bw.close()
     # ---------------- tensor-parallel decode step (configs[4], batch 1) over all ranks

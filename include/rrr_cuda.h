@@ -179,6 +179,10 @@ int rrr_silu_gate_bf16(rrr_ctx* ctx, const float* gu, uint16_t* y, int rows, int
  * [0, k_window): a rank's attention output [rows, n] placed in its O-projection window. */
 int rrr_window_bf16(rrr_ctx* ctx, const float* x, uint16_t* y, int rows, int n, int k_window,
                     int k_offset, void* stream);
+/* Logits of M rows: x_norm[m] = rms_norm(x[m]) * gamma (gamma NULL: x used as is), then
+ * y[m][v] = W[v] . x_norm[m] for a row-major f32 [V, K] W. One library GEMM; with 16+
+ * rows on the TF32 tensor cores (f32 storage and accumulation, 10-bit-mantissa products:
+ * the batched path's tensor-core tolerance), fewer rows in plain f32. */
 int rrr_logits_f32_batched(rrr_ctx* ctx, const float* W, const float* x, float* x_norm, float* y,
                            int M, int V, int K, const float* gamma, float eps, void* stream);
 

@@ -9,8 +9,9 @@
 //   window_bf16    y[m][k] = bf16(x[m][k - k_offset]) inside the window, 0 outside (the
 //                  attention output of a tensor-parallel rank's heads placed in its
 //                  O-projection column window)
-//   logits         rows normalised in f32, then one f32 GEMM (cuBLAS SGEMM, a plain
-//                  library GEMM: W row-major [V, K] times the normalised rows)
+//   logits         rows normalised in f32, then one GEMM (cuBLAS SGEMM, a plain library
+//                  GEMM: W row-major [V, K] times the normalised rows), on the TF32 tensor
+//                  cores for 16+ rows (f32 storage and accumulation)
 #include <cublas_v2.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -186,6 +187,11 @@ int rrr_logits_f32_batched(rrr_ctx* ctx, const float* W, const float* x, float* 
   cublasHandle_t h = static_cast<cublasHandle_t>(ctx->cublas);
   if (cublasSetStream(h, static_cast<cudaStream_t>(stream)) != CUBLAS_STATUS_SUCCESS)
     return set_error(ctx, RRR_ERR_CUDA, "rrr_logits_f32_batched: cublasSetStream failed");
+  // 16+ rows: TF32 tensor cores (f32 storage and accumulation, 10-bit-mantissa products),
+  // the tensor-core tolerance of the batched path; fewer rows stay on the f32 pipes
+  if (cublasSetMathMode(h, M >= 16 ? CUBLAS_TF32_TENSOR_OP_MATH : CUBLAS_DEFAULT_MATH) !=
+      CUBLAS_STATUS_SUCCESS)
+    return set_error(ctx, RRR_ERR_CUDA, "rrr_logits_f32_batched: cublasSetMathMode failed");
   // column-major view: Y^T [V, M] = (W row-major [V, K] as col-major [K, V])^T * X^T [K, M]
   const float one = 1.f, zero = 0.f;
   if (cublasSgemm(h, CUBLAS_OP_T, CUBLAS_OP_N, V, M, K, &one, W, K, xin, K, &zero, y, V) !=
