@@ -6,7 +6,7 @@ device error flag and prints "<case> ok". Sizes are the Phi-4-mini layer shapes,
 DRAM figures of a capture are those of the bench's per-GEMV lines.
 
     python -m recursive-routing-racer-rs_b200.profcases gemv            # 3 GEMV shapes x 6
-    python -m recursive-routing-racer-rs_b200.profcases decode --layers 32
+    python -m recursive-routing-racer-rs_b200.profcases decode --layers 32 [--max-seq 2048 --pos 1024]
     python -m recursive-routing-racer-rs_b200.profcases gemm --m 256    # batched tcgen05 GEMM
     python -m recursive-routing-racer-rs_b200.profcases attn --pos 1024 # RoPE + KV + attention
 """
@@ -40,11 +40,14 @@ def case_gemv(ctx, L, torch, args):
 
 
 def case_decode(ctx, L, torch, args):
-    """Eager decode steps of the synthetic Phi-4-mini model (136 launches per step at 32 layers)."""
+    """Eager decode steps of the synthetic Phi-4-mini model (136 launches per step at 32
+    layers); --max-seq > 0: the KV-cache step at positions ending at --pos (169 launches)."""
     phi4 = importlib.import_module(_PKG + ".phi4")
     cfg = phi4.ModelConfig(n_layers=args.layers)
     m = phi4.SyntheticPhi4(ctx, cfg, seed=5)
-    dec = phi4.Phi4Decoder(ctx, m)
+    dec = phi4.Phi4Decoder(ctx, m, max_seq=args.max_seq)
+    if args.max_seq:
+        dec.set_position(max(0, args.pos - args.rounds))
     h = torch.randn(cfg.d_model, device="cuda")
     lg = torch.empty(cfg.vocab_size, device="cuda")
     am = torch.zeros(1, dtype=torch.int32, device="cuda")
@@ -98,6 +101,7 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--m", type=int, default=256)
     ap.add_argument("--pos", type=int, default=1024)
+    ap.add_argument("--max-seq", type=int, default=0)
     args = ap.parse_args(argv)
     import torch
     rrr = importlib.import_module(_PKG)
