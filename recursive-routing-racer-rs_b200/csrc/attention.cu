@@ -33,7 +33,6 @@
 namespace rrr {
 namespace {
 
-constexpr int kDevErrPosition = 6;  // a position outside the cache, or a token id outside the table
 constexpr int kAttnThreads = 256;
 constexpr int kMaxHpk = 8;          // query heads per KV head
 constexpr int kMaxSplits = 16;

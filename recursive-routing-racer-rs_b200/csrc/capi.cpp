@@ -82,6 +82,70 @@ static inline bool overlap(const void* a, size_t an, const void* b, size_t bn) {
     if (_e != cudaSuccess) return cuda_error(ctx, _e, what); \
   } while (0)
 
+namespace rrr {
+
+static int check_qtype(rrr_ctx* ctx, int qtype, const char* fn) {
+  if (qtype != RRR_Q4_K && qtype != RRR_Q5_K && qtype != RRR_Q6_K)
+    return set_error(ctx, RRR_ERR_BAD_QTYPE,
+                     "%s: qtype %d is not a supported K-quant (12=Q4_K, 13=Q5_K, 14=Q6_K)", fn,
+                     qtype);
+  return RRR_OK;
+}
+
+// Bytes of the GEMV input that a prologue mode reads.
+static size_t gemv_x_bytes(int K, const rrr_gemv_prologue* pro) {
+  const int mode = pro ? pro->mode : RRR_X_PLAIN;
+  if (mode == RRR_X_SILU_GATE) return 8 * (size_t)K;
+  if (mode == RRR_X_GQA_V)
+    return 4 * (size_t)(pro->n_q_heads + 2 * pro->n_kv_heads) * pro->head_dim;
+  return 4 * (size_t)K;
+}
+
+int check_gemv(rrr_ctx* ctx, int qtype, const void* w, const float* x, float* y, int K, int N,
+               const float* residual, const rrr_gemv_prologue* pro, bool swiglu) {
+  const char* fn = swiglu ? "rrr_gemv_kq_swiglu" : "rrr_gemv_kq";
+  int rc = check_qtype(ctx, qtype, fn);
+  if (rc) return rc;
+  if (!w || !x || !y) return set_error(ctx, RRR_ERR_INVALID_ARG, "%s: null pointer", fn);
+  if (K < 256 || K % 256 != 0 || K > kGemvMaxK || N < 1)
+    return set_error(ctx, RRR_ERR_BAD_SHAPE,
+                     "%s: need K %% 256 == 0, 256 <= K <= %d, %s >= 1 (K=%d %s=%d)", fn,
+                     kGemvMaxK, swiglu ? "F" : "N", K, swiglu ? "F" : "N", N);
+  const int mode = pro ? pro->mode : RRR_X_PLAIN;
+  if (swiglu && (mode != RRR_X_PLAIN && mode != RRR_X_RMSNORM))
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "%s: prologue must be PLAIN or RMSNORM", fn);
+  if (swiglu && residual)
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "%s: no residual with the SwiGLU epilogue", fn);
+  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(y, 4) || (residual && !aligned(residual, 4)))
+    return set_error(ctx, RRR_ERR_MISALIGNED,
+                     "%s: W and x must be 16-byte aligned, y/residual 4-byte aligned", fn);
+  if (mode == RRR_X_RMSNORM) {
+    if (!pro->gamma)
+      return set_error(ctx, swiglu ? RRR_ERR_MISALIGNED : RRR_ERR_INVALID_ARG,
+                       "%s: RMSNORM needs gamma", fn);
+    if (!aligned(pro->gamma, 16))
+      return set_error(ctx, RRR_ERR_MISALIGNED, "%s: gamma must be 16-byte aligned", fn);
+  } else if (mode == RRR_X_GQA_V) {
+    const int nq = pro->n_q_heads, nkv = pro->n_kv_heads, hd = pro->head_dim;
+    const int ko = pro->k_offset;
+    if (nq <= 0 || nkv <= 0 || hd <= 0 || nq % nkv != 0 || hd % 8 != 0 || ko < 0 || ko % 8 != 0 ||
+        ko + nq * hd > K)
+      return set_error(ctx, RRR_ERR_BAD_SHAPE,
+                       "%s: GQA_V needs n_q %% n_kv == 0, head_dim %% 8 == 0, "
+                       "k_offset %% 8 == 0 and k_offset + n_q*head_dim <= K "
+                       "(n_q=%d n_kv=%d hd=%d k_offset=%d K=%d)", fn, nq, nkv, hd, ko, K);
+  } else if (mode != RRR_X_PLAIN && mode != RRR_X_SILU_GATE) {
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "%s: unknown prologue mode %d", fn, mode);
+  }
+  if (overlap(y, (size_t)N * 4, x, gemv_x_bytes(K, pro)))
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "%s: y must not overlap the input", fn);
+  if (residual && residual != y && overlap(y, (size_t)N * 4, residual, (size_t)N * 4))
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "%s: residual must equal y or not overlap it", fn);
+  return RRR_OK;
+}
+
+}  // namespace rrr
+
 extern "C" {
 
 int rrr_abi_version(void) { return RRR_ABI_VERSION; }
@@ -264,53 +328,11 @@ int rrr_device_sm_count(rrr_ctx* ctx, int* sms) {
 }
 
 // ------------------------------------------------------------------ GEMV
-static int check_qtype(rrr_ctx* ctx, int qtype, const char* fn) {
-  if (qtype != RRR_Q4_K && qtype != RRR_Q5_K && qtype != RRR_Q6_K)
-    return set_error(ctx, RRR_ERR_BAD_QTYPE,
-                     "%s: qtype %d is not a supported K-quant (12=Q4_K, 13=Q5_K, 14=Q6_K)", fn,
-                     qtype);
-  return RRR_OK;
-}
-
 int rrr_gemv_kq_ex(rrr_ctx* ctx, int qtype, const void* w, const float* x, float* y, int K,
                    int N, const float* residual, const rrr_gemv_prologue* pro, void* stream) {
   RRR_CHECK_CTX(ctx);
-  int rc = check_qtype(ctx, qtype, "rrr_gemv_kq");
+  int rc = check_gemv(ctx, qtype, w, x, y, K, N, residual, pro, false);
   if (rc) return rc;
-  if (!w || !x || !y) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq: null pointer");
-  if (K < 256 || K % 256 != 0 || K > kGemvMaxK || N < 1)
-    return set_error(ctx, RRR_ERR_BAD_SHAPE,
-                     "rrr_gemv_kq: need K %% 256 == 0, 256 <= K <= %d, N >= 1 (K=%d N=%d)",
-                     kGemvMaxK, K, N);
-  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(y, 4) || (residual && !aligned(residual, 4)))
-    return set_error(ctx, RRR_ERR_MISALIGNED,
-                     "rrr_gemv_kq: W and x must be 16-byte aligned, y/residual 4-byte aligned");
-  const int mode = pro ? pro->mode : RRR_X_PLAIN;
-  size_t x_elems = (size_t)K;
-  if (mode == RRR_X_RMSNORM) {
-    if (!pro->gamma) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq: RMSNORM needs gamma");
-    if (!aligned(pro->gamma, 16))
-      return set_error(ctx, RRR_ERR_MISALIGNED, "rrr_gemv_kq: gamma must be 16-byte aligned");
-  } else if (mode == RRR_X_SILU_GATE) {
-    x_elems = 2 * (size_t)K;
-  } else if (mode == RRR_X_GQA_V) {
-    const int nq = pro->n_q_heads, nkv = pro->n_kv_heads, hd = pro->head_dim;
-    const int ko = pro->k_offset;
-    if (nq <= 0 || nkv <= 0 || hd <= 0 || nq % nkv != 0 || hd % 8 != 0 || ko < 0 || ko % 8 != 0 ||
-        ko + nq * hd > K)
-      return set_error(ctx, RRR_ERR_BAD_SHAPE,
-                       "rrr_gemv_kq: GQA_V needs n_q %% n_kv == 0, head_dim %% 8 == 0, "
-                       "k_offset %% 8 == 0 and k_offset + n_q*head_dim <= K "
-                       "(n_q=%d n_kv=%d hd=%d k_offset=%d K=%d)", nq, nkv, hd, ko, K);
-    x_elems = (size_t)(nq + 2 * nkv) * hd;
-  } else if (mode != RRR_X_PLAIN) {
-    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq: unknown prologue mode %d", mode);
-  }
-  if (overlap(y, (size_t)N * 4, x, x_elems * 4))
-    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq: y must not overlap the input");
-  if (residual && residual != y && overlap(y, (size_t)N * 4, residual, (size_t)N * 4))
-    return set_error(ctx, RRR_ERR_INVALID_ARG,
-                     "rrr_gemv_kq: residual must equal y or not overlap it");
   RRR_BIND(ctx);
   RRR_LAUNCH_CHECK(ctx, launch_gemv_kq(make_env(ctx, stream), qtype, w, x, y, K, N, residual, pro),
                    "rrr_gemv_kq launch");
@@ -325,21 +347,8 @@ int rrr_gemv_kq(rrr_ctx* ctx, int qtype, const void* w, const float* x, float* y
 int rrr_gemv_kq_swiglu(rrr_ctx* ctx, int qtype, const void* w, const float* x, float* y, int K,
                        int F, const rrr_gemv_prologue* pro, void* stream) {
   RRR_CHECK_CTX(ctx);
-  int rc = check_qtype(ctx, qtype, "rrr_gemv_kq_swiglu");
+  int rc = check_gemv(ctx, qtype, w, x, y, K, F, nullptr, pro, true);
   if (rc) return rc;
-  if (!w || !x || !y) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq_swiglu: null pointer");
-  if (K < 256 || K % 256 != 0 || K > kGemvMaxK || F < 1)
-    return set_error(ctx, RRR_ERR_BAD_SHAPE,
-                     "rrr_gemv_kq_swiglu: need K %% 256 == 0, 256 <= K <= %d, F >= 1", kGemvMaxK);
-  const int mode = pro ? pro->mode : RRR_X_PLAIN;
-  if (mode != RRR_X_PLAIN && mode != RRR_X_RMSNORM)
-    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq_swiglu: prologue must be PLAIN or RMSNORM");
-  if (mode == RRR_X_RMSNORM && (!pro->gamma || !aligned(pro->gamma, 16)))
-    return set_error(ctx, RRR_ERR_MISALIGNED, "rrr_gemv_kq_swiglu: gamma missing or not 16-byte aligned");
-  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(y, 4))
-    return set_error(ctx, RRR_ERR_MISALIGNED, "rrr_gemv_kq_swiglu: W and x 16-byte, y 4-byte aligned");
-  if (overlap(y, (size_t)F * 4, x, (size_t)K * 4))
-    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemv_kq_swiglu: y must not overlap x");
   RRR_BIND(ctx);
   RRR_LAUNCH_CHECK(ctx, launch_gemv_kq_swiglu(make_env(ctx, stream), qtype, w, x, y, K, F, pro),
                    "rrr_gemv_kq_swiglu launch");

@@ -25,4 +25,8 @@ int cuda_error(rrr_ctx* ctx, cudaError_t e, const char* what);
 int bind_device(rrr_ctx* ctx);
 void destroy_cublas(void* handle);
 LaunchEnv make_env(rrr_ctx* ctx, void* stream);
+// Argument rules of one single-token GEMV (rrr_gemv_kq_ex; swiglu: rrr_gemv_kq_swiglu
+// with N = F).
+int check_gemv(rrr_ctx* ctx, int qtype, const void* w, const float* x, float* y, int K, int N,
+               const float* residual, const rrr_gemv_prologue* pro, bool swiglu);
 }  // namespace rrr

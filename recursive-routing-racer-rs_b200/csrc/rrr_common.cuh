@@ -16,6 +16,7 @@ enum DeviceErr : int {
   kDevErrFullTimeout = 1,   // a consumer gave up waiting for a bulk copy
   kDevErrEmptyTimeout = 2,  // the producer gave up waiting for consumers to free a stage
   kDevErrDrainTimeout = 3,  // copies still in flight at exit did not complete in time
+  kDevErrPosition = 6,      // a position outside the cache, or a token id outside the table
 };
 
 // A wait gives up after this many nanoseconds of %globaltimer (about one second); it
