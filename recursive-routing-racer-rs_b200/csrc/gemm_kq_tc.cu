@@ -608,15 +608,13 @@ cudaError_t launch_t(const LaunchEnv& env, const TcPlan& pl, const void* w, cons
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (pl.splits > 1) {
-    // a cluster of `splits` CTAs at one CTA per SM must fit in one GPC
-    int n_clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&n_clusters, kern, &cfg);
-    if (e != cudaSuccess) return e;
-    if (n_clusters < 1) {  // no GPC can hold the cluster: one split
-      p.splits = 1;
-      cfg.gridDim.z = 1;
-      attr[0].val.clusterDim.z = 1;
-    }
+    // clusters are placed per GPC: the plan's split count can need a second wave of
+    // clusters (e.g. 24 tiles x 6 splits on 22 resident clusters of 6); take the split
+    // count with the fewest waves x K-blocks per CTA
+    const int s = pick_splits((const void*)kern, cfg, pl.n_tiles * pl.m_tiles, K / 256, pl.splits);
+    p.splits = s;
+    cfg.gridDim.z = s;
+    attr[0].val.clusterDim.z = s;
   }
   return cudaLaunchKernelEx(&cfg, kern, map, wmap, p);
 }

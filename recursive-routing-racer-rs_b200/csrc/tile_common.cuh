@@ -171,5 +171,62 @@ inline bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Clusters of `cluster` CTAs of `kern` (launch config `cfg`; its grid and attributes are
+// replaced) that can be resident at once. A cluster must fit in one GPC, so at one CTA per
+// SM clusters of 3 or more leave SMs unused (on a 148-SM B200: 45 x 3, 33 x 4, 26 x 5,
+// 22 x 6, 15 x 8). Cached per (kernel, device, shared memory, cluster size).
+inline int max_active_clusters(const void* kern, cudaLaunchConfig_t cfg, int cluster) {
+  struct Entry {
+    const void* k;
+    int dev, smem, c, n;
+  };
+  static std::mutex mu;
+  static Entry cache[128];
+  static int n_cache = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < n_cache; ++i)
+      if (cache[i].k == kern && cache[i].dev == dev && cache[i].smem == (int)cfg.dynamicSmemBytes &&
+          cache[i].c == cluster)
+        return cache[i].n;
+  }
+  cudaLaunchAttribute a[1];
+  a[0].id = cudaLaunchAttributeClusterDimension;
+  a[0].val.clusterDim.x = 1;
+  a[0].val.clusterDim.y = 1;
+  a[0].val.clusterDim.z = cluster;
+  cfg.gridDim = dim3(1, 1, cluster);
+  cfg.attrs = a;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (n_cache < 128) cache[n_cache++] = Entry{kern, dev, (int)cfg.dynamicSmemBytes, cluster, n};
+  return n;
+}
+
+// Split-K factor for `base` output tiles of `nb` K-blocks each, at most `max_s`: the s
+// whose waves (ceil(base / resident clusters of s)) times K-blocks per CTA (ceil(nb / s))
+// is smallest; ties go to the smaller s (less reduction).
+inline int pick_splits(const void* kern, const cudaLaunchConfig_t& cfg, int base, int nb,
+                       int max_s) {
+  int best = 1;
+  long long best_cost = -1;
+  for (int s = 1; s <= max_s; ++s) {
+    const int fit = max_active_clusters(kern, cfg, s);
+    if (fit < 1) continue;
+    const long long cost = (long long)((base + fit - 1) / fit) * ((nb + s - 1) / s);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
 
 }  // namespace rrr
