@@ -291,6 +291,7 @@ def run_ours(args, rank, world, local_rank):
         wb = cfg.weight_bytes(qt, K, N) + 2 * M * K + 4 * M * N
         batched[f"{name}_M{M}"] = {
             "qtype": {12: "Q4_K", 13: "Q5_K", 14: "Q6_K"}[qt], "M": M, "K": K, "N": N,
+            "path": "mma.sync" if M <= 64 else "tcgen05",
             "us_per_launch": round(us, 3), "TFLOPs": round(flops / us / 1e6, 1),
             "tensor_frac": round(flops / us / 1e6 / peaks(tensor=True)[0], 4),
             "GBps": round(wb / us / 1e3, 1), "hbm_frac": round(wb / us / 1e3 / peaks()[0], 4)}
@@ -361,7 +362,7 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     bms = max_over_ranks(b0e.elapsed_time(b1e) / bsteps)
     decode_batch = {"batch": BM, "tok_s": round(BM * 1e3 / bms, 1), "ms_per_step": round(bms, 4),
-                    "graph": True, "path": "per layer: rmsnorm->bf16, 4 tcgen05 GEMMs (residual in "
+                    "graph": True, "path": "per layer: rmsnorm->bf16, 4 batched K-quant GEMMs (mma.sync at M <= 64, tcgen05 above; residual in "
                                            "the epilogue), GQA-V / SiLU glue; logits on TF32 tensor cores (cuBLAS)"}
     bdec.close()
     bw.close()
@@ -529,7 +530,8 @@ def run_ours(args, rank, world, local_rank):
             "decode_kv": decode_kv,
             "decode_batch64": decode_batch,
             "tp_decode": tp_decode,
-            "batched_gemm": {"note": "configs[3]: rrr_gemm_kq_batched (tcgen05, bf16 x bf16 -> f32); "
+            "batched_gemm": {"note": "configs[3]: rrr_gemm_kq_batched, automatic path (register-level mma.sync "
+                                     "for 16 <= M <= 64, tcgen05 + TMEM + TMA above; bf16 x bf16 -> f32); "
                                      "tensor_frac against the measured dense bf16 burst peak",
                              "cases": batched},
             "e2e": {"value": round(bytes_step / e2e_ms / 1e6, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
