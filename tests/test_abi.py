@@ -36,6 +36,30 @@ def test_ffi_binds_every_declared_symbol(rrr):
     assert not unbound, unbound
 
 
+def _header_params(name):
+    """Parameter count of a declared function (comments stripped)."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    m = re.search(r"\b" + name + r"\s*\(([^;]*?)\)\s*;", text, flags=re.S)
+    args = [a for a in m.group(1).split(",") if a.strip() and a.strip() != "void"]
+    return len(args)
+
+
+def test_rust_binding_in_integration_doc_matches_header():
+    """INTEGRATION.md's Rust extern block (the binding a maintainer adds to the reference
+    crate) declares every header function with the same number of parameters."""
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    block = doc[doc.index("```rust"):]
+    block = block[:block.index("```", 7)]
+    rust = {}
+    for m in re.finditer(r"pub fn (rrr_\w+)\((.*?)\)\s*->", block, flags=re.S):
+        params = [p for p in m.group(2).split(",") if p.strip()]
+        rust[m.group(1)] = len(params)
+    declared = declared_functions()
+    assert sorted(rust) == declared, sorted(set(declared) ^ set(rust))
+    for name in declared:
+        assert rust[name] == _header_params(name), name
+
+
 def test_status_strings_and_version(rrr):
     L = rrr.ffi.lib()
     assert L.rrr_abi_version() == 1
