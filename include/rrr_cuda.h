@@ -370,6 +370,18 @@ int rrr_phi4_create(rrr_ctx* ctx, const rrr_phi4_desc* desc, rrr_phi4** out);
  * of the step (captured on the first call for this stream and these pointers). */
 int rrr_phi4_forward(rrr_phi4* m, float* hidden, float* logits, int* argmax_out,
                      int use_graph, void* stream);
+/* M tokens in one step (Phi4Model::forward_prefill_batched, phi4.rs:1200-1445): hidden
+ * device f32 [M][d] (in/out), logits device f32 [M][vocab], argmax_out NULL or device
+ * int32[M] (greedy argmax of each row). Every layer GEMM runs on the tensor cores
+ * (rrr_gemm_kq_batched; one GEMV per token below 16 rows) on bf16-rounded inputs, so the
+ * result is within the batched path's tolerance of the one-token step, not bit-equal.
+ * Without a KV cache the M tokens are independent (each at position 0); with one they are
+ * consecutive positions p..p+M-1 from the model's position p (a prefill chunk: RoPE, KV
+ * store of the M rows, causal attention), and the position advances by M. use_graph != 0:
+ * the first call for these pointers and M runs the step and captures it; later calls
+ * replay the graph. */
+int rrr_phi4_forward_batched(rrr_phi4* m, float* hidden, float* logits, int* argmax_out, int M,
+                             int use_graph, void* stream);
 /* Number of kernel launches one forward issues. */
 int rrr_phi4_launches_per_step(rrr_phi4* m, int* n);
 /* KV-cache decode: the position of the next forward (the KVCache.len of the reference;

@@ -38,6 +38,9 @@ cudaError_t launch_residual_add(const LaunchEnv& env, const float* a, const floa
 // left zeroed by every completed launch; one launch at a time per scratch slot.
 cudaError_t launch_argmax(const LaunchEnv& env, const float* x, int n, int* out_index,
                           void* scratch);
+// Greedy argmax of each row of x ([rows] rows of n values, row pitch ld elements).
+cudaError_t launch_argmax_rows(const LaunchEnv& env, const float* x, int n, long long ld,
+                               int* out_index, int rows);
 // gate_up GEMV with the SwiGLU epilogue: W has 2F rows [gate; up], y[i] = silu(gate_i) * up_i.
 cudaError_t launch_gemv_kq_swiglu(const LaunchEnv& env, int qtype, const void* w,
                                   const float* x, float* y, int K, int F,

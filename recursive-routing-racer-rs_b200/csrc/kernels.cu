@@ -199,6 +199,41 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   }
 }
 
+// Greedy argmax of each of `rows` rows (row r at x + r * ld, n values), one CTA per row:
+// the same order-preserving keys as argmax_kernel (first maximum wins, NaN skipped, index
+// 0 when nothing compares greater than -inf), reduced in the CTA without atomics.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restrict__ x, int n,
+                                                           long long ld, int* __restrict__ out) {
+  __shared__ unsigned long long sh[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const float* row = x + (long long)blockIdx.x * ld;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < n; i += 1024) {
+    const float v = row[i];
+    if (v == v && v > -INFINITY) {
+      const unsigned long long k = argmax_key(v, i);
+      best = k > best ? k : best;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+    best = t > best ? t : best;
+  }
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    best = sh[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+      best = t > best ? t : best;
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = best ? (int)(~(uint32_t)(best & 0xFFFFFFFFull)) : 0;
+  }
+}
+
 // C[M,N] = A[M,K] B[K,N], B row-major [K, N] (the reference's transposed chunk layout).
 __global__ void matmul_f32_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                   float* __restrict__ C, int M, int K, int N) {
@@ -369,6 +404,13 @@ cudaError_t launch_argmax(const LaunchEnv& env, const float* x, int n, int* out_
   const int grid = std::max(1, std::min((n + 4095) / 4096, env.sm_count));
   return rrr_launch_pdl(argmax_kernel, dim3(grid), dim3(1024), 0, env.stream, env.pdl, x, n,
                         out_index, key, counter);
+}
+
+cudaError_t launch_argmax_rows(const LaunchEnv& env, const float* x, int n, long long ld,
+                               int* out_index, int rows) {
+  if (rows <= 0) return cudaSuccess;
+  return rrr_launch_pdl(argmax_rows_kernel, dim3(rows), dim3(1024), 0, env.stream, env.pdl, x, n,
+                        ld, out_index);
 }
 
 cudaError_t launch_matmul_f32(const LaunchEnv& env, const float* A, const float* B, float* C,

@@ -118,6 +118,7 @@ PROTOS = {
     "rrr_gguf_upload": (c_int, [vp, vp, c_char_p, POINTER(vp), POINTER(c_uint64)]),
     "rrr_phi4_create": (c_int, [vp, POINTER(Phi4Desc), POINTER(vp)]),
     "rrr_phi4_forward": (c_int, [vp, vp, vp, vp, c_int, vp]),
+    "rrr_phi4_forward_batched": (c_int, [vp, vp, vp, vp, c_int, c_int, vp]),
     "rrr_phi4_launches_per_step": (c_int, [vp, POINTER(c_int)]),
     "rrr_phi4_destroy": (c_int, [vp]),
     "rrr_set_pdl": (c_int, [vp, c_int]),

@@ -180,6 +180,15 @@ class Phi4Decoder:
                                                   c_void_p(argmax_ptr) if argmax_ptr else None,
                                                   1 if use_graph else 0, s))
 
+    def forward_batched(self, hidden_ptr: int, logits_ptr: int, M: int, argmax_ptr: int | None = None,
+                        use_graph: bool = True, stream=None) -> None:
+        """M tokens in one step (forward_prefill_batched): hidden f32 [M, d] in/out, logits
+        f32 [M, vocab], argmax int32 [M] or None; consecutive positions with a KV cache."""
+        s = None if stream is None else c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+        self.ctx.check(ffi.lib().rrr_phi4_forward_batched(
+            self.h, c_void_p(hidden_ptr), c_void_p(logits_ptr), c_void_p(argmax_ptr) if argmax_ptr else None,
+            M, 1 if use_graph else 0, s))
+
     def launches_per_step(self) -> int:
         n = c_int()
         self.ctx.check(ffi.lib().rrr_phi4_launches_per_step(self.h, ctypes.byref(n)))

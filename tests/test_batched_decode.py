@@ -233,3 +233,94 @@ def test_prefill_with_positions(rrr, ctx, oracle, G):
         dec.close()
     for w in ws + [w1]:
         w.close()
+
+
+@pytest.mark.parametrize("M", [3, 16, 40])
+def test_phi4_forward_batched(rrr, ctx, oracle, M):
+    """rrr_phi4_forward_batched (the C++ decode driver's M-token step, position 0): against
+    the bf16-aware reference, the per-row argmax against the logits, a graph replay from the
+    same input bit-equal to the first (eager) call, and the Python tensor-parallel driver at
+    G = 1 (same kernels) on the same weights."""
+    import torch
+    cfg = _cfg()
+    w = phi4.SyntheticPhi4(ctx, cfg, seed=24)
+    dec = phi4.Phi4Decoder(ctx, w)
+    torch.manual_seed(100 + M)
+    hidden0 = torch.randn(M, cfg.d_model, device="cuda")
+    h = hidden0.clone()
+    lg = torch.empty(M, cfg.vocab_size, device="cuda")
+    am = torch.full((M,), -1, dtype=torch.int32, device="cuda")
+    dec.forward_batched(h.data_ptr(), lg.data_ptr(), M, am.data_ptr(), use_graph=True)
+    torch.cuda.synchronize()
+    assert ctx.device_error() == 0
+    H, LG, AM = h.cpu().numpy(), lg.cpu().numpy(), am.cpu().numpy()
+    layers, on, wo = _host_model(oracle, w, torch)
+    Hr, LGr = _bf16_reference(oracle, layers, on, wo, hidden0.cpu().numpy(), torch, bf16_weights=M >= 16)
+    for m in range(M):
+        assert _rel(H[m], Hr[m]) < BF16_TOL, (m, _rel(H[m], Hr[m]))
+        assert _rel(LG[m], LGr[m]) < BF16_TOL, (m, _rel(LG[m], LGr[m]))
+    assert np.array_equal(AM, LG.argmax(1))
+    # the captured graph, replayed on the same input
+    h.copy_(hidden0)
+    am.fill_(-1)
+    dec.forward_batched(h.data_ptr(), lg.data_ptr(), M, am.data_ptr(), use_graph=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(h.cpu().numpy(), H) and np.array_equal(lg.cpu().numpy(), LG)
+    assert np.array_equal(am.cpu().numpy(), AM)
+    # the Python driver issues the same kernels on identical weights
+    wt = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, 1, 0), seed=24)
+    tdec = tp.TPDecoder(ctx, wt, max_batch=M)
+    h2 = hidden0.clone()
+    lg2 = torch.empty(M, cfg.vocab_size, device="cuda")
+    tdec.forward_batched(h2, lg2, M)
+    torch.cuda.synchronize()
+    assert _rel(h2.cpu().numpy(), H) < 1e-6 and _rel(lg2.cpu().numpy(), LG) < 1e-6
+    tdec.close()
+    wt.close()
+    dec.close()
+    w.close()
+
+
+def test_phi4_forward_batched_prefill(rrr, ctx, oracle):
+    """rrr_phi4_forward_batched with a KV cache: 5 tokens at positions 0-4 (eager), then 3
+    at 5-7 (captured and, for a second model state, replayed), against the bf16-aware
+    reference with the oracle's RoPE / attention; the model's position advances by M."""
+    import torch
+    cfg = _cfg()
+    max_seq = 16
+    w = phi4.SyntheticPhi4(ctx, cfg, seed=25)
+    dec = phi4.Phi4Decoder(ctx, w, max_seq=max_seq)
+    layers, on, wo = _host_model(oracle, w, torch)
+    fac = np.empty(w.n_rope_factors, np.float32)
+    ctx.check(tp.ffi.lib().rrr_d2h(ctx.h, c_void_p(fac.ctypes.data), c_void_p(w.rope_factors), fac.nbytes, None))
+    kvs = SMALL["n_kv_heads"] * SMALL["head_dim"]
+    kc = np.zeros((SMALL["n_layers"], max_seq, kvs), np.uint16)
+    vc = np.zeros_like(kc)
+    torch.manual_seed(41)
+    pos0 = 0
+    for M in (5, 3):
+        hidden0 = torch.randn(M, cfg.d_model, device="cuda")
+        h = hidden0.clone()
+        lg = torch.empty(M, cfg.vocab_size, device="cuda")
+        dec.forward_batched(h.data_ptr(), lg.data_ptr(), M, use_graph=(M == 3))
+        torch.cuda.synchronize()
+        assert ctx.device_error() == 0
+        Hr, LGr = _bf16_reference_kv(oracle, layers, on, wo, hidden0.cpu().numpy(), torch, pos0, kc, vc, fac)
+        H, LG = h.cpu().numpy(), lg.cpu().numpy()
+        for m in range(M):
+            assert _rel(H[m], Hr[m]) < BF16_TOL, (pos0 + m, _rel(H[m], Hr[m]))
+            assert _rel(LG[m], LGr[m]) < BF16_TOL
+        assert dec.position == pos0 + M
+        pos0 += M
+    # replay of the captured 3-token step at positions 5-7 from the same input
+    dec.set_position(5)
+    h.copy_(hidden0)  # same buffers as the captured call: the graph replays
+    dec.forward_batched(h.data_ptr(), lg.data_ptr(), 3, use_graph=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(h.cpu().numpy(), H) and dec.position == 8
+    # past the cache: an error, nothing launched
+    dec.set_position(14)
+    with pytest.raises(rrr.RRRError):
+        dec.forward_batched(h.data_ptr(), lg.data_ptr(), 3, use_graph=False)
+    dec.close()
+    w.close()
