@@ -343,29 +343,30 @@ def run_ours(args, rank, world, local_rank):
                  "launches_per_token": kdec.launches_per_step() + 1, "graph": True}
     kdec.close()
     # ---------------- batched decode step, 64 tokens at position 0 (configs[4] batch 64 on
-    # one GPU / one rank's replica): tcgen05 GEMMs for every layer GEMM, batched logits
-    tpm = importlib.import_module("recursive-routing-racer-rs_b200.tp")
+    # one GPU / one rank's replica) through the C++ driver (rrr_phi4_forward_batched):
+    # tensor-core GEMMs for every layer GEMM, batched logits, argmax of every row
     BM = 64
-    bw = tpm.SyntheticPhi4TP(ctx, cfg, tpm.plan(cfg, 1, 0), seed=9, stream=sp)
-    bdec = tpm.TPDecoder(ctx, bw, max_batch=BM)
+    bdec = phi4.Phi4Decoder(ctx, model)
     bh = torch.randn(BM, cfg.d_model, device="cuda")
     blg = torch.empty(BM, cfg.vocab_size, device="cuda")
+    bam = torch.zeros(BM, dtype=torch.int32, device="cuda")
     for _ in range(max(3, args.warmup)):
-        bdec.forward_batched(bh, blg, BM, use_graph=True)
+        bdec.forward_batched(bh.data_ptr(), blg.data_ptr(), BM, bam.data_ptr(), True, stream)
     barrier()
     b0e, b1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     bsteps = max(5, args.steps // 2)
     b0e.record(stream)
     for _ in range(bsteps):
-        bdec.forward_batched(bh, blg, BM, use_graph=True)
+        bdec.forward_batched(bh.data_ptr(), blg.data_ptr(), BM, bam.data_ptr(), True, stream)
     b1e.record(stream)
     barrier()
     bms = max_over_ranks(b0e.elapsed_time(b1e) / bsteps)
     decode_batch = {"batch": BM, "tok_s": round(BM * 1e3 / bms, 1), "ms_per_step": round(bms, 4),
-                    "graph": True, "path": "per layer: rmsnorm->bf16, 4 batched K-quant GEMMs (mma.sync at M <= 64, tcgen05 above; residual in "
-                                           "the epilogue), GQA-V / SiLU glue; logits on TF32 tensor cores (cuBLAS)"}
+                    "graph": True, "api": "rrr_phi4_forward_batched",
+                    "path": "per layer: rmsnorm->bf16, 4 batched K-quant GEMMs (mma.sync at M <= 64, tcgen05 above; "
+                            "residual in the epilogue), GQA-V / SiLU glue; logits on TF32 tensor cores (cuBLAS), "
+                            "row-wise argmax"}
     bdec.close()
-    bw.close()
     # ---------------- tensor-parallel decode step (configs[4], batch 1) over all ranks
     tp_decode = None
     if world > 1:
