@@ -9,6 +9,7 @@ DRAM figures of a capture are those of the bench's per-GEMV lines.
     python -m recursive-routing-racer-rs_b200.profcases decode --layers 32 [--max-seq 2048 --pos 1024]
     python -m recursive-routing-racer-rs_b200.profcases gemm --m 256    # batched tcgen05 GEMM
     python -m recursive-routing-racer-rs_b200.profcases attn --pos 1024 # RoPE + KV + attention
+    python -m recursive-routing-racer-rs_b200.profcases batched --m 64  # M-token decode step
 """
 import argparse
 import importlib
@@ -91,7 +92,23 @@ def case_attn(ctx, L, torch, args):
                                                  c_void_p(vc.data_ptr()), c_void_p(out.data_ptr()), None))
 
 
-CASES = {"gemv": case_gemv, "decode": case_decode, "gemm": case_gemm, "attn": case_attn}
+def case_batched(ctx, L, torch, args):
+    """Eager M-token steps (--m) of the synthetic Phi-4-mini model through
+    rrr_phi4_forward_batched at position 0: per layer RMSNorm -> bf16, 4 batched GEMMs,
+    GQA-V / SiLU glue; batched logits and the row-wise argmax."""
+    phi4 = importlib.import_module(_PKG + ".phi4")
+    cfg = phi4.ModelConfig(n_layers=args.layers)
+    m = phi4.SyntheticPhi4(ctx, cfg, seed=5)
+    dec = phi4.Phi4Decoder(ctx, m)
+    h = torch.randn(args.m, cfg.d_model, device="cuda")
+    lg = torch.empty(args.m, cfg.vocab_size, device="cuda")
+    am = torch.zeros(args.m, dtype=torch.int32, device="cuda")
+    for _ in range(args.rounds):
+        dec.forward_batched(h.data_ptr(), lg.data_ptr(), args.m, am.data_ptr(), False)
+
+
+CASES = {"gemv": case_gemv, "decode": case_decode, "gemm": case_gemm, "attn": case_attn,
+         "batched": case_batched}
 
 
 def main(argv=None):
