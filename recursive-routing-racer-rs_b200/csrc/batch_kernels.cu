@@ -50,6 +50,66 @@ __global__ void __launch_bounds__(256) rmsnorm_bf16_kernel(const float* __restri
     yr[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(gamma[i], xr[i]), inv));
 }
 
+// Vector forms (rows of a multiple of 4 values, 16-byte aligned inputs, 8-byte aligned
+// outputs): float4 loads, four bf16 per 8-byte store; the RMSNorm keeps its row slice in
+// registers between the sum of squares and the scaling (one pass over global memory).
+constexpr int kVecMax = 4;  // float4 per thread of a 256-thread RMSNorm row: d <= 4096
+
+__device__ __forceinline__ uint2 pack_bf16x4(float a, float b, float c, float d) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
+__global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ gamma,
+                                                               __nv_bfloat16* __restrict__ y,
+                                                               int d, float eps) {
+  __shared__ float sh[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)blockIdx.x * d);
+  uint2* yr = reinterpret_cast<uint2*>(y + (int64_t)blockIdx.x * d);
+  const int n4 = d >> 2;
+  float4 v[kVecMax];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kVecMax; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  }
+  const float tot = block_sum(ss, sh);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+#pragma unroll
+  for (int j = 0; j < kVecMax; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    if (i < n4) {
+      const float4 g = g4[i];
+      yr[i] = pack_bf16x4(__fmul_rn(__fmul_rn(g.x, v[j].x), inv), __fmul_rn(__fmul_rn(g.y, v[j].y), inv),
+                          __fmul_rn(__fmul_rn(g.z, v[j].z), inv), __fmul_rn(__fmul_rn(g.w, v[j].w), inv));
+    }
+  }
+}
+
+__device__ __forceinline__ float silu_mul(float a, float u) {
+  return __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), u);
+}
+
+__global__ void silu_gate_bf16_vec_kernel(const float* __restrict__ gu,
+                                          __nv_bfloat16* __restrict__ y, int F) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int m = blockIdx.y;
+  const float4* g = reinterpret_cast<const float4*>(gu + (int64_t)m * 2 * F);
+  const float4* u = reinterpret_cast<const float4*>(gu + (int64_t)m * 2 * F + F);
+  uint2* yr = reinterpret_cast<uint2*>(y + (int64_t)m * F);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < (F >> 2); i += gridDim.x * blockDim.x) {
+    const float4 a = g[i], b = u[i];
+    yr[i] = pack_bf16x4(silu_mul(a.x, b.x), silu_mul(a.y, b.y), silu_mul(a.z, b.z), silu_mul(a.w, b.w));
+  }
+}
+
 __global__ void gqa_v_bf16_kernel(const float* __restrict__ qkv, __nv_bfloat16* __restrict__ y,
                                   int nq, int nkv, int hd, int kwin, int koff) {
   pdl_launch_dependents();
@@ -100,6 +160,7 @@ void destroy_cublas(void* handle) { cublasDestroy(static_cast<cublasHandle_t>(ha
 using namespace rrr;
 
 static int grid_x(int n) { return n < 256 ? 1 : (n + 255) / 256 > 64 ? 64 : (n + 255) / 256; }
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 extern "C" {
 
@@ -112,8 +173,12 @@ int rrr_rmsnorm_bf16(rrr_ctx* ctx, const float* x, const float* gamma, uint16_t*
   if (rc) return rc;
   if (rows == 0) return RRR_OK;
   const LaunchEnv env = make_env(ctx, stream);
-  cudaError_t e = rrr_launch_pdl(rmsnorm_bf16_kernel, dim3(rows), dim3(256), 0, env.stream, env.pdl,
-                                 x, gamma, reinterpret_cast<__nv_bfloat16*>(y), d, eps);
+  const bool vec = d % 4 == 0 && d <= 1024 * kVecMax && aligned16(x) && aligned16(gamma) &&
+                   (reinterpret_cast<uintptr_t>(y) & 7) == 0;
+  cudaError_t e = vec ? rrr_launch_pdl(rmsnorm_bf16_vec_kernel, dim3(rows), dim3(256), 0, env.stream,
+                                       env.pdl, x, gamma, reinterpret_cast<__nv_bfloat16*>(y), d, eps)
+                      : rrr_launch_pdl(rmsnorm_bf16_kernel, dim3(rows), dim3(256), 0, env.stream,
+                                       env.pdl, x, gamma, reinterpret_cast<__nv_bfloat16*>(y), d, eps);
   return e == cudaSuccess ? RRR_OK : cuda_error(ctx, e, "rrr_rmsnorm_bf16 launch");
 }
 
@@ -143,8 +208,11 @@ int rrr_silu_gate_bf16(rrr_ctx* ctx, const float* gu, uint16_t* y, int rows, int
   if (rc) return rc;
   if (rows == 0) return RRR_OK;
   const LaunchEnv env = make_env(ctx, stream);
-  cudaError_t e = rrr_launch_pdl(silu_gate_bf16_kernel, dim3(grid_x(F), rows), dim3(256), 0,
-                                 env.stream, env.pdl, gu, reinterpret_cast<__nv_bfloat16*>(y), F);
+  const bool vec = F % 4 == 0 && aligned16(gu) && (reinterpret_cast<uintptr_t>(y) & 7) == 0;
+  cudaError_t e = vec ? rrr_launch_pdl(silu_gate_bf16_vec_kernel, dim3(grid_x(F / 4), rows), dim3(256), 0,
+                                       env.stream, env.pdl, gu, reinterpret_cast<__nv_bfloat16*>(y), F)
+                      : rrr_launch_pdl(silu_gate_bf16_kernel, dim3(grid_x(F), rows), dim3(256), 0,
+                                       env.stream, env.pdl, gu, reinterpret_cast<__nv_bfloat16*>(y), F);
   return e == cudaSuccess ? RRR_OK : cuda_error(ctx, e, "rrr_silu_gate_bf16 launch");
 }
 
