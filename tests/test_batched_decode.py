@@ -324,3 +324,52 @@ def test_phi4_forward_batched_prefill(rrr, ctx, oracle):
         dec.forward_batched(h.data_ptr(), lg.data_ptr(), 3, use_graph=False)
     dec.close()
     w.close()
+
+
+def test_phi4_prefill_then_single_token(rrr, ctx, oracle):
+    """The C++ driver's usual flow: a 5-token batched prefill, then single-token steps at
+    positions 5 and 6 on the cache the prefill left. Each single-token step is checked
+    against the oracle's KV-cache decode step run on the same cache contents (read back
+    from the device), so the prefill's cache layout, device position and host position
+    must all line up with the single-token path."""
+    import torch
+    cfg = _cfg()
+    max_seq = 16
+    w = phi4.SyntheticPhi4(ctx, cfg, seed=26)
+    dec = phi4.Phi4Decoder(ctx, w, max_seq=max_seq)
+    layers, on, wo = _host_model(oracle, w, torch)
+    fac = np.empty(w.n_rope_factors, np.float32)
+    ctx.check(tp.ffi.lib().rrr_d2h(ctx.h, c_void_p(fac.ctypes.data), c_void_p(w.rope_factors), fac.nbytes, None))
+    torch.manual_seed(51)
+    M = 5
+    h = torch.randn(M, cfg.d_model, device="cuda")
+    lg = torch.empty(M, cfg.vocab_size, device="cuda")
+    dec.forward_batched(h.data_ptr(), lg.data_ptr(), M, use_graph=False)
+    torch.cuda.synchronize()
+    assert dec.position == M
+    kvs = SMALL["n_kv_heads"] * SMALL["head_dim"]
+    L = tp.ffi.lib()
+    for pos in (M, M + 1):
+        kc = np.empty((SMALL["n_layers"], max_seq, kvs), np.uint16)
+        vc = np.empty_like(kc)
+        for layer in range(SMALL["n_layers"]):
+            kp, vp_ = dec.kv_cache(layer)
+            ctx.check(L.rrr_d2h(ctx.h, c_void_p(kc[layer].ctypes.data), c_void_p(kp), kc[layer].nbytes, None))
+            ctx.check(L.rrr_d2h(ctx.h, c_void_p(vc[layer].ctypes.data), c_void_p(vp_), vc[layer].nbytes, None))
+        ctx.check(L.rrr_sync(ctx.h, None))
+        h0 = torch.randn(cfg.d_model, device="cuda")
+        h1 = h0.clone()
+        l1 = torch.empty(cfg.vocab_size, device="cuda")
+        am = torch.zeros(1, dtype=torch.int32, device="cuda")
+        dec.forward(h1.data_ptr(), l1.data_ptr(), am.data_ptr(), use_graph=(pos == M + 1))
+        torch.cuda.synchronize()
+        assert ctx.device_error() == 0
+        h_ref, lg_ref = oracle.decode_step_kv(SMALL, layers, on, wo, h0.cpu().numpy(), pos, kc, vc,
+                                              rope_dim=ROPE["rope_dim"], theta=ROPE["theta"],
+                                              attn_factor=ROPE["attn_factor"], factors=fac)
+        assert _rel(h1.cpu().numpy(), h_ref) < 1e-4, (pos, _rel(h1.cpu().numpy(), h_ref))
+        assert _rel(l1.cpu().numpy(), lg_ref) < 1e-4
+        assert int(am.item()) == int(np.argmax(l1.cpu().numpy()))
+        assert dec.position == pos + 1
+    dec.close()
+    w.close()
