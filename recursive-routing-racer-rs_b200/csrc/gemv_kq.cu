@@ -205,10 +205,16 @@ __device__ __forceinline__ void block_q45(const uint8_t* b0, const uint8_t* b1, 
   acc1 += d1 * xs * ((float)i10 * L.w0 + (float)i11 * L.w1) - dm1 * mt1;
 }
 
-// 32-bit load from a shared-memory byte address that is 4-byte or 2-byte aligned.
-template <bool ALIGNED>
+// 32-bit load from a shared-memory byte address p with p % 4 == MIS for MIS = 0 or 2
+// (Q6_K blocks of 210 bytes start 4-byte aligned or 2 bytes past; rows and chunks start
+// at even offsets), or, MIS = 1, either of the two per lane.
+template <int MIS>
 __device__ __forceinline__ uint32_t ldw(const uint8_t* p) {
-  if (ALIGNED) return *reinterpret_cast<const uint32_t*>(p);
+  if (MIS == 0) return *reinterpret_cast<const uint32_t*>(p);
+  if (MIS == 2) {  // two bytes past a 4-byte boundary (every lane of the warp)
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(p - 2);
+    return __byte_perm(q[0], q[1], 0x5432);
+  }
   const uintptr_t a = reinterpret_cast<uintptr_t>(p);
   const uint32_t* q = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
   return __byte_perm(q[0], q[1], (a & 2) ? 0x5432 : 0x3210);
@@ -227,16 +233,33 @@ __device__ __forceinline__ uint32_t q6_bytes(uint32_t ql, uint32_t qh, int k) {
 // A = l in [0,16) (scale hg*8+2k), group B = l in [16,32) (scale hg*8+2k+1); lane tig
 // holds l = 4tig+i (A) and 16+4tig+i (B) (element layout of phi4.rs:456-475). q is taken
 // unsigned (0..63); the -32 offset is applied in f32 with the 16-element sums of x.
-template <bool AL>
+template <int AL>
 __device__ __forceinline__ void block_q6(const uint8_t* b0, const uint8_t* b1, int kb,
                                          const int8_t* dig, int ds, const float* xscale,
                                          const float* xsum, const Lane& L, float& acc0,
                                          float& acc1) {
   uint32_t sw0[4], sw1[4];
+  if (AL == 2) {
+    // the 16 scale bytes as five aligned words shifted by two bytes
+    const uint32_t* q0 = reinterpret_cast<const uint32_t*>(b0 + 190);
+    const uint32_t* q1 = reinterpret_cast<const uint32_t*>(b1 + 190);
+    uint32_t w0[5], w1[5];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    sw0[i] = ldw<AL>(b0 + 192 + 4 * i);
-    sw1[i] = ldw<AL>(b1 + 192 + 4 * i);
+    for (int i = 0; i < 5; ++i) {
+      w0[i] = q0[i];
+      w1[i] = q1[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sw0[i] = __byte_perm(w0[i], w0[i + 1], 0x5432);
+      sw1[i] = __byte_perm(w1[i], w1[i + 1], 0x5432);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sw0[i] = ldw<AL>(b0 + 192 + 4 * i);
+      sw1[i] = ldw<AL>(b1 + 192 + 4 * i);
+    }
   }
   const int8_t* dp = dig + L.dsel * ds + kb * 256 + 4 * L.tig + (L.mB ? 16 : 0);
   int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
@@ -631,10 +654,13 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_kq_kernel(const GemvP
           const uint8_t* q1 = r1 + bi * BB;
           if constexpr (QT == RRR_Q6_K) {
             const bool al = __all_sync(0xffffffffu, (((uintptr_t)q0 | (uintptr_t)q1) & 3) == 0);
+            const bool m2 = __all_sync(0xffffffffu, ((uintptr_t)q0 & 3) == 2 && ((uintptr_t)q1 & 3) == 2);
             if (al)
-              block_q6<true>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
+              block_q6<0>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
+            else if (m2)
+              block_q6<2>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
             else
-              block_q6<false>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
+              block_q6<1>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
           } else {
             block_q45<QT, FRAG>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum32, L, acc0, acc1);
           }
