@@ -220,6 +220,21 @@ __device__ __forceinline__ uint32_t ldw(const uint8_t* p) {
   return __byte_perm(q[0], q[1], (a & 2) ? 0x5432 : 0x3210);
 }
 
+// The same for lanes whose blocks start at different offsets mod 4 (0 or 2): the aligned
+// base and the permute selector are taken once per block (b = block start of this lane).
+struct LaneWords {
+  const uint8_t* base;  // b rounded down to 4 bytes
+  uint32_t sel;         // byte permute of two aligned words
+  __device__ __forceinline__ explicit LaneWords(const uint8_t* b)
+      : base(b - (reinterpret_cast<uintptr_t>(b) & 2)),
+        sel((reinterpret_cast<uintptr_t>(b) & 2) ? 0x5432u : 0x3210u) {}
+  // word at byte offset off (a multiple of 4) of the block
+  __device__ __forceinline__ uint32_t operator()(int off) const {
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(base + off);
+    return __byte_perm(q[0], q[1], sel);
+  }
+};
+
 __device__ __forceinline__ int sbyte(uint32_t w, int i) { return (int)(int8_t)(w >> (8 * i)); }
 
 // Q6_K bits of element group k: nibble (k>>1) of the ql word | 2 qh bits (2k) << 4.
@@ -238,6 +253,10 @@ __device__ __forceinline__ void block_q6(const uint8_t* b0, const uint8_t* b1, i
                                          const int8_t* dig, int ds, const float* xscale,
                                          const float* xsum, const Lane& L, float& acc0,
                                          float& acc1) {
+  // word readers of this lane's two rows (AL 1: per-lane base and selector, once)
+  const LaneWords lw0(b0), lw1(b1);
+  auto W0 = [&](int off) { return AL == 1 ? lw0(off) : ldw<AL>(b0 + off); };
+  auto W1 = [&](int off) { return AL == 1 ? lw1(off) : ldw<AL>(b1 + off); };
   uint32_t sw0[4], sw1[4];
   if (AL == 2) {
     // the 16 scale bytes as five aligned words shifted by two bytes
@@ -257,24 +276,21 @@ __device__ __forceinline__ void block_q6(const uint8_t* b0, const uint8_t* b1, i
   } else {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      sw0[i] = ldw<AL>(b0 + 192 + 4 * i);
-      sw1[i] = ldw<AL>(b1 + 192 + 4 * i);
+      sw0[i] = W0(192 + 4 * i);
+      sw1[i] = W1(192 + 4 * i);
     }
   }
   const int8_t* dp = dig + L.dsel * ds + kb * 256 + 4 * L.tig + (L.mB ? 16 : 0);
   int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
 #pragma unroll
   for (int hg = 0; hg < 2; ++hg) {
-    const uint8_t* p0 = b0 + hg * 64 + 4 * L.tig;
-    const uint8_t* p1 = b1 + hg * 64 + 4 * L.tig;
-    const uint32_t qlA0_0 = ldw<AL>(p0), qlB0_0 = ldw<AL>(p0 + 16);
-    const uint32_t qlA1_0 = ldw<AL>(p0 + 32), qlB1_0 = ldw<AL>(p0 + 48);
-    const uint32_t qlA0_1 = ldw<AL>(p1), qlB0_1 = ldw<AL>(p1 + 16);
-    const uint32_t qlA1_1 = ldw<AL>(p1 + 32), qlB1_1 = ldw<AL>(p1 + 48);
-    const uint8_t* h0p = b0 + 128 + hg * 32 + 4 * L.tig;
-    const uint8_t* h1p = b1 + 128 + hg * 32 + 4 * L.tig;
-    const uint32_t qhA_0 = ldw<AL>(h0p), qhB_0 = ldw<AL>(h0p + 16);
-    const uint32_t qhA_1 = ldw<AL>(h1p), qhB_1 = ldw<AL>(h1p + 16);
+    const int pq = hg * 64 + 4 * L.tig, ph = 128 + hg * 32 + 4 * L.tig;
+    const uint32_t qlA0_0 = W0(pq), qlB0_0 = W0(pq + 16);
+    const uint32_t qlA1_0 = W0(pq + 32), qlB1_0 = W0(pq + 48);
+    const uint32_t qlA0_1 = W1(pq), qlB0_1 = W1(pq + 16);
+    const uint32_t qlA1_1 = W1(pq + 32), qlB1_1 = W1(pq + 48);
+    const uint32_t qhA_0 = W0(ph), qhB_0 = W0(ph + 16);
+    const uint32_t qhA_1 = W1(ph), qhB_1 = W1(ph + 16);
     // this lane's scale group of MMA k: byte 2*(k&1) + hb of word 2hg + (k >> 1)
     const uint32_t tA0 = sw0[2 * hg] >> (8 * L.hb), tB0 = sw0[2 * hg + 1] >> (8 * L.hb);
     const uint32_t tA1 = sw1[2 * hg] >> (8 * L.hb), tB1 = sw1[2 * hg + 1] >> (8 * L.hb);
