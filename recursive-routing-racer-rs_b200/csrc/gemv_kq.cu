@@ -95,6 +95,7 @@ struct Lane {
   int dsel;         // digit supplied in B column g (compact layout)
   int frag_off;     // byte offset of this lane's B fragment inside a pair (fragment layout)
   float w0, w1;     // f32 weights of the lane's two D columns
+  uint32_t msel0, msel1;  // byte permutes placing min byte 2(tig&1) / +1 under 2^23's exponent
 };
 
 __device__ __forceinline__ Lane make_lane(int lane, bool q4) {
@@ -102,6 +103,8 @@ __device__ __forceinline__ Lane make_lane(int lane, bool q4) {
   L.g = lane >> 2;
   L.tig = lane & 3;
   L.hb = L.tig >> 1;
+  L.msel0 = 0x7440u | (uint32_t)(2 * (L.tig & 1));
+  L.msel1 = 0x7440u | (uint32_t)(2 * (L.tig & 1) + 1);
   L.mA = L.g < 3 ? 0xFFFFFFFFu : 0u;
   L.mB = (L.g >= 4 && L.g < 7) ? 0xFFFFFFFFu : 0u;
   L.dsel = (L.g < 3) ? L.g : (L.g >= 4 && L.g < 7) ? L.g - 4 : 0;
@@ -113,9 +116,10 @@ __device__ __forceinline__ Lane make_lane(int lane, bool q4) {
   return L;
 }
 
-// Exact float of an integer 0 <= u < 2^23 without a conversion instruction.
-__device__ __forceinline__ float small_u2f(uint32_t u) {
-  return __fsub_rn(__uint_as_float(0x4B000000u | u), 8388608.0f);
+// Exact float of byte (sel & 3) of w: one permute puts the byte under the exponent of
+// 2^23 (0x4B000000), one subtraction removes it (sel = 0x7440 | byte index).
+__device__ __forceinline__ float byte_u2f(uint32_t w, uint32_t sel) {
+  return __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, sel)), 8388608.0f);
 }
 
 // qh bit `s` of each byte moved to bit 4.
@@ -197,10 +201,9 @@ __device__ __forceinline__ void block_q45(const uint8_t* b0, const uint8_t* b1, 
                                  : (((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u));
   const uint32_t mw1 = L.tig < 2 ? (h1.z & 0x3F3F3F3Fu)
                                  : (((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u));
-  const int sh = 16 * (L.tig & 1);
   const float2 S = *reinterpret_cast<const float2*>(xsum32 + kb * 8 + 2 * L.tig);
-  const float mt0 = small_u2f((mw0 >> sh) & 0xFFu) * S.x + small_u2f((mw0 >> (sh + 8)) & 0xFFu) * S.y;
-  const float mt1 = small_u2f((mw1 >> sh) & 0xFFu) * S.x + small_u2f((mw1 >> (sh + 8)) & 0xFFu) * S.y;
+  const float mt0 = byte_u2f(mw0, L.msel0) * S.x + byte_u2f(mw0, L.msel1) * S.y;
+  const float mt1 = byte_u2f(mw1, L.msel0) * S.x + byte_u2f(mw1, L.msel1) * S.y;
   acc0 += d0 * xs * ((float)i00 * L.w0 + (float)i01 * L.w1) - dm0 * mt0;
   acc1 += d1 * xs * ((float)i10 * L.w0 + (float)i11 * L.w1) - dm1 * mt1;
 }
