@@ -85,6 +85,18 @@ __device__ __forceinline__ void mma_u8s8_z(int& d0, int& d1, int& d2, int& d3, u
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
+// prmt selector of byte i of a word, sign-extended to 32 bits (selector nibbles with bit 3
+// set replicate the sign of the selected byte). __byte_perm ignores that bit, so the
+// permute is issued as prmt.b32 directly (byte_sext).
+__host__ __device__ constexpr uint32_t sext_sel(int i) {
+  return (uint32_t)i | ((uint32_t)(i | 8) << 4) | ((uint32_t)(i | 8) << 8) | ((uint32_t)(i | 8) << 12);
+}
+__device__ __forceinline__ int byte_sext(uint32_t w, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(w), "r"(0u), "r"(sel));
+  return (int)r;
+}
+
 // Lane roles inside an MMA tile: rows g and g+8 of the A operand; B column n = g carries
 // digit n of scale group A (n = 0..2) or digit n-4 of group B (n = 4..6), columns 3 and 7
 // are zero; the lane's D columns 2*tig, 2*tig+1 therefore belong to a single group
@@ -96,6 +108,8 @@ struct Lane {
   int frag_off;     // byte offset of this lane's B fragment inside a pair (fragment layout)
   float w0, w1;     // f32 weights of the lane's two D columns
   uint32_t msel0, msel1;  // byte permutes placing min byte 2(tig&1) / +1 under 2^23's exponent
+  uint32_t ssel0, ssel1;  // byte permutes extracting scale byte hb / 2 + hb (zero-extended)
+  uint32_t qsel0, qsel1;  // the same bytes sign-extended (Q6_K int8 scales)
 };
 
 __device__ __forceinline__ Lane make_lane(int lane, bool q4) {
@@ -105,6 +119,10 @@ __device__ __forceinline__ Lane make_lane(int lane, bool q4) {
   L.hb = L.tig >> 1;
   L.msel0 = 0x7440u | (uint32_t)(2 * (L.tig & 1));
   L.msel1 = 0x7440u | (uint32_t)(2 * (L.tig & 1) + 1);
+  L.ssel0 = 0x4440u | (uint32_t)L.hb;
+  L.ssel1 = 0x4440u | (uint32_t)(2 + L.hb);
+  L.qsel0 = sext_sel(L.hb);
+  L.qsel1 = sext_sel(2 + L.hb);
   L.mA = L.g < 3 ? 0xFFFFFFFFu : 0u;
   L.mB = (L.g >= 4 && L.g < 7) ? 0xFFFFFFFFu : 0u;
   L.dsel = (L.g < 3) ? L.g : (L.g >= 4 && L.g < 7) ? L.g - 4 : 0;
@@ -153,10 +171,10 @@ __device__ __forceinline__ void block_q45(const uint8_t* b0, const uint8_t* b1, 
   const uint4 h0 = *reinterpret_cast<const uint4*>(b0);
   const uint4 h1 = *reinterpret_cast<const uint4*>(b1);
   // this lane's group (sub 2p + hb): byte 2*(p&1) + hb of the packed word of subs 0-3 / 4-7
-  const uint32_t s03_0 = (h0.y & 0x3F3F3F3Fu) >> (8 * L.hb);
-  const uint32_t s47_0 = ((h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u)) >> (8 * L.hb);
-  const uint32_t s03_1 = (h1.y & 0x3F3F3F3Fu) >> (8 * L.hb);
-  const uint32_t s47_1 = ((h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u)) >> (8 * L.hb);
+  const uint32_t s03_0 = h0.y & 0x3F3F3F3Fu;
+  const uint32_t s47_0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+  const uint32_t s03_1 = h1.y & 0x3F3F3F3Fu;
+  const uint32_t s47_1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
   uint2 qh0 = make_uint2(0u, 0u), qh1 = make_uint2(0u, 0u);
   if (QT == RRR_Q5_K) {
     qh0 = *reinterpret_cast<const uint2*>(b0 + 16 + 8 * L.tig);
@@ -185,8 +203,9 @@ __device__ __forceinline__ void block_q45(const uint8_t* b0, const uint8_t* b1, 
                ((w.y >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh0.y, sb),
                ((v.y >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh1.y, sb), bf.z, bf.w);
     }
-    const int r0 = (int)(((p < 2 ? s03_0 : s47_0) >> (16 * (p & 1))) & 0xFFu);
-    const int r1 = (int)(((p < 2 ? s03_1 : s47_1) >> (16 * (p & 1))) & 0xFFu);
+    const uint32_t ssel = (p & 1) ? L.ssel1 : L.ssel0;
+    const int r0 = (int)__byte_perm(p < 2 ? s03_0 : s47_0, 0u, ssel);
+    const int r1 = (int)__byte_perm(p < 2 ? s03_1 : s47_1, 0u, ssel);
     i00 += r0 * D0;
     i01 += r0 * D1;
     i10 += r1 * D2;
@@ -295,8 +314,8 @@ __device__ __forceinline__ void block_q6(const uint8_t* b0, const uint8_t* b1, i
     const uint32_t qhA_0 = W0(ph), qhB_0 = W0(ph + 16);
     const uint32_t qhA_1 = W1(ph), qhB_1 = W1(ph + 16);
     // this lane's scale group of MMA k: byte 2*(k&1) + hb of word 2hg + (k >> 1)
-    const uint32_t tA0 = sw0[2 * hg] >> (8 * L.hb), tB0 = sw0[2 * hg + 1] >> (8 * L.hb);
-    const uint32_t tA1 = sw1[2 * hg] >> (8 * L.hb), tB1 = sw1[2 * hg + 1] >> (8 * L.hb);
+    const uint32_t tA0 = sw0[2 * hg], tB0 = sw0[2 * hg + 1];
+    const uint32_t tA1 = sw1[2 * hg], tB1 = sw1[2 * hg + 1];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const uint32_t qlA_0 = (k & 1) ? qlA1_0 : qlA0_0, qlB_0 = (k & 1) ? qlB1_0 : qlB0_0;
@@ -305,8 +324,9 @@ __device__ __forceinline__ void block_q6(const uint8_t* b0, const uint8_t* b1, i
       int D0, D1, D2, D3;
       mma_u8s8_z(D0, D1, D2, D3, q6_bytes(qlA_0, qhA_0, k), q6_bytes(qlA_1, qhA_1, k),
                  q6_bytes(qlB_0, qhB_0, k), q6_bytes(qlB_1, qhB_1, k), bv & L.mA, bv & L.mB);
-      const int sc0 = sbyte(k < 2 ? tA0 : tB0, 2 * (k & 1));
-      const int sc1 = sbyte(k < 2 ? tA1 : tB1, 2 * (k & 1));
+      const uint32_t qsel = (k & 1) ? L.qsel1 : L.qsel0;
+      const int sc0 = byte_sext(k < 2 ? tA0 : tB0, qsel);
+      const int sc1 = byte_sext(k < 2 ? tA1 : tB1, qsel);
       i00 += sc0 * D0;
       i01 += sc0 * D1;
       i10 += sc1 * D2;
