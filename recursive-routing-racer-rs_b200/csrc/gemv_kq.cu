@@ -108,8 +108,7 @@ struct Lane {
   int frag_off;     // byte offset of this lane's B fragment inside a pair (fragment layout)
   float w0, w1;     // f32 weights of the lane's two D columns
   uint32_t msel0, msel1;  // byte permutes placing min byte 2(tig&1) / +1 under 2^23's exponent
-  uint32_t ssel0, ssel1;  // byte permutes extracting scale byte hb / 2 + hb (zero-extended)
-  uint32_t qsel0, qsel1;  // the same bytes sign-extended (Q6_K int8 scales)
+  uint32_t ssel;  // byte permute extracting scale byte hb (zero-extended); + 2: byte 2 + hb
 };
 
 __device__ __forceinline__ Lane make_lane(int lane, bool q4) {
@@ -119,10 +118,7 @@ __device__ __forceinline__ Lane make_lane(int lane, bool q4) {
   L.hb = L.tig >> 1;
   L.msel0 = 0x7440u | (uint32_t)(2 * (L.tig & 1));
   L.msel1 = 0x7440u | (uint32_t)(2 * (L.tig & 1) + 1);
-  L.ssel0 = 0x4440u | (uint32_t)L.hb;
-  L.ssel1 = 0x4440u | (uint32_t)(2 + L.hb);
-  L.qsel0 = sext_sel(L.hb);
-  L.qsel1 = sext_sel(2 + L.hb);
+  L.ssel = 0x4440u | (uint32_t)L.hb;
   L.mA = L.g < 3 ? 0xFFFFFFFFu : 0u;
   L.mB = (L.g >= 4 && L.g < 7) ? 0xFFFFFFFFu : 0u;
   L.dsel = (L.g < 3) ? L.g : (L.g >= 4 && L.g < 7) ? L.g - 4 : 0;
@@ -203,7 +199,7 @@ __device__ __forceinline__ void block_q45(const uint8_t* b0, const uint8_t* b1, 
                ((w.y >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh0.y, sb),
                ((v.y >> 4) & 0x0F0F0F0Fu) | qh_bit4(qh1.y, sb), bf.z, bf.w);
     }
-    const uint32_t ssel = (p & 1) ? L.ssel1 : L.ssel0;
+    const uint32_t ssel = L.ssel + ((p & 1) ? 2u : 0u);
     const int r0 = (int)__byte_perm(p < 2 ? s03_0 : s47_0, 0u, ssel);
     const int r1 = (int)__byte_perm(p < 2 ? s03_1 : s47_1, 0u, ssel);
     i00 += r0 * D0;
@@ -314,8 +310,8 @@ __device__ __forceinline__ void block_q6(const uint8_t* b0, const uint8_t* b1, i
     const uint32_t qhA_0 = W0(ph), qhB_0 = W0(ph + 16);
     const uint32_t qhA_1 = W1(ph), qhB_1 = W1(ph + 16);
     // this lane's scale group of MMA k: byte 2*(k&1) + hb of word 2hg + (k >> 1)
-    const uint32_t tA0 = sw0[2 * hg], tB0 = sw0[2 * hg + 1];
-    const uint32_t tA1 = sw1[2 * hg], tB1 = sw1[2 * hg + 1];
+    const uint32_t tA0 = sw0[2 * hg] >> (8 * L.hb), tB0 = sw0[2 * hg + 1] >> (8 * L.hb);
+    const uint32_t tA1 = sw1[2 * hg] >> (8 * L.hb), tB1 = sw1[2 * hg + 1] >> (8 * L.hb);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const uint32_t qlA_0 = (k & 1) ? qlA1_0 : qlA0_0, qlB_0 = (k & 1) ? qlB1_0 : qlB0_0;
@@ -324,7 +320,8 @@ __device__ __forceinline__ void block_q6(const uint8_t* b0, const uint8_t* b1, i
       int D0, D1, D2, D3;
       mma_u8s8_z(D0, D1, D2, D3, q6_bytes(qlA_0, qhA_0, k), q6_bytes(qlA_1, qhA_1, k),
                  q6_bytes(qlB_0, qhB_0, k), q6_bytes(qlB_1, qhB_1, k), bv & L.mA, bv & L.mB);
-      const uint32_t qsel = (k & 1) ? L.qsel1 : L.qsel0;
+      constexpr uint32_t qsel0 = sext_sel(0), qsel2 = sext_sel(2);
+      const uint32_t qsel = (k & 1) ? qsel2 : qsel0;
       const int sc0 = byte_sext(k < 2 ? tA0 : tB0, qsel);
       const int sc1 = byte_sext(k < 2 ? tA1 : tB1, qsel);
       i00 += sc0 * D0;
