@@ -37,7 +37,7 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 # DRAM bytes (read + write) of one gate_up GEMV launch, from the ncu capture summarised in
 # profiles/gemv_kq_phi4_layer_shapes.md (28,369,152 read + 0 written; the algorithmic
 # bytes are 28,389,376).
-GATE_UP_DRAM_BYTES = 28369408
+GATE_UP_DRAM_BYTES = 28369152
 METRIC = "K-quant GEMV HBM GB/s (% of peak) per B200; Phi-4-mini-shape decode tok/s"
 
 
