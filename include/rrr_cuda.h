@@ -144,8 +144,9 @@ int rrr_dequant_kq(rrr_ctx* ctx, int qtype, const void* w_raw, float* out,
 /* ---- kernel (2): batched-token K-quant GEMM, Y[M,N] = X[M,K] W^T (f32 out) ----------
  * Replaces the `matmul_gpuq{4,5,6}_batch` dispatches (push [K, N, M], workgroups
  * [N, M, 1], phi4.rs:1257-1268, 1346-1357, 1380-1391). X is bf16 [M,K] row-major
- * (uint16 bit patterns). Tensor-core path (tcgen05) for M >= 16; smaller M is routed
- * to the GEMV kernel per token. */
+ * (uint16 bit patterns). Tensor cores: register-level mma.sync for 3 <= M <= 64 when
+ * every weight row is a multiple of 16 bytes, tcgen05 otherwise from M = 16; M <= 2 (and
+ * M < 16 with unaligned rows) runs the GEMV kernel once per token. */
 int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16_t* x_bf16,
                         float* y, int M, int K, int N, void* stream);
 
@@ -154,9 +155,10 @@ int rrr_gemm_kq_batched(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16
 int rrr_gemm_kq_batched_ex(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16_t* x_bf16,
                            float* y, int M, int K, int N, const float* residual, void* stream);
 /* The same GEMM with the kernel chosen explicitly (tests, benchmarks): RRR_GEMM_AUTO is
- * rrr_gemm_kq_batched_ex's choice (mma.sync for 16 <= M <= 64 when every weight row is a
- * multiple of 16 bytes, tcgen05 for larger M, one GEMV per token below 16); the others force
- * one kernel and fail with RRR_ERR_BAD_SHAPE where it does not apply. */
+ * rrr_gemm_kq_batched_ex's choice (mma.sync for 3 <= M <= 64 when every weight row is a
+ * multiple of 16 bytes, tcgen05 for larger M or unaligned rows from M = 16, one GEMV per
+ * token otherwise); the others force one kernel (mma.sync takes 1 <= M <= 64, tcgen05
+ * M >= 16) and fail with RRR_ERR_BAD_SHAPE where it does not apply. */
 enum { RRR_GEMM_AUTO = 0, RRR_GEMM_TCGEN05 = 1, RRR_GEMM_MMA = 2, RRR_GEMM_PER_TOKEN = 3 };
 int rrr_gemm_kq_batched_path(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16_t* x_bf16,
                              float* y, int M, int K, int N, const float* residual, int path,

@@ -396,7 +396,10 @@ int rrr_gemm_kq_batched_path(rrr_ctx* ctx, int qtype, const void* w, const uint1
   RRR_BIND(ctx);
   const LaunchEnv env = make_env(ctx, stream);
   MmaPlan mplan;
-  if ((path == RRR_GEMM_AUTO || path == RRR_GEMM_MMA) &&
+  // Automatic choice: the mma.sync kernel from 3 tokens (a 16-token tile with the rows past
+  // M zero-filled by the X copy reads each weight once, where one GEMV per token reads the
+  // weights M times), the tcgen05 kernel above 64 tokens.
+  if ((path == RRR_GEMM_MMA || (path == RRR_GEMM_AUTO && M >= kMmaMinTokens)) &&
       plan_gemm_kq_mma(qtype, M, K, N, ctx->sm_count, &mplan)) {
     RRR_LAUNCH_CHECK(ctx, launch_gemm_kq_mma(env, qtype, w, x, y, M, K, N, mplan, residual),
                      "rrr_gemm_kq_batched (mma.sync) launch");
@@ -404,7 +407,7 @@ int rrr_gemm_kq_batched_path(rrr_ctx* ctx, int qtype, const void* w, const uint1
   }
   if (path == RRR_GEMM_MMA)
     return set_error(ctx, RRR_ERR_BAD_SHAPE,
-                     "rrr_gemm_kq_batched_path: the mma.sync kernel takes 16 <= M <= 64 and rows "
+                     "rrr_gemm_kq_batched_path: the mma.sync kernel takes 1 <= M <= 64 and rows "
                      "of a multiple of 16 bytes");
   TcPlan plan;
   if ((path == RRR_GEMM_AUTO || path == RRR_GEMM_TCGEN05) && M >= 16 &&

@@ -483,7 +483,7 @@ cudaError_t launch_q(const LaunchEnv& env, const MmaPlan& pl, const void* w, con
 
 bool plan_gemm_kq_mma(int qtype, int M, int K, int N, int sm_count, MmaPlan* pl) {
   const int bb = kq_block_bytes(qtype);
-  if (M < 16 || M > kMaxTn || K < 256 || K % 256 || N < 1 || bb == 0) return false;
+  if (M < 1 || M > kMaxTn || K < 256 || K % 256 || N < 1 || bb == 0) return false;
   // the raw stage is one TMA box: every row must start 16-byte aligned
   if (((long long)(K / 256) * bb) % 16 != 0) return false;
   MmaPlan r{};

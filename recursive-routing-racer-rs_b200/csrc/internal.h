@@ -73,9 +73,11 @@ cudaError_t launch_gemm_kq_tc(const LaunchEnv& env, int qtype, const void* w,
 // *d_ok when the device result matches the expected product).
 cudaError_t launch_mma_selftest(const LaunchEnv& env, int* d_ok);
 
-// Batched-token GEMM for 16 <= M <= 64 on mma.sync (gemm_kq_mma.cu): 256-row tiles, the
+// Batched-token GEMM for 1 <= M <= 64 on mma.sync (gemm_kq_mma.cu): 256-row tiles, the
 // weights dequantised into A fragments in registers. plan_gemm_kq_mma returns false for
-// shapes it does not handle (M outside [16, 64], rows not 16-byte aligned).
+// shapes it does not handle (M outside [1, 64], rows not 16-byte aligned). The automatic
+// choice takes it from kMmaMinTokens tokens (fewer run one GEMV per token).
+constexpr int kMmaMinTokens = 3;
 struct MmaPlan {
   int tn;          // tokens per tile: M rounded up to 16
   int m_tiles, n_tiles;

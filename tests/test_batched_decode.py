@@ -66,13 +66,21 @@ def _bf16(a, torch):
     return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy()
 
 
-def _bf16_reference(oracle, layers, on, wo, H0, torch, bf16_weights=True):
-    """The batched step with the tensor-core path's roundings made explicit: GEMM inputs
-    (and, for the tensor-core path, M >= 16, the dequantised weights) rounded to bf16
-    (nearest even), products summed in f64, everything else in f32 with the reference's
-    formulas (rms_norm (g*x)*inv, phi4.rs:593-599; silu, :601-606; position-0 attention
-    output = V of the head's KV group). M < 16 runs one GEMV per token on the bf16 rows
-    with the exact weights."""
+def _bf16_weights(M, qt, K):
+    """Whether the batched GEMM of M tokens rounds the dequantised weights to bf16: the
+    tensor-core kernels do (mma.sync from 3 tokens when a weight row is a multiple of 16
+    bytes, tcgen05 from 16); one GEMV per token (M <= 2, or rows that are not a multiple
+    of 16 bytes below 16 tokens) uses the exact weights."""
+    aligned = (K // 256) * BB[qt] % 16 == 0
+    return M >= 16 or (M >= 3 and aligned)
+
+
+def _bf16_reference(oracle, layers, on, wo, H0, torch):
+    """The batched step with the GEMM kernels' roundings made explicit: GEMM inputs (and,
+    where _bf16_weights says so, the dequantised weights) rounded to bf16 (nearest even),
+    products summed in f64, everything else in f32 with the reference's formulas
+    (rms_norm (g*x)*inv, phi4.rs:593-599; silu, :601-606; position-0 attention output = V
+    of the head's KV group)."""
     c = SMALL
     d, F, hd, nq, nkv = c["d_model"], c["ffn_dim"], c["head_dim"], c["n_heads"], c["n_kv_heads"]
     qkv_dim = (nq + 2 * nkv) * hd
@@ -83,7 +91,7 @@ def _bf16_reference(oracle, layers, on, wo, H0, torch, bf16_weights=True):
 
     def W(L, key, qt, K, N):
         w = oracle.dequant(qt, L[key], N * K).reshape(N, K)
-        return (_bf16(w, torch) if bf16_weights else w).astype(np.float64)
+        return (_bf16(w, torch) if _bf16_weights(H0.shape[0], qt, K) else w).astype(np.float64)
 
     for L in layers:
         xn = _bf16(rms(H, L["attn_norm"]), torch).astype(np.float64)
@@ -114,7 +122,7 @@ def test_batched_step_single_gpu(rrr, ctx, oracle, M):
     assert ctx.device_error() == 0
     layers, on, wo = _host_model(oracle, w, torch)
     H, LG, H0 = h.cpu().numpy(), lg.cpu().numpy(), hidden0.cpu().numpy()
-    Hr, LGr = _bf16_reference(oracle, layers, on, wo, H0, torch, bf16_weights=M >= 16)
+    Hr, LGr = _bf16_reference(oracle, layers, on, wo, H0, torch)
     for m in range(M):
         assert _rel(H[m], Hr[m]) < BF16_TOL, (m, _rel(H[m], Hr[m]))
         assert _rel(LG[m], LGr[m]) < BF16_TOL, (m, _rel(LG[m], LGr[m]))
@@ -152,8 +160,7 @@ ROPE = dict(rope_dim=96, theta=10000.0, attn_factor=1.190238)
 
 def _bf16_reference_kv(oracle, layers, on, wo, H0, torch, pos0, kc, vc, fac):
     """Prefill of M consecutive tokens at positions pos0.. with the step's bf16 roundings
-    made explicit (GEMM inputs rounded to bf16, exact weights: M < 16 runs one GEMV per
-    token): per layer the QKV rows, RoPE + f16 KV store of every row, causal attention of
+    made explicit (GEMM inputs rounded to bf16, weights as _bf16_weights says): per layer the QKV rows, RoPE + f16 KV store of every row, causal attention of
     each row over the cache, then O / FFN as _bf16_reference. kc / vc (uint16 [L, S, kvs])
     are updated."""
     c = SMALL
@@ -166,7 +173,8 @@ def _bf16_reference_kv(oracle, layers, on, wo, H0, torch, pos0, kc, vc, fac):
         return np.stack([oracle.rms_norm(r, g, c["eps"]) for r in x])
 
     def W(L, key, qt, K, N):
-        return oracle.dequant(qt, L[key], N * K).reshape(N, K).astype(np.float64)
+        w = oracle.dequant(qt, L[key], N * K).reshape(N, K)
+        return (_bf16(w, torch) if _bf16_weights(M, qt, K) else w).astype(np.float64)
 
     for li, L in enumerate(layers):
         xn = _bf16(rms(H, L["attn_norm"]), torch).astype(np.float64)
@@ -255,7 +263,7 @@ def test_phi4_forward_batched(rrr, ctx, oracle, M):
     assert ctx.device_error() == 0
     H, LG, AM = h.cpu().numpy(), lg.cpu().numpy(), am.cpu().numpy()
     layers, on, wo = _host_model(oracle, w, torch)
-    Hr, LGr = _bf16_reference(oracle, layers, on, wo, hidden0.cpu().numpy(), torch, bf16_weights=M >= 16)
+    Hr, LGr = _bf16_reference(oracle, layers, on, wo, hidden0.cpu().numpy(), torch)
     for m in range(M):
         assert _rel(H[m], Hr[m]) < BF16_TOL, (m, _rel(H[m], Hr[m]))
         assert _rel(LG[m], LGr[m]) < BF16_TOL, (m, _rel(LG[m], LGr[m]))

@@ -368,7 +368,7 @@ def test_gemm_batched(rrr, ctx, oracle, G, qt, M):
         assert rel_l2(got[m], oracle.gemv_kq(qt, raw, Xf[m], K, N)) < 1e-2
 
 
-GEMM_TCGEN05, GEMM_MMA = 1, 2   # RRR_GEMM_* of rrr_gemm_kq_batched_path
+GEMM_TCGEN05, GEMM_MMA, GEMM_PER_TOKEN = 1, 2, 3   # RRR_GEMM_* of rrr_gemm_kq_batched_path
 
 
 def _gemm_tc_case(rrr, ctx, oracle, G, qt, M, K, N, seed, repeats=1, path=GEMM_TCGEN05):
@@ -434,6 +434,9 @@ MMA_SHAPES = [
     (37, 1024, 530),     # ragged token tile (TN 48), 3 row tiles
     (48, 512, 19000),    # 75 row tiles: split-K 1
     (20, 8192, 3072),    # down-projection shape, 12 tiles x split-K 8
+    (3, 3072, 1000),     # 3 tokens in a 16-token tile (rows 3-15 zero-filled), ragged rows
+    (1, 2048, 256),      # one token (the forced path; the automatic choice runs a GEMV)
+    (9, 8192, 3072),     # down-projection shape below 16 tokens
 ]
 
 
@@ -473,13 +476,37 @@ def test_gemm_path_selection(rrr, ctx, oracle, G):
     assert ctx.device_error() == 0
 
 
+@pytest.mark.parametrize("qt,K", [(12, 1024), (13, 1024), (14, 2048), (14, 1024)])
+def test_gemm_auto_small_m(rrr, ctx, oracle, G, qt, K):
+    """The automatic choice below 16 tokens: one GEMV per token for M <= 2 and for rows
+    that are not a multiple of 16 bytes (Q6_K, K = 1024), the mma.sync kernel from 3
+    tokens otherwise; each result bit-identical to the forced kernel's."""
+    import torch
+    N = 512
+    L = rrr.ffi.lib()
+    w = G.dev(oracle.random_blocks(qt, N * (K // 256), np.random.default_rng(qt + K)))
+    aligned = (K // 256) * {12: 144, 13: 176, 14: 210}[qt] % 16 == 0
+    for M in (1, 2, 3, 8, 15):
+        x = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).to(torch.bfloat16).cuda()
+        want = GEMM_MMA if (M >= 3 and aligned) else GEMM_PER_TOKEN
+        ys = []
+        for path in (0, want):
+            y = torch.full((M, N), float("nan"), device="cuda")
+            ctx.check(L.rrr_gemm_kq_batched_path(ctx.h, qt, vp(w), vp(x), vp(y), M, K, N, None, path, None))
+            ys.append(y.cpu().numpy())
+        assert ctx.device_error() == 0
+        assert np.isfinite(ys[0]).all()
+        assert np.array_equal(ys[0], ys[1]), (M, want)
+
+
 @pytest.mark.parametrize("qt", QTYPES)
 @pytest.mark.parametrize("M,K,N,inplace", [(16, 1024, 768, True), (40, 1024, 768, True),
                                             (40, 768, 2048, False), (3, 512, 256, True),
                                             (300, 512, 256, True)])
 def test_gemm_tc_residual(rrr, ctx, oracle, G, qt, M, K, N, inplace):
     """rrr_gemm_kq_batched_ex: Y = X W^T + R with R == Y (in place) or separate, on the
-    split-K cluster path, the single-split path and the per-token path (M < 16)."""
+    split-K cluster path, the single-split path, the mma.sync path below 16 tokens and the
+    per-token path."""
     import torch
     rng = np.random.default_rng(M + K + N + qt)
     raw = oracle.random_blocks(qt, N * (K // 256), rng)
@@ -495,7 +522,9 @@ def test_gemm_tc_residual(rrr, ctx, oracle, G, qt, M, K, N, inplace):
     Y0 = Y.clone()
     R0 = Rd.clone()
     aligned_rows = (K // 256) * {12: 144, 13: 176, 14: 210}[qt] % 16 == 0
-    paths = [0] + ([GEMM_TCGEN05] if M >= 16 else []) + ([GEMM_MMA] if 16 <= M <= 64 and aligned_rows else [])
+    paths = [0] + ([GEMM_TCGEN05] if M >= 16 else []) + ([GEMM_MMA] if M <= 64 and aligned_rows else [])
+    if M < 16:
+        paths.append(GEMM_PER_TOKEN)
     for path in paths:
         Y.copy_(Y0)
         Rd.copy_(R0)
