@@ -532,7 +532,7 @@ def run_ours(args, rank, world, local_rank):
             "decode_batch64": decode_batch,
             "tp_decode": tp_decode,
             "batched_gemm": {"note": "configs[3]: rrr_gemm_kq_batched, automatic path (register-level mma.sync "
-                                     "for 16 <= M <= 64, tcgen05 + TMEM + TMA above; bf16 x bf16 -> f32); "
+                                     "for 3 <= M <= 64, tcgen05 + TMEM + TMA above; bf16 x bf16 -> f32); "
                                      "tensor_frac against the measured dense bf16 burst peak",
                              "cases": batched},
             "e2e": {"value": round(bytes_step / e2e_ms / 1e6, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
