@@ -268,7 +268,8 @@ def run_ours(args, rank, world, local_rank):
     # ---------------- batched-token GEMM: tcgen05 tiles, one launch per layer's
     # weights (32 distinct matrices per pass, larger than L2), M tokens of bf16 input
     batched = {}
-    for name, M in [(n, m) for n in ("gate_up", "down") for m in (16, 64, 256)]:
+    # configs[3]'s M = 16 / 64 / 256, and 4 / 8 tokens (the mma.sync kernel's 16-token tile)
+    for name, M in [(n, m) for n in ("gate_up", "down") for m in (4, 8, 16, 64, 256)]:
         _, qt, K, N = model.layers[0][name]
         Xb = torch.randn(M, K, device="cuda").to(torch.bfloat16)
         Yb = torch.empty(M, N, device="cuda")
@@ -291,7 +292,7 @@ def run_ours(args, rank, world, local_rank):
         wb = cfg.weight_bytes(qt, K, N) + 2 * M * K + 4 * M * N
         batched[f"{name}_M{M}"] = {
             "qtype": {12: "Q4_K", 13: "Q5_K", 14: "Q6_K"}[qt], "M": M, "K": K, "N": N,
-            "path": "mma.sync" if M <= 64 else "tcgen05",
+            "path": "mma.sync" if 3 <= M <= 64 else "tcgen05" if M > 64 else "per-token GEMV",
             "us_per_launch": round(us, 3), "TFLOPs": round(flops / us / 1e6, 1),
             "tensor_frac": round(flops / us / 1e6 / peaks(tensor=True)[0], 4),
             "GBps": round(wb / us / 1e3, 1), "hbm_frac": round(wb / us / 1e3 / peaks()[0], 4)}
