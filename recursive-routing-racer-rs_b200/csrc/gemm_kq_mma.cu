@@ -231,6 +231,11 @@ __global__ void __launch_bounds__(threads_for<MT>(), 1)
     fence_mbarrier_init();
   }
   __syncthreads();
+  // Programmatic dependent launch: the next grid may be scheduled now; every global
+  // access of this one (X, weights, Y, residual) comes after the previous grid's results
+  // are visible.
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------- producer
@@ -448,11 +453,13 @@ cudaError_t launch_t(const LaunchEnv& env, const MmaPlan& pl, const void* w, con
   cfg.blockDim = dim3(threads_for<MT>());
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = env.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = pl.splits;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (pl.splits > 1) {
@@ -464,6 +471,7 @@ cudaError_t launch_t(const LaunchEnv& env, const MmaPlan& pl, const void* w, con
     cfg.gridDim.z = s;
     attr[0].val.clusterDim.z = s;
   }
+  cfg.numAttrs = env.pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, xmap, wmap, p);
 }
 
