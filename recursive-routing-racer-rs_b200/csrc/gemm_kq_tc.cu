@@ -334,6 +334,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: the next grid may be scheduled now; every global
+  // access of this one comes after the previous grid's results are visible.
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------- raw-block producer: runs up to R super-blocks ahead
@@ -600,11 +604,13 @@ cudaError_t launch_t(const LaunchEnv& env, const TcPlan& pl, const void* w, cons
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = env.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = pl.splits;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (pl.splits > 1) {
@@ -616,6 +622,7 @@ cudaError_t launch_t(const LaunchEnv& env, const TcPlan& pl, const void* w, cons
     cfg.gridDim.z = s;
     attr[0].val.clusterDim.z = s;
   }
+  cfg.numAttrs = env.pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, map, wmap, p);
 }
 
