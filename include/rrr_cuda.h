@@ -96,7 +96,12 @@ int rrr_selftest_mma(rrr_ctx* ctx, int* ok);
  * workgroups [N,1,1]). W: N rows x K (raw blocks, 16-B aligned base), x: f32[K]
  * (16-B aligned), y: f32[N]. residual: NULL or f32[N]; when given, y = residual + W x
  * (the residual_add shader, phi4.rs:1028,1033, fused). y may alias residual.
- * Supported: K % 256 == 0, 256 <= K <= 16384, N >= 1. */
+ * Supported: K % 256 == 0, 256 <= K <= 16384, N >= 1.
+ * With programmatic dependent launch on (the default), the GEMV starts streaming weight
+ * blocks before the previous kernel on its stream has finished, so W must not be written
+ * by the kernel launched just before it on the same stream. The library's own fills
+ * (rrr_fill_*) end with a marker kernel that keeps this rule; a caller that writes
+ * weights with its own kernel must synchronise, or launch something between. */
 int rrr_gemv_kq(rrr_ctx* ctx, int qtype, const void* w_raw, const float* x, float* y,
                 int K, int N, const float* residual, void* stream);
 
@@ -217,8 +222,9 @@ int rrr_argmax_f32(rrr_ctx* ctx, const float* x, int n, int* out_index, void* st
  * cudaMalloc / cudaFree, and uses a fixed file-scope device scratch array (16 KB on every
  * GPU that loads this library, until the process exits). Same result as rrr_argmax_f32.
  * Limit: 1 <= n <= 8,388,608 (larger n is rejected with RRR_ERR_BAD_SHAPE). The first
- * call on a device looks up the scratch array's device address; make that first call
- * before any stream capture. Every call shares the scratch array, so calls that overlap
+ * call in a CUDA context looks up the scratch array's device address (cached per
+ * context, so a context created again after cudaDeviceReset gets a fresh lookup); make
+ * that first call before any stream capture. Every call shares the scratch array, so calls that overlap
  * on the GPU (concurrent streams) race; serialise them. Errors: rrr_last_error(NULL). */
 int rrr_argmax_f32_noalloc(const float* x, int n, int* out_index, void* stream);
 

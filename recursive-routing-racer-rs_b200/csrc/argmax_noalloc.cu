@@ -14,6 +14,7 @@
 // Result semantics are those of rrr_argmax_f32 (the reference's CPU scan,
 // src/model/phi4.rs:1172-1183): the first maximum wins, NaN is never selected, and the
 // index is 0 when no element compares greater than -inf.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -103,10 +104,41 @@ __global__ void __launch_bounds__(1024) argmax_noalloc_kernel(const float* __res
   }
 }
 
-// Device address of the scratch array, looked up once per device (the name of a
-// __device__ variable is not a device address in host code).
+// Device address of the scratch array (the name of a __device__ variable is not a device
+// address in host code), looked up once per CUDA context and cached with that context's
+// unique id. A context that is destroyed and created again (cudaDeviceReset, a host that
+// swaps contexts) gets a new id, so a stale address from a previous module load is never
+// used. The two driver queries come from cudaGetDriverEntryPoint, so the library does not
+// link libcuda.
 std::mutex g_setup_mutex;
-unsigned long long* g_scratch_addr[64] = {};
+struct ScratchSlot {
+  unsigned long long ctx_id;
+  unsigned long long* addr;
+};
+ScratchSlot g_slots[64] = {};
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
+// Id of the calling thread's current context (the runtime makes the device's primary
+// context current first if none is). Returns false if the driver entry points are missing.
+bool current_context_id(unsigned long long* id) {
+  if (!g_ctx_get_current || !g_ctx_get_id) {
+    void* f1 = nullptr;
+    void* f2 = nullptr;
+    cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = q1;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) != cudaSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) != cudaSuccess ||
+        q1 != cudaDriverEntryPointSuccess || q2 != cudaDriverEntryPointSuccess || !f1 || !f2)
+      return false;
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+    g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f2);
+  }
+  CUcontext c = nullptr;
+  if (g_ctx_get_current(&c) != CUDA_SUCCESS || !c) return false;
+  return g_ctx_get_id(c, id) == CUDA_SUCCESS;
+}
 
 }  // namespace
 
@@ -127,16 +159,22 @@ extern "C" int rrr_argmax_f32_noalloc(const float* x, int n, int* out_index, voi
   unsigned long long* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (!g_scratch_addr[dev]) {
+    // cudaGetDevice above made the device's primary context current if none was
+    unsigned long long id = 0;
+    if (!current_context_id(&id))
+      return set_error(nullptr, RRR_ERR_CUDA, "rrr_argmax_f32_noalloc: no current CUDA context");
+    ScratchSlot& slot = g_slots[dev];
+    if (!slot.addr || slot.ctx_id != id) {
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, g_argmax_noalloc_scratch);
       if (e != cudaSuccess || !p)
         return set_error(nullptr, RRR_ERR_CUDA,
                          "rrr_argmax_f32_noalloc: cudaGetSymbolAddress: %s",
                          cudaGetErrorString(e));
-      g_scratch_addr[dev] = static_cast<unsigned long long*>(p);
+      slot.addr = static_cast<unsigned long long*>(p);
+      slot.ctx_id = id;
     }
-    scratch = g_scratch_addr[dev];
+    scratch = slot.addr;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the finish counter must start at zero (a call cut short would leave it set)

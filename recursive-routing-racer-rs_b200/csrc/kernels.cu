@@ -420,6 +420,18 @@ cudaError_t launch_matmul_f32(const LaunchEnv& env, const float* A, const float*
                         env.pdl, A, B, C, M, K, N);
 }
 
+// An empty kernel launched without programmatic stream serialisation: it starts only once
+// every earlier kernel of the stream has completed and its writes are visible. Kernels
+// that read weights before their griddepcontrol.wait (the GEMV producers stream weight
+// blocks ahead of the dependency wait) may then overlap with this one safely, which they
+// could not with a fill kernel that has just written those weights.
+__global__ void full_dependency_marker_kernel() {}
+
+cudaError_t end_with_full_dependency(const LaunchEnv& env) {
+  full_dependency_marker_kernel<<<1, 32, 0, env.stream>>>();
+  return cudaGetLastError();
+}
+
 cudaError_t launch_fill_kquant(const LaunchEnv& env, int qtype, void* dst, int64_t rows,
                                int64_t bpr, int64_t src_row, int64_t block0, uint64_t seed) {
   const int64_t n_blocks = rows * bpr;
@@ -438,7 +450,8 @@ cudaError_t launch_fill_kquant(const LaunchEnv& env, int qtype, void* dst, int64
       break;
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
+  const cudaError_t e = cudaGetLastError();
+  return e != cudaSuccess ? e : end_with_full_dependency(env);
 }
 
 cudaError_t launch_fill_f32(const LaunchEnv& env, float* dst, int64_t n, int64_t offset,
@@ -446,7 +459,8 @@ cudaError_t launch_fill_f32(const LaunchEnv& env, float* dst, int64_t n, int64_t
   if (n <= 0) return cudaSuccess;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)env.sm_count * 32);
   fill_f32_kernel<<<grid, 256, 0, env.stream>>>(dst, n, offset, normal, a, b, seed);
-  return cudaGetLastError();
+  const cudaError_t e = cudaGetLastError();
+  return e != cudaSuccess ? e : end_with_full_dependency(env);
 }
 
 }  // namespace rrr

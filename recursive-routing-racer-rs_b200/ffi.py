@@ -1,8 +1,8 @@
 """ctypes binding of include/rrr_cuda.h (librrr_cuda.so, built in-tree for sm_100a).
 
-This is the Python side of the C ABI; a Rust host would bind the same header with an
-`extern "C"` block. Loading fails loudly if the library is missing:
-there is no fallback implementation.
+This is the Python side of the C ABI; a Rust host binds the same header with an
+`extern "C"` block. Loading fails loudly if the library is missing: there is no fallback
+implementation.
 """
 from __future__ import annotations
 

@@ -5,15 +5,20 @@ capture selects (`ncu -k regex:<kernel> -s <skip> -c <count>`), checks the conte
 device error flag and prints "<case> ok". Sizes are the Phi-4-mini layer shapes, so the
 DRAM figures of a capture are those of the bench's per-GEMV lines.
 
-    python -m recursive-routing-racer-rs_b200.profcases gemv            # 3 GEMV shapes x 6
-    python -m recursive-routing-racer-rs_b200.profcases decode --layers 32 [--max-seq 2048 --pos 1024]
-    python -m recursive-routing-racer-rs_b200.profcases gemm --m 256    # batched tcgen05 GEMM
-    python -m recursive-routing-racer-rs_b200.profcases attn --pos 1024 # RoPE + KV + attention
-    python -m recursive-routing-racer-rs_b200.profcases batched --m 64  # M-token decode step
+    python tests/profcases.py gemv            # 3 GEMV shapes x 6
+    python tests/profcases.py decode --layers 32 [--max-seq 2048 --pos 1024]
+    python tests/profcases.py gemm --m 256    # batched tcgen05 GEMM
+    python tests/profcases.py attn --pos 1024 # RoPE + KV + attention
+    python tests/profcases.py batched --m 64  # M-token decode step
 """
 import argparse
 import importlib
+import os
+import sys
 from ctypes import c_void_p
+
+# run as a script from the repository root: the package directory sits one level up
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 _PKG = "recursive-routing-racer-rs_b200"
 BLOCK_BYTES = {12: 144, 13: 176, 14: 210}

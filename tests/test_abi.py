@@ -45,8 +45,9 @@ def _header_params(name):
 
 
 def test_rust_binding_in_integration_doc_matches_header():
-    """INTEGRATION.md's Rust extern block (the binding a maintainer adds to the reference
-    crate) declares every header function with the same number of parameters."""
+    """The Rust extern block of the integration guide (the binding a maintainer adds to
+    the reference crate) declares every header function with the same number of
+    parameters."""
     doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
     block = doc[doc.index("```rust"):]
     block = block[:block.index("```", 7)]
