@@ -79,6 +79,13 @@ int rrr_sync(rrr_ctx* ctx, void* stream);
  * a token id outside the embedding table (code 6: RRR_ERR_BAD_SHAPE). Synchronises the
  * device. *code = 0 if no kernel reported an error. */
 int rrr_check_device_error(rrr_ctx* ctx, int* code);
+/* Limit of every bounded device-side wait of this context's kernels (bulk-copy and ring
+ * barriers, peer flags of the exchanges), in ns; 0 restores the default of 1 s. A wait
+ * that runs out records its code in the device error flag and the kernel returns, so
+ * rrr_check_device_error reports RRR_ERR_TIMEOUT and the context stays usable. Range
+ * [1e5, 6e10] ns. No reference counterpart (the reference's fence waits are unbounded,
+ * engine.rs:312,369). */
+int rrr_set_wait_limit(rrr_ctx* ctx, uint64_t ns);
 /* Programmatic dependent launch (default on): each kernel of the library may start while
  * the previous kernel on its stream finishes (weights stream early; inputs are read after
  * the grid dependency wait). enable = 0 serialises every launch (a debugging aid). */

@@ -295,6 +295,19 @@ int rrr_sync(rrr_ctx* ctx, void* stream) {
   return RRR_OK;
 }
 
+int rrr_set_wait_limit(rrr_ctx* ctx, uint64_t ns) {
+  RRR_CHECK_CTX(ctx);
+  if (ns != 0 && (ns < 100000ull || ns > 60000000000ull))
+    return set_error(ctx, RRR_ERR_INVALID_ARG,
+                     "rrr_set_wait_limit: %llu ns outside [1e5, 6e10] (0 = the 1 s default)",
+                     (unsigned long long)ns);
+  RRR_BIND(ctx);
+  const unsigned long long v = ns;
+  RRR_LAUNCH_CHECK(ctx, cudaMemcpy(ctx->d_err + rrr::kWaitLimitSlot, &v, sizeof v, cudaMemcpyHostToDevice),
+                   "rrr_set_wait_limit: write");
+  return RRR_OK;
+}
+
 int rrr_check_device_error(rrr_ctx* ctx, int* code) {
   RRR_CHECK_CTX(ctx);
   if (!code) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_check_device_error: null code");

@@ -51,16 +51,18 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
   return v;
 }
 
-// The value of word p once its epoch is e; gives up (ok = false) after kWaitLimitNs.
+// The value of word p once its epoch is e; gives up (ok = false) after the context's wait
+// limit (wait_limit_ns).
 __device__ __forceinline__ float wait_word(const unsigned long long* p, unsigned e, bool& ok,
                                            int* err) {
   unsigned long long w = ld_relaxed_sys_u64(p);
   if ((unsigned)(w >> 32) != e && ok) {
     const uint64_t t0 = globaltimer_ns();
+    const uint64_t limit = wait_limit_ns(err);
     for (int i = 0;; ++i) {
       w = ld_relaxed_sys_u64(p);
       if ((unsigned)(w >> 32) == e) break;
-      if ((i & 63) == 63 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      if ((i & 63) == 63 && globaltimer_ns() - t0 > limit) {
         atomicCAS(err, 0, kDevErrCommTimeout);
         ok = false;
         break;

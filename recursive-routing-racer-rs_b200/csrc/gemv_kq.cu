@@ -9,12 +9,14 @@
 //    complete_tx) into a ring of shared-memory stages; consumers free a stage through an
 //    "empty" mbarrier. Every wait is bounded (%globaltimer) and reports through the
 //    context's error flag instead of hanging.
-//  * x is decomposed once per CTA into three int8 "digits" per element against a per-
-//    256-element scale xs: x ~= xs*(d0 + d1/2^7 + d2/2^14), |error| <= xs*2^-15 (about
-//    f32 precision). The per-scale-group sums sum_j q_j*x_j then come from exact integer
-//    tensor-core dot products (mma.sync m16n8k32, u8 quants x s8 digits, s32
-//    accumulate): a 16-row x 32-weight tile per instruction, the digits of two scale
-//    groups in B columns 0-2 and 3-5. Scales are applied by integer multiply-add per
+//  * x is decomposed once per CTA into four int8 "digits" per element against a per-
+//    256-element power-of-two scale xs = 2^(E-5), E = floor(log2 max|x|):
+//    x ~= xs*(d0 + d1/2^7 + d2/2^14 + d3/2^21), |error| <= xs*2^-22 <= max|x|*2^-27
+//    (elements within 1/8 of the block maximum are represented exactly). The per-scale-
+//    group sums sum_j q_j*x_j then come from exact integer tensor-core dot products
+//    (mma.sync m16n8k32, u8 quants x s8 digits, s32 accumulate): a 16-row x 32-weight
+//    tile per instruction, the digits of two scale groups in B columns 0-3 and 4-7.
+//    Scales are applied by integer multiply-add per
 //    group, d / dmin in f32 once per half block. The CUDA cores do about one instruction
 //    per weight, so the kernel stays memory-bound. Dequantised weights are never
 //    materialised; the bit-exact dequantisation is rrr_dequant_kq (kernels.cu).
@@ -98,9 +100,9 @@ __device__ __forceinline__ int byte_sext(uint32_t w, uint32_t sel) {
 }
 
 // Lane roles inside an MMA tile: rows g and g+8 of the A operand; B column n = g carries
-// digit n of scale group A (n = 0..2) or digit n-4 of group B (n = 4..6), columns 3 and 7
-// are zero; the lane's D columns 2*tig, 2*tig+1 therefore belong to a single group
-// (hb = tig >> 1), so one scale per row applies to both.
+// digit n of scale group A (n = 0..3) or digit n-4 of group B (n = 4..7); the lane's D
+// columns 2*tig, 2*tig+1 therefore belong to a single group (hb = tig >> 1), so one scale
+// per row applies to both.
 struct Lane {
   int g, tig, hb;
   uint32_t mA, mB;  // masks selecting which half of a compact B fragment this lane fills
@@ -119,14 +121,14 @@ __device__ __forceinline__ Lane make_lane(int lane, bool q4) {
   L.msel0 = 0x7440u | (uint32_t)(2 * (L.tig & 1));
   L.msel1 = 0x7440u | (uint32_t)(2 * (L.tig & 1) + 1);
   L.ssel = 0x4440u | (uint32_t)L.hb;
-  L.mA = L.g < 3 ? 0xFFFFFFFFu : 0u;
-  L.mB = (L.g >= 4 && L.g < 7) ? 0xFFFFFFFFu : 0u;
-  L.dsel = (L.g < 3) ? L.g : (L.g >= 4 && L.g < 7) ? L.g - 4 : 0;
+  L.mA = L.g < 4 ? 0xFFFFFFFFu : 0u;
+  L.mB = L.g >= 4 ? 0xFFFFFFFFu : 0u;
+  L.dsel = L.g & 3;
   L.frag_off = (L.g * 4 + L.tig) * 16;
-  // columns: tig 0 -> (d0, d1), tig 1 -> (d2, 0), tig 2 -> (d0, d1), tig 3 -> (d2, 0)
+  // columns: tig 0 -> (d0, d1), tig 1 -> (d2, d3), tig 2 -> (d0, d1), tig 3 -> (d2, d3)
   const float scale = (q4 && L.hb) ? (1.f / 16.f) : 1.f;  // Q4_K high nibbles enter x16
   L.w0 = ((L.tig & 1) ? (1.f / 16384.f) : 1.f) * scale;
-  L.w1 = ((L.tig & 1) ? 0.f : (1.f / 128.f)) * scale;
+  L.w1 = ((L.tig & 1) ? (1.f / 2097152.f) : (1.f / 128.f)) * scale;
   return L;
 }
 
@@ -412,8 +414,8 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
 // Digits, block scales and partial sums of the GEMV input, in one pass over x: warp w
 // handles blocks w, w+8, ..., loading up to kPrepGroup blocks at once (one L2 round trip per
 // group while the weight stream loads the memory system). The digits quantise gamma*x per
-// 256-block (the RMS factor cancels in T = round(v*127*2^14/max|v|)); misc[warp] receives
-// the warp's sum of x^2 (RMSNORM) for the factor applied to the row sums.
+// 256-block (the RMS factor is applied to the finished row sums instead); misc[warp]
+// receives the warp's sum of x^2 (RMSNORM) for that factor.
 constexpr int kPrepGroup = 2;
 
 template <bool FRAG>
@@ -457,33 +459,37 @@ __device__ void prepare_x(const GemvParams& p, int8_t* dig, float* xscale, float
       if (g >= ng) break;
       const int b = bg + g * NPW;
       const float* v = vg[g];
-      // T = round(x * 127 * 2^14 / max) as an integer (|T| <= 127 * 2^14 < 2^22, through
-      // the 1.5 * 2^23 magic constant), split into balanced base-128 digits:
-      // T = q0 * 2^14 + q1 * 2^7 + q2 with q0 in [-127, 127], q1, q2 in [-64, 64].
-      const float inv = m[g] > 0.f ? __fdividef(127.f * 16384.f, m[g]) : 0.f;
-      int q0[8], q1[8], q2[8];
+      // Block scale xs = 2^(E-5) with E = floor(log2 max) (from the exponent field; E is
+      // clamped to >= -100 so that 2^(26-E) stays finite, which only coarsens blocks whose
+      // maximum is below 2^-100), so |v| / xs < 64. T = round(v * 2^21 / xs) is one
+      // rounding of a power-of-two scaling (|T| < 2^27), split into balanced base-128
+      // digits: T = q0 * 2^21 + q1 * 2^14 + q2 * 2^7 + q3, every digit in [-64, 64].
+      const int E = max((int)((__float_as_uint(m[g]) >> 23) & 0xFFu) - 127, -100);
+      const float up = __uint_as_float((uint32_t)(127 + 26 - E) << 23);  // 2^(26-E)
+      int q0[8], q1[8], q2[8], q3[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int T = __float_as_int(__fmaf_rn(v[i], inv, 12582912.0f)) - 0x4B400000;
-        q0[i] = (T + 8192) >> 14;
-        const int r = T - q0[i] * 16384;
-        q1[i] = (r + 64) >> 7;
-        q2[i] = r - q1[i] * 128;
+        const int T = __float2int_rn(__fmul_rn(v[i], up));
+        q0[i] = (T + (1 << 20)) >> 21;
+        int r = T - q0[i] * (1 << 21);
+        q1[i] = (r + (1 << 13)) >> 14;
+        r -= q1[i] * (1 << 14);
+        q2[i] = (r + 64) >> 7;
+        q3[i] = r - q2[i] * 128;
       }
       if (FRAG) {
         // per-lane B fragments: pair P = 4b + lane/8, group (lane>>2)&1, tig = lane&3;
         // column n of the pair at n*64 + tig*16 holds (b0, b1) of MMA 1 and MMA 2
         const int grp = (lane >> 2) & 1;
         uint8_t* fb = reinterpret_cast<uint8_t*>(dig) + (b * 4 + (lane >> 3)) * 512 + (lane & 3) * 16;
-        const uint32_t m1[3] = {pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q1[0], q1[1], q1[2], q1[3]),
-                                pack4(q2[0], q2[1], q2[2], q2[3])};
-        const uint32_t m2[3] = {pack4(q0[4], q0[5], q0[6], q0[7]), pack4(q1[4], q1[5], q1[6], q1[7]),
-                                pack4(q2[4], q2[5], q2[6], q2[7])};
+        const uint32_t m1[4] = {pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q1[0], q1[1], q1[2], q1[3]),
+                                pack4(q2[0], q2[1], q2[2], q2[3]), pack4(q3[0], q3[1], q3[2], q3[3])};
+        const uint32_t m2[4] = {pack4(q0[4], q0[5], q0[6], q0[7]), pack4(q1[4], q1[5], q1[6], q1[7]),
+                                pack4(q2[4], q2[5], q2[6], q2[7]), pack4(q3[4], q3[5], q3[6], q3[7])};
 #pragma unroll
-        for (int dgt = 0; dgt < 3; ++dgt)
+        for (int dgt = 0; dgt < 4; ++dgt)
           *reinterpret_cast<uint4*>(fb + (grp * 4 + dgt) * 64) =
               grp ? make_uint4(0u, m1[dgt], 0u, m2[dgt]) : make_uint4(m1[dgt], 0u, m2[dgt], 0u);
-        *reinterpret_cast<uint4*>(fb + (grp * 4 + 3) * 64) = make_uint4(0u, 0u, 0u, 0u);
       } else {
         const int k0 = b * 256 + lane * 8;
         *reinterpret_cast<uint2*>(dig + k0) =
@@ -492,10 +498,12 @@ __device__ void prepare_x(const GemvParams& p, int8_t* dig, float* xscale, float
             make_uint2(pack4(q1[0], q1[1], q1[2], q1[3]), pack4(q1[4], q1[5], q1[6], q1[7]));
         *reinterpret_cast<uint2*>(dig + 2 * p.dig_stride + k0) =
             make_uint2(pack4(q2[0], q2[1], q2[2], q2[3]), pack4(q2[4], q2[5], q2[6], q2[7]));
+        *reinterpret_cast<uint2*>(dig + 3 * p.dig_stride + k0) =
+            make_uint2(pack4(q3[0], q3[1], q3[2], q3[3]), pack4(q3[4], q3[5], q3[6], q3[7]));
       }
       if ((lane & 1) == 0) xsum[b * 16 + (lane >> 1)] = s16[g];
       if ((lane & 3) == 0) xsum[p.K / 16 + b * 8 + (lane >> 2)] = s32[g];
-      if (lane == 0) xscale[b] = m[g] / 127.f;
+      if (lane == 0) xscale[b] = m[g] > 0.f ? __uint_as_float((uint32_t)(127 + E - 5) << 23) : 0.f;
     }
   }
   ssq = warp_sum(ssq);
@@ -769,7 +777,7 @@ int plan_layout(GemvParams& p, bool frag) {
   p.row_stride = rs;
   p.stage_bytes = kTileRows * p.row_stride;
   p.dig_stride = p.K + 96;
-  const int dig_bytes = frag ? p.K * 8 : 3 * p.dig_stride;
+  const int dig_bytes = frag ? p.K * 8 : 4 * p.dig_stride;
   int fixed = kGroups * 2 * kMaxStages * 8 + dig_bytes + 16;
   fixed += p.nb * 4 + 16 + (p.K / 16) * 4 + (p.K / 32) * 4;  // xscale, xsum16, xsum32
   fixed += kGroups * kSlots * kNW * kTileRows * 4;            // red

@@ -8,6 +8,11 @@
 
 namespace rrr {
 
+// The context's device error block (256 bytes): int [0] is the error flag kernels set, the
+// 64-bit word at int index kWaitLimitSlot holds the bounded waits' limit in ns (0 = the
+// 1 s default), bytes 64-79 the argmax key and counter.
+constexpr int kWaitLimitSlot = 8;
+
 struct LaunchEnv {
   cudaStream_t stream;
   int sm_count;

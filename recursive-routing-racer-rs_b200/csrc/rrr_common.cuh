@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "../../include/rrr_cuda.h"
+#include "internal.h"
 
 namespace rrr {
 
@@ -19,9 +20,15 @@ enum DeviceErr : int {
   kDevErrPosition = 6,      // a position outside the cache, or a token id outside the table
 };
 
-// A wait gives up after this many nanoseconds of %globaltimer (about one second); it
-// then records an error and lets the kernel return instead of hanging the GPU.
+// A wait gives up after this many nanoseconds of %globaltimer (about one second) unless the
+// context sets another limit (rrr_set_wait_limit); it then records an error and lets the
+// kernel return instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
+__device__ __forceinline__ uint64_t wait_limit_ns(const int* err) {
+  if (!err) return kWaitLimitNs;
+  const uint64_t v = *reinterpret_cast<const volatile unsigned long long*>(err + kWaitLimitSlot);
+  return v ? v : kWaitLimitNs;
+}
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -82,15 +89,16 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
   return ok != 0;
 }
 
-// Waits for phase `parity` of `bar` to complete. Gives up after kWaitLimitNs: records
-// `code` in *err (first error wins) and returns false.
+// Waits for phase `parity` of `bar` to complete. Gives up after the context's wait limit
+// (wait_limit_ns): records `code` in *err (first error wins) and returns false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
                                                   int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(err);
   while (true) {
     if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }

@@ -122,6 +122,7 @@ PROTOS = {
     "rrr_phi4_launches_per_step": (c_int, [vp, POINTER(c_int)]),
     "rrr_phi4_destroy": (c_int, [vp]),
     "rrr_set_pdl": (c_int, [vp, c_int]),
+    "rrr_set_wait_limit": (c_int, [vp, c_uint64]),
     "rrr_position_advance": (c_int, [vp, vp, c_int, vp]),
     "rrr_window_bf16": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, vp]),
     "rrr_gemm_kq_batched_path": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, c_int, vp, c_int, vp]),

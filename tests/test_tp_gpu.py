@@ -2,7 +2,7 @@
 
 * the range fills give exactly the slices of the full synthetic tensors;
 * the G-rank split run in one process (exchanges done with torch ops, all shards on one
-  GPU) equals the 1-GPU rrr_phi4_forward step at G = 2 and 8 (8: O-proj windows that
+  GPU) equals the 1-GPU rrr_phi4_forward step at G = 2, 4 and 8 (8: O-proj windows that
   cut super-blocks) within 1e-4 relative L2 (only the summation order differs);
 * with 2+ GPUs: the run with one process per GPU, eager and as a CUDA graph, with the
   exchanges as NCCL collectives or as the peer-memory kernels, equals the 1-GPU step.
@@ -61,7 +61,7 @@ def _single_gpu(ctx, cfg, seed, hidden0):
     return out
 
 
-@pytest.mark.parametrize("G", [2, 8])
+@pytest.mark.parametrize("G", [2, 4, 8])
 def test_tp_split_emulated_matches_single_gpu(rrr, ctx, G):
     """Phi-4-mini shapes (2 layers, full vocab), all G ranks' shards on this GPU."""
     import torch
@@ -85,7 +85,7 @@ def test_tp_split_emulated_matches_single_gpu(rrr, ctx, G):
         w.close()
 
 
-@pytest.mark.parametrize("G", [2, 8])
+@pytest.mark.parametrize("G", [2, 4, 8])
 def test_tp_kv_decode_emulated_matches_single_gpu(rrr, ctx, G):
     """KV-cache decode at positions 0..3 (RoPE, f16 caches of the rank's KV heads, fused
     attention; the O-projection input is the heads' attention output in the rank's column
