@@ -154,6 +154,33 @@ class SyntheticPhi4TP:
         self.arena.free_all()
 
 
+class TPTimeout(RuntimeError):
+    """A collective did not complete before its host deadline (or its group failed); the
+    process group has been torn down, so no later collective can wait on it."""
+
+
+def all_reduce_with_deadline(t, timeout_s: float, group=None) -> None:
+    """dist.all_reduce(t) (sum, in place) that gives up after `timeout_s` seconds of host
+    time: a rank that skipped the collective, stalled or died makes the call raise
+    TPTimeout instead of blocking, and the group is destroyed (its pending work is
+    abandoned). The reference waits on its fences without a limit (engine.rs:312,369)."""
+    import datetime
+    import torch.distributed as dist
+    work = dist.all_reduce(t, group=group, async_op=True)
+    try:
+        done = work.wait(timeout=datetime.timedelta(seconds=timeout_s))
+        err = None if done is not False else "the wait returned False"
+    except RuntimeError as e:
+        err = str(e)
+    if err is not None:
+        try:
+            dist.destroy_process_group(group)
+        except Exception:
+            pass
+        raise TPTimeout(f"all_reduce missed its {timeout_s:g} s host deadline or its group "
+                        f"failed: {err}")
+
+
 class P2PComm:
     """The C ABI's NVLink peer-memory exchanges (rrr_comm_*) for one rank; the 64-byte IPC
     handles are swapped with torch.distributed.all_gather_object."""

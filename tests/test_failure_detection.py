@@ -1,0 +1,147 @@
+"""Failure detection, exercised without faulting, trapping or hanging a GPU.
+
+* On the GPU: rank 0 of a 2-rank peer-memory exchange (rrr_comm, NVLink/IPC mappings)
+  whose rank 1 process maps its buffer but never calls the exchange. Rank 0's bounded wait
+  runs out after the context's wait limit (set to 50 ms), the kernel records its code and
+  returns, rrr_check_device_error reports RRR_ERR_TIMEOUT, and the context and the GPU
+  keep working (a GEMV afterwards matches the oracle). The reference waits on its fences
+  with no limit (src/gpu/engine.rs:312,369: u64::MAX).
+* On the host (gloo ranks on CPU): a collective that one rank skips ends on the other
+  rank with a clean timeout error from the host deadline, and the group is torn down.
+"""
+import ctypes
+import importlib
+import multiprocessing as mp
+import os
+import socket
+import time
+from ctypes import c_void_p
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+tp = importlib.import_module("recursive-routing-racer-rs_b200.tp")
+
+
+def _idle_peer(q, done):
+    """Rank 1: creates its exchange buffer, publishes the IPC handle, never exchanges."""
+    rrr = importlib.import_module("recursive-routing-racer-rs_b200")
+    L = rrr.ffi.lib()
+    ctx = rrr.Context(0)
+    comm = c_void_p()
+    h = ctypes.create_string_buffer(64)
+    ctx.check(L.rrr_comm_create(ctx.h, 1, 2, 4096, ctypes.byref(comm), h))
+    q.put(bytes(h.raw))
+    done.wait(120)
+    L.rrr_comm_destroy(comm)
+    ctx.close()
+
+
+@pytest.mark.gpu
+def test_exchange_wait_expires_when_a_rank_never_arrives(rrr, ctx, oracle):
+    import torch
+    L = rrr.ffi.lib()
+    spawn = mp.get_context("spawn")
+    q, done = spawn.Queue(), spawn.Event()
+    peer = spawn.Process(target=_idle_peer, args=(q, done))
+    peer.start()
+    comm = c_void_p()
+    try:
+        peer_handle = q.get(timeout=120)
+        mine = ctypes.create_string_buffer(64)
+        ctx.check(L.rrr_comm_create(ctx.h, 0, 2, 4096, ctypes.byref(comm), mine))
+        handles = (ctypes.c_char * 128).from_buffer_copy(bytes(mine.raw) + peer_handle)
+        ctx.check(L.rrr_comm_connect(comm, handles))
+        ctx.check(L.rrr_set_wait_limit(ctx.h, 50_000_000))          # 50 ms
+        x = torch.ones(4096, device="cuda")
+        torch.cuda.synchronize()
+        t0 = time.time()
+        ctx.check(L.rrr_comm_allreduce_f32(comm, c_void_p(x.data_ptr()), 4096, None))
+        code = ctypes.c_int(0)
+        rc = L.rrr_check_device_error(ctx.h, ctypes.byref(code))
+        elapsed = time.time() - t0
+        assert rc == -7, rrr.ffi.last_error(ctx.h)                   # RRR_ERR_TIMEOUT
+        assert code.value == 5                                       # exchange wait gave up
+        assert 0.04 < elapsed < 5.0, elapsed
+        # the context and the GPU still answer: a GEMV checked against the oracle
+        ctx.check(L.rrr_set_wait_limit(ctx.h, 0))
+        rng = np.random.default_rng(5)
+        K, N = 3072, 256
+        raw = oracle.random_blocks(12, N * K // 256, rng)
+        xv = rng.standard_normal(K).astype(np.float32)
+        wd, xd = torch.from_numpy(raw).cuda(), torch.from_numpy(xv).cuda()
+        y = torch.empty(N, device="cuda")
+        ctx.check(L.rrr_gemv_kq(ctx.h, 12, c_void_p(wd.data_ptr()), c_void_p(xd.data_ptr()),
+                                c_void_p(y.data_ptr()), K, N, None, None))
+        assert rel_l2(y.cpu().numpy(), oracle.gemv_kq(12, raw, xv, K, N)) < 1e-4
+        assert ctx.device_error() == 0
+    finally:
+        L.rrr_set_wait_limit(ctx.h, 0)
+        if comm.value:
+            L.rrr_comm_disconnect(comm)
+            L.rrr_comm_destroy(comm)
+        done.set()
+        peer.join(60)
+        if peer.is_alive():
+            peer.kill()
+    assert peer.exitcode == 0
+
+
+def test_wait_limit_range_is_checked(rrr):
+    """Out-of-range limits are rejected; no GPU is needed to reach the check."""
+    L = rrr.ffi.lib()
+    assert L.rrr_set_wait_limit(None, 0) == -1
+
+
+# ------------------------------------------------------------------ host side, gloo
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_rank(rank, port, q):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+    t = torch.ones(1000)
+    # step 1: both ranks take part
+    tp.all_reduce_with_deadline(t, timeout_s=30.0)
+    ok1 = float(t[0]) == 2.0
+    if rank == 1:
+        # rank 1 stays alive but never joins the next collective (a stalled rank)
+        q.put((rank, ok1, None, 0.0))
+        time.sleep(6.0)
+        return
+    t0 = time.time()
+    err = None
+    try:
+        tp.all_reduce_with_deadline(t, timeout_s=2.0)
+    except tp.TPTimeout as e:
+        err = str(e)
+    q.put((rank, ok1, err, time.time() - t0))
+
+
+def test_host_deadline_on_a_skipped_collective():
+    spawn = mp.get_context("spawn")
+    q = spawn.Queue()
+    port = _free_port()
+    procs = [spawn.Process(target=_gloo_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, ok1, err, el = q.get(timeout=120)
+        res[r] = (ok1, err, el)
+    for p in procs:
+        p.join(60)
+        if p.is_alive():
+            p.kill()
+        assert p.exitcode == 0
+    assert res[0][0] and res[1][0]
+    assert res[0][1] is not None and "deadline" in res[0][1]
+    assert 1.5 < res[0][2] < 20.0
