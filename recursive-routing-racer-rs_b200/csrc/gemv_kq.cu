@@ -10,9 +10,9 @@
 //    "empty" mbarrier. Every wait is bounded (%globaltimer) and reports through the
 //    context's error flag instead of hanging.
 //  * x is decomposed once per CTA into four int8 "digits" per element against a per-
-//    256-element power-of-two scale xs = 2^(E-5), E = floor(log2 max|x|):
-//    x ~= xs*(d0 + d1/2^7 + d2/2^14 + d3/2^21), |error| <= xs*2^-22 <= max|x|*2^-27
-//    (elements within 1/8 of the block maximum are represented exactly). The per-scale-
+//    256-element power-of-two scale xs = 2^(E-20), E = floor(log2 max|x|):
+//    x ~= xs*(d0 + 256*d1 + 65536*d2 + d3/128), |error| <= xs/256 <= max|x|*2^-28
+//    (elements within 1/16 of the block maximum are represented exactly). The per-scale-
 //    group sums sum_j q_j*x_j then come from exact integer tensor-core dot products
 //    (mma.sync m16n8k32, u8 quants x s8 digits, s32 accumulate): a 16-row x 32-weight
 //    tile per instruction, the digits of two scale groups in B columns 0-3 and 4-7.
@@ -127,8 +127,8 @@ __device__ __forceinline__ Lane make_lane(int lane, bool q4) {
   L.frag_off = (L.g * 4 + L.tig) * 16;
   // columns: tig 0 -> (d0, d1), tig 1 -> (d2, d3), tig 2 -> (d0, d1), tig 3 -> (d2, d3)
   const float scale = (q4 && L.hb) ? (1.f / 16.f) : 1.f;  // Q4_K high nibbles enter x16
-  L.w0 = ((L.tig & 1) ? (1.f / 16384.f) : 1.f) * scale;
-  L.w1 = ((L.tig & 1) ? (1.f / 2097152.f) : (1.f / 128.f)) * scale;
+  L.w0 = ((L.tig & 1) ? 65536.f : 1.f) * scale;
+  L.w1 = ((L.tig & 1) ? (1.f / 128.f) : 256.f) * scale;
   return L;
 }
 
@@ -407,8 +407,11 @@ __device__ __forceinline__ float finish8(const GemvParams& p, float v[8], const 
   return ss;
 }
 
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+// Byte `i` of four words, packed (a.bi, b.bi, c.bi, d.bi).
+template <int I>
+__device__ __forceinline__ uint32_t gather_byte(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  constexpr uint32_t sel = (uint32_t)I | ((uint32_t)(I + 4) << 4);  // (x.bI, y.bI) in bytes 0, 1
+  return __byte_perm(__byte_perm(a, b, sel), __byte_perm(c, d, sel), 0x5410);
 }
 
 // Digits, block scales and partial sums of the GEMV input, in one pass over x: warp w
@@ -459,51 +462,56 @@ __device__ void prepare_x(const GemvParams& p, int8_t* dig, float* xscale, float
       if (g >= ng) break;
       const int b = bg + g * NPW;
       const float* v = vg[g];
-      // Block scale xs = 2^(E-5) with E = floor(log2 max) (from the exponent field; E is
-      // clamped to >= -100 so that 2^(26-E) stays finite, which only coarsens blocks whose
-      // maximum is below 2^-100), so |v| / xs < 64. T = round(v * 2^21 / xs) is one
-      // rounding of a power-of-two scaling (|T| < 2^27), split into balanced base-128
-      // digits: T = q0 * 2^21 + q1 * 2^14 + q2 * 2^7 + q3, every digit in [-64, 64].
+      // Block scale xs = 2^(E-20) with E = floor(log2 max) (from the exponent field; E
+      // is clamped to >= -100 so that 1/xs stays finite, which only coarsens blocks whose
+      // maximum is below 2^-100), so |v| / xs < 2^21. T = round(v / xs) comes out of one
+      // FMA with the magic number 1.5*2^23 + 0x8080: the result lies in [2^23, 2^24), so its
+      // mantissa holds T + 0x8080 + 2^22 exactly, and bytes 0, 1, 2 of the float are the
+      // base-256 digits b0, b1 (unsigned) and b2 (7 bits) of T + 0x8080 + 2^22. The signed
+      // digits are d0 = b0 - 128, d1 = b1 - 128 (a flip of bit 7), d2 = b2 - 64, so that
+      // T = d0 + 256*d1 + 65536*d2 with d0, d1 in [-128, 127] and d2 in [-32, 32]. The
+      // remainder v/xs - T (exact in f32, |.| <= 1/2) gives d3 = round(128 * remainder) in
+      // [-64, 64] from a second magic FMA (byte 0, offset 128).
       const int E = max((int)((__float_as_uint(m[g]) >> 23) & 0xFFu) - 127, -100);
-      const float up = __uint_as_float((uint32_t)(127 + 26 - E) << 23);  // 2^(26-E)
-      int q0[8], q1[8], q2[8], q3[8];
+      const float up = __uint_as_float((uint32_t)(127 + 20 - E) << 23);  // 1/xs = 2^(20-E)
+      constexpr float kMagicHi = 12615808.0f;  // 1.5*2^23 + 0x8080
+      constexpr float kMagicLo = 12583040.0f;  // 1.5*2^23 + 128
+      uint32_t hi[8], lo[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int T = __float2int_rn(__fmul_rn(v[i], up));
-        q0[i] = (T + (1 << 20)) >> 21;
-        int r = T - q0[i] * (1 << 21);
-        q1[i] = (r + (1 << 13)) >> 14;
-        r -= q1[i] * (1 << 14);
-        q2[i] = (r + 64) >> 7;
-        q3[i] = r - q2[i] * 128;
+        const float a = __fmaf_rn(v[i], up, kMagicHi);
+        const float r = __fmaf_rn(v[i], up, -__fsub_rn(a, kMagicHi));
+        hi[i] = __float_as_uint(a);
+        lo[i] = __float_as_uint(__fmaf_rn(r, 128.f, kMagicLo));
       }
+      // digit rows of elements 0-3 (m1) and 4-7 (m2)
+      auto d2fix = [](uint32_t w) { return ((w | 0x80808080u) - 0x40404040u) ^ 0x80808080u; };
+      const uint32_t m1[4] = {gather_byte<0>(hi[0], hi[1], hi[2], hi[3]) ^ 0x80808080u,
+                              gather_byte<1>(hi[0], hi[1], hi[2], hi[3]) ^ 0x80808080u,
+                              d2fix(gather_byte<2>(hi[0], hi[1], hi[2], hi[3])),
+                              gather_byte<0>(lo[0], lo[1], lo[2], lo[3]) ^ 0x80808080u};
+      const uint32_t m2[4] = {gather_byte<0>(hi[4], hi[5], hi[6], hi[7]) ^ 0x80808080u,
+                              gather_byte<1>(hi[4], hi[5], hi[6], hi[7]) ^ 0x80808080u,
+                              d2fix(gather_byte<2>(hi[4], hi[5], hi[6], hi[7])),
+                              gather_byte<0>(lo[4], lo[5], lo[6], lo[7]) ^ 0x80808080u};
       if (FRAG) {
         // per-lane B fragments: pair P = 4b + lane/8, group (lane>>2)&1, tig = lane&3;
         // column n of the pair at n*64 + tig*16 holds (b0, b1) of MMA 1 and MMA 2
         const int grp = (lane >> 2) & 1;
         uint8_t* fb = reinterpret_cast<uint8_t*>(dig) + (b * 4 + (lane >> 3)) * 512 + (lane & 3) * 16;
-        const uint32_t m1[4] = {pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q1[0], q1[1], q1[2], q1[3]),
-                                pack4(q2[0], q2[1], q2[2], q2[3]), pack4(q3[0], q3[1], q3[2], q3[3])};
-        const uint32_t m2[4] = {pack4(q0[4], q0[5], q0[6], q0[7]), pack4(q1[4], q1[5], q1[6], q1[7]),
-                                pack4(q2[4], q2[5], q2[6], q2[7]), pack4(q3[4], q3[5], q3[6], q3[7])};
 #pragma unroll
         for (int dgt = 0; dgt < 4; ++dgt)
           *reinterpret_cast<uint4*>(fb + (grp * 4 + dgt) * 64) =
               grp ? make_uint4(0u, m1[dgt], 0u, m2[dgt]) : make_uint4(m1[dgt], 0u, m2[dgt], 0u);
       } else {
         const int k0 = b * 256 + lane * 8;
-        *reinterpret_cast<uint2*>(dig + k0) =
-            make_uint2(pack4(q0[0], q0[1], q0[2], q0[3]), pack4(q0[4], q0[5], q0[6], q0[7]));
-        *reinterpret_cast<uint2*>(dig + p.dig_stride + k0) =
-            make_uint2(pack4(q1[0], q1[1], q1[2], q1[3]), pack4(q1[4], q1[5], q1[6], q1[7]));
-        *reinterpret_cast<uint2*>(dig + 2 * p.dig_stride + k0) =
-            make_uint2(pack4(q2[0], q2[1], q2[2], q2[3]), pack4(q2[4], q2[5], q2[6], q2[7]));
-        *reinterpret_cast<uint2*>(dig + 3 * p.dig_stride + k0) =
-            make_uint2(pack4(q3[0], q3[1], q3[2], q3[3]), pack4(q3[4], q3[5], q3[6], q3[7]));
+#pragma unroll
+        for (int dgt = 0; dgt < 4; ++dgt)
+          *reinterpret_cast<uint2*>(dig + dgt * p.dig_stride + k0) = make_uint2(m1[dgt], m2[dgt]);
       }
       if ((lane & 1) == 0) xsum[b * 16 + (lane >> 1)] = s16[g];
       if ((lane & 3) == 0) xsum[p.K / 16 + b * 8 + (lane >> 2)] = s32[g];
-      if (lane == 0) xscale[b] = m[g] > 0.f ? __uint_as_float((uint32_t)(127 + E - 5) << 23) : 0.f;
+      if (lane == 0) xscale[b] = m[g] > 0.f ? __uint_as_float((uint32_t)(127 + E - 20) << 23) : 0.f;
     }
   }
   ssq = warp_sum(ssq);
