@@ -193,10 +193,13 @@ int rrr_silu_gate_bf16(rrr_ctx* ctx, const float* gu, uint16_t* y, int rows, int
  * [0, k_window): a rank's attention output [rows, n] placed in its O-projection window. */
 int rrr_window_bf16(rrr_ctx* ctx, const float* x, uint16_t* y, int rows, int n, int k_window,
                     int k_offset, void* stream);
-/* Logits of M rows: x_norm[m] = rms_norm(x[m]) * gamma (gamma NULL: x used as is), then
- * y[m][v] = W[v] . x_norm[m] for a row-major f32 [V, K] W. One library GEMM; with 16+
- * rows on the TF32 tensor cores (f32 storage and accumulation, 10-bit-mantissa products:
- * the batched path's tensor-core tolerance), fewer rows in plain f32. */
+/* Logits of M rows (the batched prefill's logits, phi4.rs:1408-1434): x_norm[m] =
+ * rms_norm(x[m]) * gamma (gamma NULL: x used as is), then y[m][v] = W[v] . x_norm[m] for a
+ * row-major f32 [V, K] W, on the tcgen05 tensor cores with three tf32 products per element
+ * pair (3xTF32: W and x split into a tf32 part and an f32 remainder; the dropped
+ * remainder-by-remainder product is 2^-22 of the product), so the result carries f32-level
+ * accuracy; W is streamed once per 128 rows of x. K % 4 == 0; W and the GEMM input
+ * (x_norm with gamma, else x) 16-byte aligned (RRR_ERR_MISALIGNED otherwise). */
 int rrr_logits_f32_batched(rrr_ctx* ctx, const float* W, const float* x, float* x_norm, float* y,
                            int M, int V, int K, const float* gamma, float eps, void* stream);
 

@@ -44,7 +44,7 @@ def build(verbose: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, newest, verbose), srcs))
     if os.path.exists(LIB) and os.path.getmtime(LIB) >= max(os.path.getmtime(o) for o in objs):
         return LIB
-    cmd = [NVCC, *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-lcublas", "-ldl", "-lpthread"]
+    cmd = [NVCC, *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-ldl", "-lpthread"]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

@@ -12,7 +12,6 @@
 //   logits         rows normalised in f32, then one GEMM (cuBLAS SGEMM, a plain library
 //                  GEMM: W row-major [V, K] times the normalised rows), on the TF32 tensor
 //                  cores for 16+ rows (f32 storage and accumulation)
-#include <cublas_v2.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -153,7 +152,6 @@ __global__ void window_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* _
 
 }  // namespace
 
-void destroy_cublas(void* handle) { cublasDestroy(static_cast<cublasHandle_t>(handle)); }
 
 }  // namespace rrr
 
@@ -240,31 +238,19 @@ int rrr_logits_f32_batched(rrr_ctx* ctx, const float* W, const float* x, float* 
   if (M < 1 || V < 1 || K < 1) return set_error(ctx, RRR_ERR_BAD_SHAPE, "rrr_logits_f32_batched: M, V, K >= 1");
   int rc = bind_device(ctx);
   if (rc) return rc;
-  const float* xin = x;
+  const float* xin = gamma ? x_norm : x;
+  if (K % 4 || (reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(xin) & 15))
+    return set_error(ctx, RRR_ERR_MISALIGNED,
+                     "rrr_logits_f32_batched: K %% 4 == 0 and 16-byte aligned W and GEMM input "
+                     "(x_norm with gamma, else x) are required");
   if (gamma) {
     rc = rrr_rmsnorm(ctx, x, gamma, x_norm, M, K, eps, stream);
     if (rc) return rc;
-    xin = x_norm;
   }
-  if (!ctx->cublas) {
-    cublasHandle_t h = nullptr;
-    if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS)
-      return set_error(ctx, RRR_ERR_CUDA, "rrr_logits_f32_batched: cublasCreate failed");
-    ctx->cublas = h;
-  }
-  cublasHandle_t h = static_cast<cublasHandle_t>(ctx->cublas);
-  if (cublasSetStream(h, static_cast<cudaStream_t>(stream)) != CUBLAS_STATUS_SUCCESS)
-    return set_error(ctx, RRR_ERR_CUDA, "rrr_logits_f32_batched: cublasSetStream failed");
-  // 16+ rows: TF32 tensor cores (f32 storage and accumulation, 10-bit-mantissa products),
-  // the tensor-core tolerance of the batched path; fewer rows stay on the f32 pipes
-  if (cublasSetMathMode(h, M >= 16 ? CUBLAS_TF32_TENSOR_OP_MATH : CUBLAS_DEFAULT_MATH) !=
-      CUBLAS_STATUS_SUCCESS)
-    return set_error(ctx, RRR_ERR_CUDA, "rrr_logits_f32_batched: cublasSetMathMode failed");
-  // column-major view: Y^T [V, M] = (W row-major [V, K] as col-major [K, V])^T * X^T [K, M]
-  const float one = 1.f, zero = 0.f;
-  if (cublasSgemm(h, CUBLAS_OP_T, CUBLAS_OP_N, V, M, K, &one, W, K, xin, K, &zero, y, V) !=
-      CUBLAS_STATUS_SUCCESS)
-    return set_error(ctx, RRR_ERR_CUDA, "rrr_logits_f32_batched: cublasSgemm failed");
+  // 3xTF32 tensor-core kernel (logits_tc.cu): f32-level products, W streamed once per
+  // 128-token tile
+  const cudaError_t e = launch_logits_tc(make_env(ctx, stream), W, xin, y, M, V, K);
+  if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_logits_f32_batched launch");
   return RRR_OK;
 }
 

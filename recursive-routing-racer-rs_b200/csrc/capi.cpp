@@ -217,7 +217,6 @@ int rrr_destroy(rrr_ctx* ctx) {
   bind_device(ctx);
   cudaDeviceSynchronize();
   if (ctx->d_err) cudaFree(ctx->d_err);
-  if (ctx->cublas) rrr::destroy_cublas(ctx->cublas);
   delete ctx;
   return RRR_OK;
 }

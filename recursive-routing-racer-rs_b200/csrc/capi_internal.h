@@ -13,7 +13,6 @@ struct rrr_ctx {
   int* d_err = nullptr;  // 256 B: [0] device error flag written by kernels whose bounded
                          // waits give up; [64..79] argmax key + counter (kept zeroed)
   bool pdl = true;       // launch kernels with programmatic dependent launch
-  void* cublas = nullptr;  // cuBLAS handle of the batched logits GEMM (created on first use)
   std::string last_error;
   void* argmax_scratch() { return reinterpret_cast<char*>(d_err) + 64; }
 };
@@ -23,7 +22,6 @@ namespace rrr {
 int set_error(rrr_ctx* ctx, int code, const char* fmt, ...);
 int cuda_error(rrr_ctx* ctx, cudaError_t e, const char* what);
 int bind_device(rrr_ctx* ctx);
-void destroy_cublas(void* handle);
 LaunchEnv make_env(rrr_ctx* ctx, void* stream);
 // Argument rules of one single-token GEMV (rrr_gemv_kq_ex; swiglu: rrr_gemv_kq_swiglu
 // with N = F).

@@ -74,6 +74,11 @@ bool plan_gemm_kq_tc(int qtype, int M, int K, int N, int sm_count, TcPlan* plan)
 cudaError_t launch_gemm_kq_tc(const LaunchEnv& env, int qtype, const void* w,
                               const uint16_t* x_bf16, float* y, int M, int K, int N,
                               const TcPlan& plan, const float* residual);
+// Batched F32 logits Y[M, V] = X[M, K] W[V, K]^T on the tcgen05 tensor cores with three
+// tf32 products per K step (logits_tc.cu); K % 4 == 0, W and x 16-byte aligned.
+constexpr int kMaxTokTile = 128;  // tokens per tile of that kernel
+cudaError_t launch_logits_tc(const LaunchEnv& env, const float* W, const float* x, float* y,
+                             int M, int V, int K);
 // Self-test of the integer tensor-core fragment layout used by the GEMV (writes 1 to
 // *d_ok when the device result matches the expected product).
 cudaError_t launch_mma_selftest(const LaunchEnv& env, int* d_ok);

@@ -1,0 +1,309 @@
+// logits_tc.cu — kernel (4), batched form: F32 logits of M tokens on the tcgen05 tensor
+// cores, Y[M, V] = X[M, K] · W[V, K]^T with W the f32 output matrix (row-major [V, K],
+// 2.46 GB for Phi-4-mini's 200,064 x 3072). Replaces the logits `matmul_tiled` chunks of
+// the batched prefill (src/model/phi4.rs:1408-1434) and of the decode step
+// (phi4.rs:1049-1064) when several tokens share one pass over W.
+//
+// Accuracy: f32 products from three tf32 tensor-core products (3xTF32). Every element of
+// W and X is split into big = the element with its 13 low mantissa bits cleared (an
+// exact tf32 value) and small = element - big (exact in f32, itself rounded to tf32 by
+// the MMA, a relative error of 2^-21 of the element). Y = Wb·Xb + Wb·Xs + Ws·Xb; the
+// dropped Ws·Xs term is 2^-22 of the product. The two products that share Wb run as one
+// MMA with the B operand [Xb; Xs] stacked along N (N = 2·TN): its first TN columns hold
+// Wb·Xb and its last TN columns Wb·Xs, to which a second MMA (N = TN) adds Ws·Xb; the
+// epilogue adds the two halves. So each 8-deep K step is two MMAs, not three.
+//
+// One CTA (persistent, one per SM) takes 128-row tiles of W x TN-token tiles of X in turn:
+//   warp 0     TMA producer: per 32-wide K chunk, one box of W (128 rows x 128 bytes) and
+//              one of X (TN rows x 128 bytes), both with the 128-byte swizzle, into a ring
+//              of stages [W | Ws | X | Xs];
+//   warps 2-5  split each staged chunk: W -> (Wb in place, Ws), X -> (Xb in place, Xs),
+//              elementwise on the swizzled bytes (so Ws / Xs keep the layout the MMA reads);
+//   warp 1     allocates TMEM (two accumulators of 2·TN f32 columns) and one thread issues
+//              the MMAs (kind::tf32, M = 128, K = 8) and tcgen05.commit's each stage back
+//              to the producer and each finished tile to the epilogue;
+//   warps 6-9  epilogue: tcgen05.ld of the two halves, their sum, coalesced stores of Y
+//              (32 consecutive vocabulary rows per warp and token), while the MMAs of the
+//              next tile run into the other accumulator.
+// W and X tiles past V / M / K are zero-filled by the TMA unit; their rows are not stored.
+// All waits are bounded; a wait that gives up records an error in the context's device
+// flag, the CTA stops issuing work, waits for its copies and MMAs in flight, frees its TMEM
+// and returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <string.h>
+
+#include <algorithm>
+
+#include "internal.h"
+#include "rrr_common.cuh"
+#include "tile_common.cuh"
+
+namespace rrr {
+namespace {
+
+constexpr int kRows = 128;                // W rows per tile = MMA M = TMEM lanes
+constexpr int kBK = 32;                   // K per stage: one 128-byte swizzle row of f32
+constexpr int kThreads = 320;             // 10 warps
+constexpr int kABytes = kRows * kBK * 4;  // 16 KB
+constexpr int kMaxStages = 6;
+constexpr int kSmemBudget = 232448;       // 227 KB opt-in maximum on sm_100
+
+struct LgParams {
+  float* y;
+  int M, V, K;
+  int tn;                 // tokens per tile (multiple of 16, <= kMaxTokTile)
+  int v_tiles, m_tiles, n_k;
+  int stages;
+  uint32_t stage_bytes;   // 2 * kABytes + 2 * tn * 128
+  uint32_t off_bar;
+  uint32_t idesc_2n, idesc_n;
+  uint32_t tmem_cols;
+  int* err;
+};
+
+// big = x with the low 13 mantissa bits cleared (exact tf32), small = x - big (exact).
+__device__ __forceinline__ void split4(float4* big, float4* small) {
+  const float4 w = *big;
+  float4 h, l;
+  h.x = __uint_as_float(__float_as_uint(w.x) & 0xFFFFE000u);
+  h.y = __uint_as_float(__float_as_uint(w.y) & 0xFFFFE000u);
+  h.z = __uint_as_float(__float_as_uint(w.z) & 0xFFFFE000u);
+  h.w = __uint_as_float(__float_as_uint(w.w) & 0xFFFFE000u);
+  l.x = __fsub_rn(w.x, h.x);
+  l.y = __fsub_rn(w.y, h.y);
+  l.z = __fsub_rn(w.z, h.z);
+  l.w = __fsub_rn(w.w, h.w);
+  *big = h;
+  *small = l;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    logits_tc_kernel(const __grid_constant__ CUtensorMap wmap,
+                     const __grid_constant__ CUtensorMap xmap, const LgParams p) {
+  extern __shared__ uint8_t smem_dyn[];
+  // 1024-byte-aligned base (the swizzle pattern is a function of the address bits)
+  uint8_t* smem = smem_dyn + ((1024u - (smem_addr(smem_dyn) & 1023u)) & 1023u);
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);  // TMA bytes landed
+  uint64_t* ready = full + S;                                      // split done (4 warps)
+  uint64_t* empty = ready + S;                                     // MMAs done with the stage
+  uint64_t* acc_full = empty + S;                                  // [2] tile accumulated
+  uint64_t* acc_empty = acc_full + 2;                              // [2] tile stored (4 warps)
+  uint64_t* fin = acc_empty + 2;                                   // every MMA completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = p.v_tiles * p.m_tiles;
+  const int my_tiles =
+      (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int total = my_tiles * p.n_k;  // stages this CTA streams
+  const uint32_t b_bytes = (uint32_t)p.tn * 128u;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(fin, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, p.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: the next grid may be scheduled now; X (written by the
+  // preceding RMSNorm) and Y are touched only after the preceding grid has completed.
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    int issued = 0;
+    for (int it = 0; it < total; ++it) {
+      if (warp_aborted(abort_flag)) break;
+      const int s = it % S;
+      if (it >= S && !warp_wait(&empty[s], (uint32_t)((it / S) - 1) & 1u, p.err)) {
+        *abort_flag = 1;
+        break;
+      }
+      const int t = (int)blockIdx.x + (it / p.n_k) * (int)gridDim.x;
+      const int vt = t % p.v_tiles, mt = t / p.v_tiles;
+      const int k = (it % p.n_k) * kBK;
+      uint8_t* st = smem + (size_t)s * p.stage_bytes;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[s], (uint32_t)kABytes + b_bytes);
+        tma_load_2d(st, &wmap, k, vt * kRows, &full[s]);
+        tma_load_2d(st + 2 * kABytes, &xmap, k, mt * p.tn, &full[s]);
+      }
+      __syncwarp();
+      ++issued;
+    }
+    // copies in flight (only after an abort) must land before the CTA exits
+    for (int s = 0; s < S; ++s) {
+      const int cnt = issued > s ? (issued - s + S - 1) / S : 0;
+      if (cnt) warp_wait(&full[s], (uint32_t)(cnt - 1) & 1u, p.err);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tl = 0; tl < my_tiles && ok; ++tl) {
+        const int b = tl & 1;
+        if (tl >= 2 && !mbar_wait_bounded(&acc_empty[b], (uint32_t)((tl / 2) - 1) & 1u, p.err,
+                                          kDevErrTileWait)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * 2 * p.tn);
+        for (int kc = 0; kc < p.n_k; ++kc, ++it) {
+          const int s = it % S;
+          if (*abort_flag ||
+              !mbar_wait_bounded(&ready[s], (uint32_t)(it / S) & 1u, p.err, kDevErrTileWait)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_addr(smem + (size_t)s * p.stage_bytes);
+          const uint32_t as = a + (uint32_t)kABytes, bx = a + 2u * (uint32_t)kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 8; ++kk) {
+            // [Wb·Xb | Wb·Xs] into columns [0, 2tn), then Ws·Xb added to columns [tn, 2tn)
+            umma_tf32(d, sw128_desc(a + 32u * kk), sw128_desc(bx + 32u * kk), p.idesc_2n,
+                      (kc | kk) != 0);
+            umma_tf32(d + (uint32_t)p.tn, sw128_desc(as + 32u * kk), sw128_desc(bx + 32u * kk),
+                      p.idesc_n, 1u);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[b]);
+      }
+      umma_commit(fin);  // arrives once every MMA issued above has completed
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ---------------- split into big / small halves (128 threads)
+    const int t = (int)threadIdx.x - 64;
+    for (int it = 0; it < total; ++it) {
+      if (warp_aborted(abort_flag)) break;
+      const int s = it % S;
+      if (!warp_wait(&full[s], (uint32_t)(it / S) & 1u, p.err)) {
+        *abort_flag = 1;
+        break;
+      }
+      uint8_t* st = smem + (size_t)s * p.stage_bytes;
+      float4* A = reinterpret_cast<float4*>(st);
+      float4* As = reinterpret_cast<float4*>(st + kABytes);
+#pragma unroll 4
+      for (int i = t; i < kABytes / 16; i += 128) split4(A + i, As + i);
+      float4* B = reinterpret_cast<float4*>(st + 2 * kABytes);
+      float4* Bs = B + b_bytes / 16;
+      for (int i = t; i < (int)(b_bytes / 16); i += 128) split4(B + i, Bs + i);
+      fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[s]);
+    }
+  } else {
+    // ---------------- epilogue (warps 6-9: TMEM lane quarter warp % 4)
+    const int q = warp & 3;
+    for (int tl = 0; tl < my_tiles; ++tl) {
+      const int b = tl & 1;
+      if (!warp_wait(&acc_full[b], (uint32_t)(tl / 2) & 1u, p.err)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int t = (int)blockIdx.x + tl * (int)gridDim.x;
+      const int vt = t % p.v_tiles, mt = t / p.v_tiles;
+      const int v = vt * kRows + q * 32 + lane;
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * p.tn);
+      for (int c = 0; c < p.tn; c += 8) {
+        uint32_t u[8], w[8];
+        tmem_ld8(base + (uint32_t)c, u);
+        tmem_ld8(base + (uint32_t)(p.tn + c), w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int m = mt * p.tn + c + i;
+          if (m < p.M && v < p.V)
+            p.y[(size_t)m * p.V + v] = __fadd_rn(__uint_as_float(u[i]), __uint_as_float(w[i]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    // no MMA may still be running when its TMEM is freed
+    warp_wait(fin, 0u, p.err);
+    tc_fence_after();
+    tmem_dealloc(tmem, p.tmem_cols);
+  }
+}
+
+uint32_t tf32_idesc(int n) {
+  // f32 accumulator (bits 4-5 = 1), A and B tf32 (bits 7-9 and 10-12 = 2), both K-major
+  // (bits 15, 16 = 0), N >> 3 (bits 17-22), M >> 4 (bits 24-28)
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(kRows >> 4) << 24);
+}
+
+}  // namespace
+
+cudaError_t launch_logits_tc(const LaunchEnv& env, const float* W, const float* x, float* y,
+                             int M, int V, int K) {
+  if (M < 1 || V < 1 || K < 1 || K % 4) return cudaErrorInvalidValue;
+  LgParams p{};
+  p.y = y;
+  p.M = M;
+  p.V = V;
+  p.K = K;
+  p.m_tiles = (M + kMaxTokTile - 1) / kMaxTokTile;
+  p.tn = ((M + p.m_tiles - 1) / p.m_tiles + 15) / 16 * 16;
+  p.v_tiles = (V + kRows - 1) / kRows;
+  p.n_k = (K + kBK - 1) / kBK;
+  p.stage_bytes = 2u * kABytes + 2u * (uint32_t)p.tn * 128u;
+  const int bar_bytes = 256;
+  p.stages = std::min(kMaxStages, (kSmemBudget - 1024 - bar_bytes) / (int)p.stage_bytes);
+  if (p.stages < 2) return cudaErrorInvalidValue;
+  p.off_bar = (uint32_t)p.stages * p.stage_bytes;
+  const int smem = (int)p.off_bar + bar_bytes + 1024;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(4 * p.tn)) cols <<= 1;  // two accumulators of 2·tn columns
+  p.tmem_cols = cols;
+  p.idesc_2n = tf32_idesc(2 * p.tn);
+  p.idesc_n = tf32_idesc(p.tn);
+  p.err = env.d_err;
+
+  CUtensorMap wmap, xmap;
+  if (!encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, W, (uint64_t)K, (uint64_t)V,
+                 (uint64_t)K * 4, (uint32_t)kBK, (uint32_t)kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, x, (uint64_t)K, (uint64_t)M,
+                 (uint64_t)K * 4, (uint32_t)kBK, (uint32_t)p.tn, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+
+  auto kern = logits_tc_kernel;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  const int grid = std::max(1, std::min(p.v_tiles * p.m_tiles, env.sm_count));
+  return rrr_launch_pdl(kern, dim3(grid), dim3(kThreads), (size_t)smem, env.stream, env.pdl,
+                        wmap, xmap, p);
+}
+
+}  // namespace rrr

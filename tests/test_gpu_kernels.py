@@ -593,3 +593,58 @@ def test_decode_step_small(rrr, ctx, oracle, G):
 
 def test_no_device_errors(rrr, ctx):
     assert ctx.device_error() == 0
+
+
+@pytest.mark.parametrize("M,V,K", [(1, 1000, 3072), (3, 4097, 512), (16, 1000, 3072), (64, 2000, 3072),
+                                   (100, 777, 100), (130, 300, 256), (300, 257, 64)])
+def test_logits_f32_batched_tensor_core(rrr, ctx, oracle, G, M, V, K):
+    """Batched logits on the tcgen05 tensor cores (3xTF32): every token row within the f32
+    bar (1e-4 relative L2) of the oracle's f32 GEMV, with and without the fused output
+    RMSNorm; ragged vocabulary tiles, K not a multiple of the 32-wide stage, 1 to 3 token
+    tiles; repeated calls bit-identical."""
+    import torch
+    rng = np.random.default_rng(M * 7 + V + K)
+    W = (rng.standard_normal((V, K)) * 0.02).astype(np.float32)
+    X = (rng.standard_normal((M, K)) * 2).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, K).astype(np.float32)
+    Wd, Xd, gd = G.dev(W), G.dev(X), G.dev(g)
+    xn = torch.empty(M * K, device="cuda")
+    L = rrr.ffi.lib()
+    for gamma in (None, gd):
+        outs = []
+        for _ in range(2):
+            Y = torch.full((M, V), float("nan"), device="cuda")
+            ctx.check(L.rrr_logits_f32_batched(ctx.h, vp(Wd), vp(Xd), vp(xn), vp(Y), M, V, K,
+                                               vp(gamma) if gamma is not None else None, 1e-5, None))
+            outs.append(G.host(Y).reshape(M, V))
+        got = outs[0]
+        assert np.array_equal(outs[0], outs[1])
+        for m in range(M):
+            xin = oracle.rms_norm(X[m], g, 1e-5) if gamma is not None else X[m]
+            e = rel_l2(got[m], oracle.gemv_f32(W, xin))
+            assert e < TOL, (m, e)
+    assert ctx.device_error() == 0
+
+
+def test_logits_f32_batched_full_vocab(rrr, ctx, oracle, G):
+    """64 tokens over the full 200064 x 3072 matrix (generated on the device), output norm
+    fused: 512 sampled vocabulary rows of every token within 1e-4 of the oracle."""
+    import torch
+    V, K, M = 200064, 3072, 64
+    L = rrr.ffi.lib()
+    W = torch.empty(V * K, dtype=torch.float32, device="cuda")
+    ctx.check(L.rrr_fill_f32_normal(ctx.h, vp(W), V * K, 0.0, 0.02, 123, None))
+    rng = np.random.default_rng(6)
+    X = (rng.standard_normal((M, K)) * 2).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, K).astype(np.float32)
+    Xd, gd = G.dev(X), G.dev(g)
+    xn = torch.empty(M * K, device="cuda")
+    Y = torch.empty((M, V), device="cuda")
+    ctx.check(L.rrr_logits_f32_batched(ctx.h, vp(W), vp(Xd), vp(xn), vp(Y), M, V, K, vp(gd), 1e-5, None))
+    got = G.host(Y)
+    rows = np.unique(np.concatenate([[0, V - 1], rng.choice(V, 512, replace=False)]))
+    Wr = W.view(V, K)[torch.from_numpy(rows).cuda()].cpu().numpy()
+    for m in range(M):
+        ref = oracle.gemv_f32(Wr, oracle.rms_norm(X[m], g, 1e-5))
+        assert rel_l2(got[m, rows], ref) < TOL, m
+    del W
