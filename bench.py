@@ -11,10 +11,12 @@ synthetic blocks resident in HBM, 2.08 GB per pass, larger than the 126 MB L2, s
 flush is needed between steps). `value` = algorithmic bytes (weights + x + y) of all
 ranks / device time (max over ranks). Under torchrun each rank runs its own copy of the
 layer stack (independent weights, no data-path collective): scaling "weak".
-Also reported: per-GEMV GB/s, the full decode step tok/s with its CUDA
-graph, the end-to-end number through the C ABI with host buffers, the roofline of the
-dominant kernel and a CPU baseline (the oracle's restatement of the reference's
-dequant + f32 dot on the host cores).
+Also reported: per-GEMV GB/s, the batched GEMM, the batched logits, the
+end-to-end number through the C ABI with host buffers, a CPU baseline (the oracle's
+restatement of the reference's dequant + f32 dot on the host cores) and, last on the line,
+the full decode step tok/s with its CUDA graph, the tensor-parallel decode
+step over all ranks (configs[4]; at one GPU the 1-GPU steps) and the roofline of the
+dominant kernel (the layer GEMV with the largest time per layer).
 """
 from __future__ import annotations
 
@@ -34,11 +36,22 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
-# DRAM bytes (read + write) of one gate_up GEMV launch, from the ncu capture summarised in
-# profiles/gemv_kq_phi4_layer_shapes.md (28,369,152 read + 0 written; the algorithmic
-# bytes are 28,389,376).
-GATE_UP_DRAM_BYTES = 28369152
+# DRAM bytes (read + write) of one launch of each layer GEMV, from the ncu capture
+# summarised in profiles/gemv_kq_phi4_layer_shapes.md (nothing is written back to DRAM:
+# the outputs stay in L2).
+DRAM_BYTES = {"o_proj": 5367552, "gate_up": 28370688, "down": 20738304}
 METRIC = "K-quant GEMV HBM GB/s (% of peak) per B200; Phi-4-mini-shape decode tok/s"
+KERNEL_NAMES = {"qkv": "gemv_kq_kernel<Q5_K> (QKV 5120x3072)", "o_proj": "gemv_kq_kernel<Q4_K> (O 3072x3072)",
+                "gate_up": "gemv_kq_kernel<Q4_K> (gate_up 16384x3072)",
+                "down": "gemv_kq_kernel<Q6_K> (down 3072x8192)"}
+
+
+def bench_config(world: int) -> dict:
+    """The workload of the headline metric (the same dict on both arms)."""
+    return {"workload": "configs[1]: per-layer GEMV set at batch 1 (QKV Q5_K 5120x3072, O Q4_K 3072x3072, "
+                        "gate_up Q4_K 16384x3072, down Q6_K 3072x8192) over 32 layers' weights per step",
+            "l2": "inputs larger than L2 (2.08 GB rotation per step), no flush",
+            "parallelism": f"independent layer stacks per GPU (x{world})"}
 
 
 def peaks(tensor: bool = False):
@@ -158,8 +171,7 @@ def run_reference(args, rank, world):
     line = {"metric": METRIC, "value": v, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * el / max(1, args.steps), 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "configs[1] per-layer GEMV set, batch 1 (CPU sample: one layer)",
-                                            "threads": cb["cores"]},
+            "data": "synthetic", "config": bench_config(args.gpus),
             "cpu_baseline": cb, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -365,9 +377,35 @@ def run_ours(args, rank, world, local_rank):
     decode_batch = {"batch": BM, "tok_s": round(BM * 1e3 / bms, 1), "ms_per_step": round(bms, 4),
                     "graph": True, "api": "rrr_phi4_forward_batched",
                     "path": "per layer: rmsnorm->bf16, 4 batched K-quant GEMMs (mma.sync at M <= 64, tcgen05 above; "
-                            "residual in the epilogue), GQA-V / SiLU glue; logits on TF32 tensor cores (cuBLAS), "
+                            "residual in the epilogue), GQA-V / SiLU glue; logits on the 3xTF32 tcgen05 kernel, "
                             "row-wise argmax"}
     bdec.close()
+    # ---------------- batched logits alone (rrr_logits_f32_batched: 3xTF32 tcgen05 kernel,
+    # output RMSNorm fused) for the 64 tokens over the 200064 x 3072 f32 matrix (2.46 GB per
+    # launch, larger than L2)
+    lx = torch.randn(BM, cfg.d_model, device="cuda")
+    lxn = torch.empty(BM, cfg.d_model, device="cuda")
+    ly = torch.empty(BM, cfg.vocab_size, device="cuda")
+
+    def logits_b():
+        ctx.check(L.rrr_logits_f32_batched(ctx.h, c_void_p(model.w_out), c_void_p(lx.data_ptr()),
+                                           c_void_p(lxn.data_ptr()), c_void_p(ly.data_ptr()), BM,
+                                           cfg.vocab_size, cfg.d_model, c_void_p(model.output_norm),
+                                           cfg.rms_eps, sp))
+    for _ in range(3):
+        logits_b()
+    l0e, l1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0e.record(stream)
+    for _ in range(5):
+        logits_b()
+    l1e.record(stream)
+    torch.cuda.synchronize()
+    lus = 1e3 * l0e.elapsed_time(l1e) / 5
+    lbytes = 4 * cfg.vocab_size * cfg.d_model + 8 * BM * cfg.d_model + 4 * BM * cfg.vocab_size
+    logits_batched = {"M": BM, "V": cfg.vocab_size, "K": cfg.d_model, "us": round(lus, 1),
+                      "GBps": round(lbytes / lus / 1e3, 1), "hbm_frac": round(lbytes / lus / 1e3 / peaks()[0], 4),
+                      "kernel": "logits_tc_kernel (3xTF32 tcgen05) + rmsnorm"}
+    del lx, lxn, ly
     # ---------------- tensor-parallel decode step (configs[4], batch 1) over all ranks
     tp_decode = None
     if world > 1:
@@ -425,18 +463,13 @@ def run_ours(args, rank, world, local_rank):
         barrier()
         tbms = max_over_ranks(t0e.elapsed_time(t1e) / bsteps)
         tb.close()
-        tp_decode = {"tok_s": round(1e3 / tms, 2), "ms_per_token": round(tms, 4), "n_gpus": world,
-                     "exchange": "rrr_comm peer-memory kernels over NVLink (all-reduce x2 per layer "
-                                 "+ logits all-gather)",
+        # the tensor-parallel decode step over all ranks (peer-memory exchanges;
+        # NCCL beside it), batch 1 at position 0 and at positions 1024+, and batch 64
+        tp_decode = {"n_gpus": world, "tok_s": round(1e3 / tms, 2), "ms_per_token": round(tms, 4),
                      "tok_s_nccl": round(1e3 / tms_nccl, 2),
-                     "kv_tok_s": round(1e3 / tkms, 2), "kv_positions": [1024, 1024 + dsteps],
-                     "batch64_tok_s": round(BM * 1e3 / tbms, 1), "batch64_ms_per_step": round(tbms, 4),
-                     "bytes_per_rank": tw.shard_bytes(),
+                     "kv_tok_s": round(1e3 / tkms, 2), "batch64_tok_s": round(BM * 1e3 / tbms, 1),
                      "GBps_per_rank": round(tw.shard_bytes() / tms / 1e6, 1),
-                     "exchanges_per_token": 2 * cfg.n_layers + 1,
-                     "launches_per_token": tl_p2p, "graph": True,
-                     "split": "QKV by KV-head group, O-proj by head columns (super-block window), "
-                              "gate_up rows / down columns, logits by vocab"}
+                     "exchanges_per_token": 2 * cfg.n_layers + 1, "launches_per_token": tl_p2p}
         tw.close()
     # ---------------- end to end through the C ABI with host buffers (pinned): copy every
     # x of the step in, replay the prebuilt table, copy every y out, synchronise
@@ -509,41 +542,46 @@ def run_ours(args, rank, world, local_rank):
         cb = cpu_baseline(oracle, cfg, seconds=10.0)
     if rank == 0:
         gbs = bytes_step * world / ms / 1e6
-        dom = per["gate_up"]
+        # the dominant kernel: the layer GEMV with the largest time per layer
+        dom_name = max(per, key=lambda k: per[k]["us_per_launch"])
+        dom = per[dom_name]
+        cases = {k: [v["us_per_launch"], v["path"], v["TFLOPs"], v["tensor_frac"], v["hbm_frac"]]
+                 for k, v in batched.items()}
+        if tp_decode is None:
+            # one GPU: the decode steps themselves are the 1-rank point of the TP curve
+            tp_decode = {"n_gpus": 1, "tok_s": decode["tok_s"], "kv_tok_s": decode_kv["tok_s"],
+                         "batch64_tok_s": decode_batch["tok_s"]}
+        # Order: the bulky detail first, the figures a reader looks for last (the driver keeps
+        # the tail of the line).
         line = {
             "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 (K-quant) x f32",
             "data": "synthetic",
-            "config": {"workload": "configs[1]: per-layer GEMV set at batch 1 (QKV Q5_K 5120x3072, O Q4_K "
-                                   "3072x3072, gate_up Q4_K 16384x3072, down Q6_K 3072x8192) over 32 layers' "
-                                   "weights per step", "bytes_per_step_per_gpu": bytes_step,
-                       "l2": "inputs larger than L2 (2.08 GB rotation per step), no flush",
-                       "parallelism": f"independent layer stacks per GPU (x{world})"},
+            "config": bench_config(world),
+            "batched_gemm": {"cols": ["us", "path", "TFLOPs", "tensor_frac", "hbm_frac"], "cases": cases},
+            "decode_batch64": {"tok_s": decode_batch["tok_s"], "ms_per_step": decode_batch["ms_per_step"],
+                               "api": decode_batch["api"]},
+            "logits_batched": logits_batched,
+            "per_gemv": {k: {"us": v["us_per_launch"], "GBps": v["GBps"], "frac": v["frac"]} for k, v in per.items()},
             "frac_of_peak": round(gbs / world / peak, 4),
-            "per_gemv": per,
-            "roofline": {"bound": "hbm", "kernel": "gemv_kq_kernel<Q4_K> (gate_up)",
-                         "achieved": dom["GBps"], "peak": peak, "unit": "GB/s",
-                         "frac": round(dom["GBps"] / peak, 4), "peak_source": peak_src,
-                         "traffic": GATE_UP_DRAM_BYTES,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one gate_up "
-                                           "launch (profiles/gemv_kq_phi4_layer_shapes.md)"},
-            "decode": decode,
-            "decode_kv": decode_kv,
-            "decode_batch64": decode_batch,
-            "tp_decode": tp_decode,
-            "batched_gemm": {"note": "configs[3]: rrr_gemm_kq_batched, automatic path (register-level mma.sync "
-                                     "for 3 <= M <= 64, tcgen05 + TMEM + TMA above; bf16 x bf16 -> f32); "
-                                     "tensor_frac against the measured dense bf16 burst peak",
-                             "cases": batched},
             "e2e": {"value": round(bytes_step / e2e_ms / 1e6, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "per chunk of 8 layers: rrr_h2d of its x (copy stream) -> rrr_batch_launch of its prebuilt "
-                            "table of 32 GEMVs (compute stream) -> rrr_d2h of its y (second copy stream), chunks "
-                            "overlapping; pinned host buffers; wall clock to a full device synchronise"},
+                    "path": "rrr_h2d (copy stream) -> rrr_batch_launch of a prebuilt table of 32 GEMVs -> rrr_d2h "
+                            "(second copy stream), per chunk of 8 layers, overlapped; pinned host buffers"},
             "gpu_launches": launches_step * args.steps,
             "clocks": clk,
             "cpu_baseline": cb,
+            "decode": {"tok_s": decode["tok_s"], "ms_per_token": decode["ms_per_token"],
+                       "frac_of_peak": decode["frac_of_peak"], "launches": decode["launches_per_token"]},
+            "decode_kv": {"tok_s": decode_kv["tok_s"], "positions": decode_kv["positions"]},
+            "tp_decode": tp_decode,
+            "roofline": {"bound": "hbm", "kernel": KERNEL_NAMES[dom_name],
+                         "achieved": dom["GBps"], "peak": peak, "unit": "GB/s",
+                         "frac": round(dom["GBps"] / peak, 4), "peak_source": peak_src,
+                         "traffic": DRAM_BYTES.get(dom_name),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                           "(profiles/gemv_kq_phi4_layer_shapes.md)"},
         }
         print(json.dumps(line), flush=True)
     model.close()

@@ -6,25 +6,32 @@
 //
 // Accuracy: f32 products from three tf32 tensor-core products (3xTF32). Every element of
 // W and X is split into big = the element with its 13 low mantissa bits cleared (an
-// exact tf32 value) and small = element - big (exact in f32, itself rounded to tf32 by
-// the MMA, a relative error of 2^-21 of the element). Y = Wb·Xb + Wb·Xs + Ws·Xb; the
+// exact tf32 value) and small = element - big (exact in f32, itself truncated to tf32 by
+// the MMA, a relative error of 2^-21 of the element). The tf32 MMA reads an f32 operand
+// as exactly that truncation (the low 13 bits are ignored; the parity tests at the f32
+// bar pin it), so the staged raw values serve as the big parts and only the remainders
+// are written. Y = Wb·Xb + Wb·Xs + Ws·Xb; the
 // dropped Ws·Xs term is 2^-22 of the product. The two products that share Wb run as one
 // MMA with the B operand [Xb; Xs] stacked along N (N = 2·TN): its first TN columns hold
-// Wb·Xb and its last TN columns Wb·Xs, to which a second MMA (N = TN) adds Ws·Xb; the
-// epilogue adds the two halves. So each 8-deep K step is two MMAs, not three.
+// Wb·Xb and its last TN columns Wb·Xs; a second MMA (N = TN) computes Ws·Xb into its own
+// TN columns. So each 8-deep K step is two MMAs, not three. Consecutive MMAs into one
+// accumulator wait for each other, and at these small N that latency, not the tensor
+// throughput, would set the pace; so the K steps rotate over `nslot` independent
+// accumulator slots of 3·TN columns, and the epilogue adds the 3·nslot partial columns of
+// each output in a fixed order (deterministic).
 //
-// One CTA (persistent, one per SM) takes 128-row tiles of W x TN-token tiles of X in turn:
-//   warp 0     TMA producer: per 32-wide K chunk, one box of W (128 rows x 128 bytes) and
-//              one of X (TN rows x 128 bytes), both with the 128-byte swizzle, into a ring
-//              of stages [W | Ws | X | Xs];
-//   warps 2-5  split each staged chunk: W -> (Wb in place, Ws), X -> (Xb in place, Xs),
-//              elementwise on the swizzled bytes (so Ws / Xs keep the layout the MMA reads);
-//   warp 1     allocates TMEM (two accumulators of 2·TN f32 columns) and one thread issues
-//              the MMAs (kind::tf32, M = 128, K = 8) and tcgen05.commit's each stage back
-//              to the producer and each finished tile to the epilogue;
-//   warps 6-9  epilogue: tcgen05.ld of the two halves, their sum, coalesced stores of Y
-//              (32 consecutive vocabulary rows per warp and token), while the MMAs of the
-//              next tile run into the other accumulator.
+// One CTA (persistent, one per SM) takes 128-row tiles of W x TN-token tiles of X in turn,
+// through a ring of stages [W | Ws | X | Xs], one 32-wide K chunk each:
+//   warp 0     TMA producer: per chunk one box of W (128 rows x 128 bytes) and one of X
+//              (TN rows x 128 bytes), both with the 128-byte swizzle;
+//   warps 2-5  split each chunk: Ws and Xs next to the raw values, elementwise on the
+//              swizzled bytes, so every part keeps the layout the MMA reads;
+//   warp 1     allocates TMEM (nbuf x nslot accumulator slots of 3·TN f32 columns); one thread issues the
+//              MMAs (kind::tf32, M = 128, K = 8) and tcgen05.commit's the three slots of a
+//              chunk back and each finished tile to the epilogue;
+//   warps 6-9  epilogue: tcgen05.ld of the partial columns, their sum, coalesced stores of
+//              Y (32 consecutive vocabulary rows per warp and token); with two accumulator
+//              sets (nbuf = 2) the MMAs of the next tile run meanwhile.
 // W and X tiles past V / M / K are zero-filled by the TMA unit; their rows are not stored.
 // All waits are bounded; a wait that gives up records an error in the context's device
 // flag, the CTA stops issuing work, waits for its copies and MMAs in flight, frees its TMEM
@@ -47,8 +54,8 @@ namespace {
 constexpr int kRows = 128;                // W rows per tile = MMA M = TMEM lanes
 constexpr int kBK = 32;                   // K per stage: one 128-byte swizzle row of f32
 constexpr int kThreads = 320;             // 10 warps
-constexpr int kABytes = kRows * kBK * 4;  // 16 KB
-constexpr int kMaxStages = 6;
+constexpr int kABytes = kRows * kBK * 4;  // 16 KB: one W chunk
+constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 232448;       // 227 KB opt-in maximum on sm_100
 
 struct LgParams {
@@ -57,16 +64,18 @@ struct LgParams {
   int tn;                 // tokens per tile (multiple of 16, <= kMaxTokTile)
   int v_tiles, m_tiles, n_k;
   int stages;
-  uint32_t stage_bytes;   // 2 * kABytes + 2 * tn * 128
+  uint32_t stage_bytes;   // [W 16 KB | Ws 16 KB | X tn*128 | Xs tn*128]
   uint32_t off_bar;
   uint32_t idesc_2n, idesc_n;
   uint32_t tmem_cols;
+  int nbuf, nslot;        // accumulator sets (1 or 2) x K-step slots per set
   int* err;
 };
 
-// big = x with the low 13 mantissa bits cleared (exact tf32), small = x - big (exact).
-__device__ __forceinline__ void split4(float4* big, float4* small) {
-  const float4 w = *big;
+// small = x - big with big = x with its low 13 mantissa bits cleared (the tf32 value the
+// MMA reads for x); the difference is exact.
+__device__ __forceinline__ void split4(const float4* x, float4* small) {
+  const float4 w = *x;
   float4 h, l;
   h.x = __uint_as_float(__float_as_uint(w.x) & 0xFFFFE000u);
   h.y = __uint_as_float(__float_as_uint(w.y) & 0xFFFFE000u);
@@ -76,7 +85,6 @@ __device__ __forceinline__ void split4(float4* big, float4* small) {
   l.y = __fsub_rn(w.y, h.y);
   l.z = __fsub_rn(w.z, h.z);
   l.w = __fsub_rn(w.w, h.w);
-  *big = h;
   *small = l;
 }
 
@@ -88,10 +96,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_dyn + ((1024u - (smem_addr(smem_dyn) & 1023u)) & 1023u);
   const int S = p.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);  // TMA bytes landed
-  uint64_t* ready = full + S;                                      // split done (4 warps)
+  uint64_t* ready = full + S;                                      // chunk split (4 warps)
   uint64_t* empty = ready + S;                                     // MMAs done with the stage
-  uint64_t* acc_full = empty + S;                                  // [2] tile accumulated
-  uint64_t* acc_empty = acc_full + 2;                              // [2] tile stored (4 warps)
+  uint64_t* acc_full = empty + S;                                  // [nbuf] tile accumulated
+  uint64_t* acc_empty = acc_full + 2;                              // [nbuf] tile stored (4 warps)
   uint64_t* fin = acc_empty + 2;                                   // every MMA completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -100,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = p.v_tiles * p.m_tiles;
   const int my_tiles =
       (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int total = my_tiles * p.n_k;  // stages this CTA streams
+  const int total = my_tiles * p.n_k;  // K chunks this CTA streams
   const uint32_t b_bytes = (uint32_t)p.tn * 128u;
 
   if (threadIdx.x == 0) {
@@ -159,15 +167,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      const uint32_t slot_cols = 3u * (uint32_t)p.tn;
       for (int tl = 0; tl < my_tiles && ok; ++tl) {
-        const int b = tl & 1;
-        if (tl >= 2 && !mbar_wait_bounded(&acc_empty[b], (uint32_t)((tl / 2) - 1) & 1u, p.err,
-                                          kDevErrTileWait)) {
+        const int b = tl % p.nbuf;
+        if (tl >= p.nbuf && !mbar_wait_bounded(&acc_empty[b], (uint32_t)((tl / p.nbuf) - 1) & 1u,
+                                               p.err, kDevErrTileWait)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(b * 2 * p.tn);
+        const uint32_t dset = tmem + (uint32_t)(b * p.nslot) * slot_cols;
+        int step = 0;  // K step of the tile
         for (int kc = 0; kc < p.n_k; ++kc, ++it) {
           const int s = it % S;
           if (*abort_flag ||
@@ -180,12 +190,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a = smem_addr(smem + (size_t)s * p.stage_bytes);
           const uint32_t as = a + (uint32_t)kABytes, bx = a + 2u * (uint32_t)kABytes;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 8; ++kk) {
-            // [Wb·Xb | Wb·Xs] into columns [0, 2tn), then Ws·Xb added to columns [tn, 2tn)
-            umma_tf32(d, sw128_desc(a + 32u * kk), sw128_desc(bx + 32u * kk), p.idesc_2n,
-                      (kc | kk) != 0);
-            umma_tf32(d + (uint32_t)p.tn, sw128_desc(as + 32u * kk), sw128_desc(bx + 32u * kk),
-                      p.idesc_n, 1u);
+          for (int kk = 0; kk < kBK / 8; ++kk, ++step) {
+            // slot j: [Wb·Xb | Wb·Xs] into its columns [0, 2tn), Ws·Xb into [2tn, 3tn)
+            const int j = step % p.nslot;
+            const uint32_t d = dset + (uint32_t)j * slot_cols;
+            const uint32_t acc = step >= p.nslot ? 1u : 0u;
+            umma_tf32(d, sw128_desc(a + 32u * kk), sw128_desc(bx + 32u * kk), p.idesc_2n, acc);
+            umma_tf32(d + 2u * (uint32_t)p.tn, sw128_desc(as + 32u * kk), sw128_desc(bx + 32u * kk),
+                      p.idesc_n, acc);
           }
           umma_commit(&empty[s]);
         }
@@ -195,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp < 6) {
-    // ---------------- split into big / small halves (128 threads)
+    // ---------------- remainders (warps 2-5, 128 threads)
     const int t = (int)threadIdx.x - 64;
     for (int it = 0; it < total; ++it) {
       if (warp_aborted(abort_flag)) break;
@@ -205,12 +217,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       uint8_t* st = smem + (size_t)s * p.stage_bytes;
-      float4* A = reinterpret_cast<float4*>(st);
+      const float4* A = reinterpret_cast<const float4*>(st);
       float4* As = reinterpret_cast<float4*>(st + kABytes);
 #pragma unroll 4
       for (int i = t; i < kABytes / 16; i += 128) split4(A + i, As + i);
-      float4* B = reinterpret_cast<float4*>(st + 2 * kABytes);
-      float4* Bs = B + b_bytes / 16;
+      const float4* B = reinterpret_cast<const float4*>(st + 2 * kABytes);
+      float4* Bs = reinterpret_cast<float4*>(st + 2 * kABytes + b_bytes);
       for (int i = t; i < (int)(b_bytes / 16); i += 128) split4(B + i, Bs + i);
       fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's async proxy
       __syncwarp();
@@ -219,9 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue (warps 6-9: TMEM lane quarter warp % 4)
     const int q = warp & 3;
+    const uint32_t slot_cols = 3u * (uint32_t)p.tn;
     for (int tl = 0; tl < my_tiles; ++tl) {
-      const int b = tl & 1;
-      if (!warp_wait(&acc_full[b], (uint32_t)(tl / 2) & 1u, p.err)) {
+      const int b = tl % p.nbuf;
+      if (!warp_wait(&acc_full[b], (uint32_t)(tl / p.nbuf) & 1u, p.err)) {
         *abort_flag = 1;
         break;
       }
@@ -229,16 +242,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = (int)blockIdx.x + tl * (int)gridDim.x;
       const int vt = t % p.v_tiles, mt = t / p.v_tiles;
       const int v = vt * kRows + q * 32 + lane;
-      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * p.tn);
+      const uint32_t base =
+          tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * p.nslot) * slot_cols;
       for (int c = 0; c < p.tn; c += 8) {
-        uint32_t u[8], w[8];
-        tmem_ld8(base + (uint32_t)c, u);
-        tmem_ld8(base + (uint32_t)(p.tn + c), w);
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int j = 0; j < p.nslot; ++j) {
+#pragma unroll
+          for (int part = 0; part < 3; ++part) {
+            uint32_t u[8];
+            tmem_ld8(base + (uint32_t)j * slot_cols + (uint32_t)(part * p.tn + c), u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __uint_as_float(u[i]));
+          }
+        }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int m = mt * p.tn + c + i;
-          if (m < p.M && v < p.V)
-            p.y[(size_t)m * p.V + v] = __fadd_rn(__uint_as_float(u[i]), __uint_as_float(w[i]));
+          if (m < p.M && v < p.V) p.y[(size_t)m * p.V + v] = acc[i];
         }
       }
       tc_fence_before();
@@ -284,9 +306,13 @@ cudaError_t launch_logits_tc(const LaunchEnv& env, const float* W, const float* 
   if (p.stages < 2) return cudaErrorInvalidValue;
   p.off_bar = (uint32_t)p.stages * p.stage_bytes;
   const int smem = (int)p.off_bar + bar_bytes + 1024;
-  uint32_t cols = 32;
-  while (cols < (uint32_t)(4 * p.tn)) cols <<= 1;  // two accumulators of 2·tn columns
-  p.tmem_cols = cols;
+  // TMEM (512 columns): nbuf sets of nslot slots of 3·tn columns; two sets (the epilogue of
+  // a tile overlaps the next tile's MMAs) when at least two slots per set still fit
+  const int slot = 3 * p.tn;
+  p.nbuf = (512 / (2 * slot) >= 2) ? 2 : 1;
+  p.nslot = std::min(4, 512 / (p.nbuf * slot));
+  if (p.nslot < 1) return cudaErrorInvalidValue;
+  p.tmem_cols = 512;
   p.idesc_2n = tf32_idesc(2 * p.tn);
   p.idesc_n = tf32_idesc(p.tn);
   p.err = env.d_err;
