@@ -440,6 +440,73 @@ int rrr_comm_allgather_rows_f32(rrr_comm* comm, float* out, const float* part, i
 int rrr_comm_disconnect(rrr_comm* comm);
 int rrr_comm_destroy(rrr_comm* comm);
 
+/* ---- tensor-parallel decode step over G GPUs of one box ------
+ * No reference counterpart: the reference runs the model on one GPU (forward_gpu,
+ * phi4.rs:1099-1196, its dispatch table replayed by dispatch_batch_persistent_v2,
+ * engine.rs:317-370). A Rust host that keeps forward_gpu's call pattern replaces the
+ * one-GPU rrr_phi4 with one rank of this split per process:
+ *   QKV      rows of the rank's query heads [q_head0, q_head1) and of their KV heads
+ *            [kv_head0, kv_head1), in Q, K, V order (position-0 attention stays local);
+ *   O-proj   the super-block window [o_block0, o_block1) of its K around the heads' columns
+ *            (the GEMV input is zero outside the heads, from o_k_offset); partial sums
+ *            all-reduced, the residual added by rank 0 only;
+ *   gate_up  gate rows [ffn0, ffn1) and the same up rows (SwiGLU local); down the matching
+ *            K columns, all-reduced;
+ *   logits   vocabulary rows [vocab0, vocab1), all-gathered; argmax replicated.
+ * Two all-reduces per layer and one all-gather per step. */
+typedef struct rrr_tp_shard {
+  int G, g;                 /* ranks, this rank */
+  int q_head0, q_head1;     /* query heads */
+  int kv_head0, kv_head1;   /* KV heads */
+  int qkv_rows[3][2];       /* Q, K, V row ranges of the full QKV matrix */
+  int qkv_dim;              /* rows of the rank's QKV shard */
+  int o_block0, o_block1;   /* super-block window of the O-projection's K */
+  int o_k, o_k_offset;      /* window width (256 per block); first head column in it */
+  int ffn0, ffn1;           /* gate / up rows; down's K columns */
+  int vocab0, vocab1;       /* logits rows */
+} rrr_tp_shard;
+/* The shard ranges of rank g of G for a model of these dimensions (host only, no GPU
+ * needed). RRR_ERR_BAD_SHAPE when the model does not split G ways: n_heads, n_kv_heads
+ * and vocab multiples of G, ffn_dim a multiple of 256*G, n_heads a multiple of n_kv_heads. */
+int rrr_tp_plan(int d_model, int n_heads, int n_kv_heads, int head_dim, int ffn_dim, int vocab,
+                int G, int g, rrr_tp_shard* out);
+
+/* The exchange channel of one rank. NCCL (loaded at run time: libnccl.so.2, the copy
+ * already in the process if there is one): rank 0 creates a 128-byte unique id, the host
+ * sends it to every rank (any channel), every rank creates its communicator with it.
+ * Peer memory: a connected rrr_comm (not owned; destroy it after this). */
+typedef struct rrr_tp_comm rrr_tp_comm;
+int rrr_tp_nccl_unique_id(void* id_out /* 128 bytes */);
+int rrr_tp_comm_nccl(rrr_ctx* ctx, const void* unique_id, int rank, int world, rrr_tp_comm** out);
+int rrr_tp_comm_p2p(rrr_comm* comm, rrr_tp_comm** out);
+/* Host-side failure detection: waits for the work issued on `stream` with a deadline,
+ * polling the communicator's asynchronous error (NCCL) and the device error flag. On a
+ * communicator error the communicator is aborted and RRR_ERR_NCCL is returned; past the
+ * deadline it is aborted and RRR_ERR_TIMEOUT is returned (an aborted NCCL communicator
+ * refuses further use; recreate it). The reference waits on its fences without a limit
+ * (engine.rs:312,369). */
+int rrr_tp_wait(rrr_tp_comm* comm, void* stream, int timeout_ms);
+int rrr_tp_comm_destroy(rrr_tp_comm* comm);
+
+/* One rank's decode step. desc carries the FULL model's dimensions (d_model, n_heads,
+ * n_kv_heads, head_dim, ffn_dim, vocab) and this rank's shard tensors: w_qkv [qkv_dim, d],
+ * w_o [d, o_k] (the block window), w_gate_up [2*(ffn1-ffn0), d] (gate rows then up rows),
+ * w_down [d, ffn1-ffn0], the norms whole, w_out [vocab1-vocab0, d]. shard must be
+ * rrr_tp_plan's for (desc, G, g). comm may be NULL when G == 1 or when the rank is only run
+ * through rrr_phi4_tp_forward_emulated. The returned model is driven by rrr_phi4_forward /
+ * rrr_phi4_forward_batched / rrr_phi4_set_position / rrr_phi4_destroy like the 1-GPU one
+ * (hidden and logits full-size on every rank; the exchanges run inside the step and are
+ * captured in its CUDA graph). Every rank must run the same calls in the same order. */
+int rrr_phi4_tp_create(rrr_ctx* ctx, const rrr_phi4_desc* desc, const rrr_tp_shard* shard,
+                       rrr_tp_comm* comm, rrr_phi4** out);
+/* All G ranks of one split on the calling process's GPU, run in lockstep with the
+ * exchanges done by local kernels (sums in rank order): for checking the split on one GPU.
+ * ranks[r] are rrr_phi4_tp_create models of ranks r = 0..G-1 of one context; hidden[r],
+ * logits[r], argmax[r] (NULL entries or a NULL array: no argmax) their buffers. M = 0: the
+ * one-token step (rrr_phi4_forward); M >= 1: the batched step of M tokens. */
+int rrr_phi4_tp_forward_emulated(rrr_phi4* const* ranks, int G, float* const* hidden,
+                                 float* const* logits, int* const* argmax, int M, void* stream);
+
 /* ---- seeded synthetic data on the device (bench / tests) --------------------------
  * Blocks follow the distributions of the benchmark configs: d, dmin f16 ~ U[1e-4,1e-2];
  * Q6_K scales int8 ~ U[-32,31]; all other bytes uniform. Block i depends only on

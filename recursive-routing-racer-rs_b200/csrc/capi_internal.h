@@ -23,6 +23,16 @@ int set_error(rrr_ctx* ctx, int code, const char* fmt, ...);
 int cuda_error(rrr_ctx* ctx, cudaError_t e, const char* what);
 int bind_device(rrr_ctx* ctx);
 LaunchEnv make_env(rrr_ctx* ctx, void* stream);
+// Tensor parallelism (tp.cpp): the exchanges of a rank, in-place sum of n floats over the
+// ranks and all-gather of `rows` rows of npr floats (part [rows][npr] -> out
+// [rows][world * npr]); the peer-memory communicator's parameters.
+int tp_comm_world(const rrr_tp_comm* c);
+int tp_comm_rank(const rrr_tp_comm* c);
+bool tp_comm_is_p2p(const rrr_tp_comm* c);
+int tp_allreduce(rrr_tp_comm* c, float* x, int64_t n, void* stream);
+int tp_allgather_rows(rrr_tp_comm* c, float* out, const float* part, int rows, int64_t npr,
+                      void* stream);
+void comm_info(const rrr_comm* c, rrr_ctx** ctx, int* rank, int* world, int64_t* max_elems);
 // Argument rules of one single-token GEMV (rrr_gemv_kq_ex; swiglu: rrr_gemv_kq_swiglu
 // with N = F).
 int check_gemv(rrr_ctx* ctx, int qtype, const void* w, const float* x, float* y, int K, int N,

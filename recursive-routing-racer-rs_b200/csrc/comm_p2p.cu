@@ -137,6 +137,15 @@ static size_t data_bytes(int world, int64_t max_elems) {
   return (size_t)2 * world * max_elems * sizeof(unsigned long long);
 }
 
+namespace rrr {
+void comm_info(const rrr_comm* c, rrr_ctx** ctx, int* rank, int* world, int64_t* max_elems) {
+  *ctx = c->ctx;
+  *rank = c->rank;
+  *world = c->world;
+  *max_elems = c->max_elems;
+}
+}  // namespace rrr
+
 extern "C" {
 
 int rrr_comm_create(rrr_ctx* ctx, int rank, int world, int64_t max_elems, rrr_comm** out,

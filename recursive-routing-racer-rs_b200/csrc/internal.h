@@ -122,6 +122,16 @@ int attention_smem_for(int hd, int hpk, int seq_max);
 cudaError_t launch_embed_rows(const LaunchEnv& env, int type, const void* table, long long n_rows,
                               long long row_bytes, int d, const int* tokens, int n_tokens,
                               float* out);
+// Exchanges of the one-GPU emulation of a tensor-parallel split (tp_exchange.cu): bufs[r]
+// (G <= 8) summed in rank order into every bufs[r]; parts[r] [rows][npr] gathered into
+// every outs[r] [rows][G * npr]; and the NCCL row all-gather's reorder, tmp [G][rows][npr]
+// -> out [rows][G * npr].
+constexpr int kMaxTpRanks = 8;
+cudaError_t launch_local_allreduce(const LaunchEnv& env, float* const* bufs, int G, int64_t n);
+cudaError_t launch_local_allgather_rows(const LaunchEnv& env, const float* const* parts,
+                                        float* const* outs, int G, int rows, int64_t npr);
+cudaError_t launch_rows_from_ranks(const LaunchEnv& env, const float* tmp, float* out, int G,
+                                   int rows, int64_t npr);
 // *d_pos += delta after the preceding kernels of the stream have completed.
 cudaError_t launch_pos_advance(const LaunchEnv& env, int* d_pos, int delta);
 

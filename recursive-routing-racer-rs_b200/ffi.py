@@ -57,6 +57,15 @@ class Phi4Desc(ctypes.Structure):
                 ("rope_factors", c_void_p), ("n_rope_factors", c_int)]
 
 
+class TPShard(ctypes.Structure):
+    """rrr_tp_shard (include/rrr_cuda.h): rank g of G's ranges, [start, stop)."""
+    _fields_ = [("G", c_int), ("g", c_int), ("q_head0", c_int), ("q_head1", c_int),
+                ("kv_head0", c_int), ("kv_head1", c_int), ("qkv_rows", (c_int * 2) * 3),
+                ("qkv_dim", c_int), ("o_block0", c_int), ("o_block1", c_int), ("o_k", c_int),
+                ("o_k_offset", c_int), ("ffn0", c_int), ("ffn1", c_int), ("vocab0", c_int),
+                ("vocab1", c_int)]
+
+
 class AttnDesc(ctypes.Structure):
     _fields_ = [("n_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int), ("rope_dim", c_int),
                 ("rope_theta", c_float), ("rope_attn_factor", c_float), ("rope_factors", c_void_p),
@@ -123,6 +132,15 @@ PROTOS = {
     "rrr_phi4_destroy": (c_int, [vp]),
     "rrr_set_pdl": (c_int, [vp, c_int]),
     "rrr_set_wait_limit": (c_int, [vp, c_uint64]),
+    "rrr_tp_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, POINTER(TPShard)]),
+    "rrr_tp_nccl_unique_id": (c_int, [vp]),
+    "rrr_tp_comm_nccl": (c_int, [vp, vp, c_int, c_int, POINTER(vp)]),
+    "rrr_tp_comm_p2p": (c_int, [vp, POINTER(vp)]),
+    "rrr_tp_wait": (c_int, [vp, vp, c_int]),
+    "rrr_tp_comm_destroy": (c_int, [vp]),
+    "rrr_phi4_tp_create": (c_int, [vp, POINTER(Phi4Desc), POINTER(TPShard), vp, POINTER(vp)]),
+    "rrr_phi4_tp_forward_emulated": (c_int, [POINTER(vp), c_int, POINTER(vp), POINTER(vp), POINTER(vp),
+                                             c_int, vp]),
     "rrr_position_advance": (c_int, [vp, vp, c_int, vp]),
     "rrr_window_bf16": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, vp]),
     "rrr_gemm_kq_batched_path": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, c_int, vp, c_int, vp]),

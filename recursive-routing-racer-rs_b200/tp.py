@@ -1,23 +1,25 @@
 """Tensor-parallel decode step of the weight path over G GPUs of one box (one process per
-GPU, torch.distributed over NCCL for the exchanges).
+GPU): the Python host of the C ABI's rrr_tp_* / rrr_phi4_tp_* entry points.
 
-The reference runs the whole model on one GPU (src/model/phi4.rs:1099-1196); this module
-splits the same per-layer weight GEMVs so that every rank streams 1/G of the bytes:
+The reference runs the whole model on one GPU (src/model/phi4.rs:1099-1196); the split
+(rrr_tp_plan) makes every rank stream 1/G of the bytes:
 
     QKV       rows of the rank's query heads [h0, h1) and their KV heads [v0, v1): the
               position-0 attention (output = V of the head's KV group) is then local
     O-proj    the K columns of those heads (Megatron split). When the heads do not cover
               whole 256-wide super-blocks (8 GPUs: 384 columns), the rank keeps the
               super-block window around them and the GEMV input is zero outside the
-              heads (RRR_X_GQA_V with k_offset), so no block is split; the partial
-              outputs are summed with an all-reduce
+              heads, so no block is split; the partial outputs are summed (all-reduce)
     gate_up   rows [f0, f1) of gate and the same rows of up: SiLU(gate)*up stays local
     down      the matching K columns [f0, f1) of every row; all-reduce of the partials
     logits    vocab rows [V*g/G, V*(g+1)/G), output RMSNorm fused; all-gather of the rows
 
-The residual is added by rank 0 only (in its O-proj / down epilogue), so the all-reduced
-sum carries it once. Everything else (RMSNorm, the argmax) is replicated. Per token: 2
-all-reduces per layer and one all-gather.
+The residual is added by rank 0 only, so the all-reduced sum carries it once. RMSNorm and
+the argmax are replicated. The step itself (kernels and exchanges, one CUDA graph) runs in
+C++ (rrr_phi4_forward on a rank made by rrr_phi4_tp_create); this module generates the
+synthetic shards, sets up the exchange channel (NCCL through a unique id broadcast over
+torch.distributed, or the peer-memory rrr_comm with IPC handles all-gathered the same
+way) and runs the one-GPU emulation of a split (rrr_phi4_tp_forward_emulated).
 """
 from __future__ import annotations
 
@@ -60,26 +62,32 @@ class TPShard:
 
 
 def plan(cfg: ModelConfig, G: int, g: int) -> TPShard:
-    """Shard ranges of rank g of G (the split of the tensor-parallel section above)."""
-    if G < 1 or not 0 <= g < G:
-        raise ValueError(f"bad rank {g} of {G}")
-    nq, nkv, hd, F, V = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab_size
-    if nq % G or nkv % G or nq % nkv:
-        raise ValueError(f"{nq} query / {nkv} KV heads do not split over {G} GPUs")
-    if F % (256 * G):
-        raise ValueError(f"ffn_dim {F} is not a multiple of 256*{G}")
-    if V % G:
-        raise ValueError(f"vocab {V} is not a multiple of {G}")
-    h0, h1 = nq * g // G, nq * (g + 1) // G
-    v0, v1 = nkv * g // G, nkv * (g + 1) // G
-    qkv_rows = ((h0 * hd, h1 * hd),
-                (nq * hd + v0 * hd, nq * hd + v1 * hd),
-                ((nq + nkv) * hd + v0 * hd, (nq + nkv) * hd + v1 * hd))
-    c0, c1 = h0 * hd, h1 * hd
-    b0, b1 = c0 // 256, (c1 + 255) // 256
-    f0, f1 = F * g // G, F * (g + 1) // G
-    return TPShard(G, g, (h0, h1), (v0, v1), qkv_rows, (b0, b1), c0 - 256 * b0, (f0, f1),
-                   (V * g // G, V * (g + 1) // G))
+    """Shard ranges of rank g of G (rrr_tp_plan of the C ABI; no GPU needed)."""
+    sh = ffi.TPShard()
+    rc = ffi.lib().rrr_tp_plan(cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim,
+                               cfg.vocab_size, G, g, ctypes.byref(sh))
+    if rc != 0:
+        raise ValueError(ffi.last_error(None))
+    return TPShard(sh.G, sh.g, (sh.q_head0, sh.q_head1), (sh.kv_head0, sh.kv_head1),
+                   tuple((sh.qkv_rows[i][0], sh.qkv_rows[i][1]) for i in range(3)),
+                   (sh.o_block0, sh.o_block1), sh.o_k_offset, (sh.ffn0, sh.ffn1),
+                   (sh.vocab0, sh.vocab1))
+
+
+def c_shard(shard: TPShard) -> "ffi.TPShard":
+    """The rrr_tp_shard of a plan (what rrr_phi4_tp_create checks against its own plan)."""
+    sh = ffi.TPShard()
+    sh.G, sh.g = shard.G, shard.g
+    sh.q_head0, sh.q_head1 = shard.q_heads
+    sh.kv_head0, sh.kv_head1 = shard.kv_heads
+    for i, (a, b) in enumerate(shard.qkv_rows):
+        sh.qkv_rows[i][0], sh.qkv_rows[i][1] = a, b
+    sh.qkv_dim = shard.qkv_dim
+    sh.o_block0, sh.o_block1 = shard.o_blocks
+    sh.o_k, sh.o_k_offset = shard.o_k, shard.o_k_offset
+    sh.ffn0, sh.ffn1 = shard.ffn
+    sh.vocab0, sh.vocab1 = shard.vocab
+    return sh
 
 
 class SyntheticPhi4TP:
@@ -140,6 +148,23 @@ class SyntheticPhi4TP:
                                              tensor_seed(seed, -1, "rope_factors"), s))
         ctx.check(L.rrr_sync(ctx.h, s))
 
+    def desc(self, max_seq: int = 0):
+        """rrr_phi4_desc of the shard tensors (full model dimensions); returns (desc, keep)."""
+        cfg = self.cfg
+        arr = (ffi.Phi4Layer * cfg.n_layers)()
+        for i, e in enumerate(self.layers):
+            arr[i].w_qkv, arr[i].qkv_type = e["qkv"], cfg.qkv_type
+            arr[i].w_o, arr[i].o_type = e["o_proj"], cfg.o_type
+            arr[i].w_gate_up, arr[i].gate_up_type = e["gate_up"], cfg.gate_up_type
+            arr[i].w_down, arr[i].down_type = e["down"], cfg.down_type
+            arr[i].attn_norm, arr[i].ffn_norm = e["attn_norm"], e["ffn_norm"]
+        d = ffi.Phi4Desc(cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim,
+                         cfg.n_layers, cfg.vocab_size, cfg.rms_eps, cfg.logits_chunk_rows,
+                         ctypes.cast(arr, ctypes.POINTER(ffi.Phi4Layer)), self.output_norm, self.w_out,
+                         max_seq, cfg.rope_dim, cfg.rope_theta, cfg.rope_attn_factor,
+                         self.rope_factors, self.n_rope_factors)
+        return d, arr
+
     def shard_bytes(self) -> int:
         """Weight bytes one decode step streams on this rank."""
         c, sh = self.cfg, self.shard
@@ -183,7 +208,8 @@ def all_reduce_with_deadline(t, timeout_s: float, group=None) -> None:
 
 class P2PComm:
     """The C ABI's NVLink peer-memory exchanges (rrr_comm_*) for one rank; the 64-byte IPC
-    handles are swapped with torch.distributed.all_gather_object."""
+    handles are swapped with torch.distributed.all_gather_object. `tp` is its
+    rrr_tp_comm for rrr_phi4_tp_create."""
 
     def __init__(self, ctx: ffi.Context, rank: int, world: int, max_elems: int, group=None):
         import torch.distributed as dist
@@ -198,367 +224,155 @@ class P2PComm:
         allh = ctypes.create_string_buffer(b"".join(handles), 64 * world)
         ctx.check(L.rrr_comm_connect(self.h, allh))
         dist.barrier(group=group)
-
-    def all_reduce(self, t, stream) -> None:
-        self.ctx.check(ffi.lib().rrr_comm_allreduce_f32(self.h, c_void_p(t.data_ptr()), t.numel(), stream))
-
-    def all_gather(self, out, part, stream) -> None:
-        self.ctx.check(ffi.lib().rrr_comm_allgather_f32(self.h, c_void_p(out.data_ptr()),
-                                                        c_void_p(part.data_ptr()), part.numel(), stream))
+        self.tp = c_void_p()
+        ctx.check(L.rrr_tp_comm_p2p(self.h, ctypes.byref(self.tp)))
 
     def close(self) -> None:
         """Collective: every rank unmaps the others' buffers, then frees its own."""
         import torch.distributed as dist
+        L = ffi.lib()
+        if self.tp:
+            L.rrr_tp_comm_destroy(self.tp)
+            self.tp = None
         if self.h:
-            ffi.lib().rrr_comm_disconnect(self.h)
+            L.rrr_comm_disconnect(self.h)
             dist.barrier(group=self.group)
-            ffi.lib().rrr_comm_destroy(self.h)
+            L.rrr_comm_destroy(self.h)
             self.h = None
 
 
+class NcclComm:
+    """An NCCL communicator made by the C ABI (rrr_tp_comm_nccl); rank 0's unique id is
+    broadcast with torch.distributed."""
+
+    def __init__(self, ctx: ffi.Context, rank: int, world: int, group=None):
+        import torch.distributed as dist
+        L = ffi.lib()
+        uid = ctypes.create_string_buffer(128)
+        if rank == 0:
+            ffi.check(L.rrr_tp_nccl_unique_id(uid))
+        obj = [bytes(uid.raw)]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        uid = ctypes.create_string_buffer(obj[0], 128)
+        self.tp = c_void_p()
+        ctx.check(L.rrr_tp_comm_nccl(ctx.h, uid, rank, world, ctypes.byref(self.tp)))
+
+    def close(self) -> None:
+        if self.tp:
+            ffi.lib().rrr_tp_comm_destroy(self.tp)
+            self.tp = None
+
+
 class TPDecoder:
-    """One rank's decode step: the kernels of the 1-GPU step on the rank's shards, with
-    torch.distributed all-reduce / all-gather (NCCL) or the peer-memory kernels between
-    them. The step can be captured into a CUDA graph (kernels and collectives) and
-    replayed.
+    """One rank's decode step on the C ABI (rrr_phi4_tp_create + rrr_phi4_forward[_batched]):
+    the kernels of the 1-GPU step on the rank's shards with the exchanges between them
+    (NCCL, or the peer-memory kernels), capturable into one CUDA graph.
 
     max_seq = 0: every token at position 0 (attention output = V; forward_batched runs M
     independent sequences). max_seq > 0: a KV cache of the rank's KV heads (f16, max_seq
     rows per layer) and a device position: forward decodes one token at the position and
     advances it (RoPE, KV store and attention fused in one launch per layer);
     forward_batched is a prefill of M consecutive tokens of one sequence (RoPE + KV store
-    of the M rows, causal attention, phi4.rs:1270-1309) and advances the position by M."""
+    of the M rows, causal attention, phi4.rs:1270-1309) and advances the position by M.
+    comm = None with G > 1: the rank is only run through emulate_step."""
 
-    def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4TP, group=None, comm: str = "nccl",
+    def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4TP, group=None, comm: str | None = None,
                  max_batch: int = 1, max_seq: int = 0):
-        """comm: "nccl" (torch.distributed collectives) or "p2p" (rrr_comm_* kernels over
-        NVLink peer memory); max_batch: the largest M of forward_batched; max_seq: KV-cache
-        rows (0: position-0 steps)."""
-        import torch
-        import torch.distributed as dist
-        self.torch, self.dist = torch, dist
+        """comm: "nccl" (rrr_tp_comm_nccl), "p2p" (rrr_comm_* kernels over NVLink peer
+        memory) or None; max_batch: the largest M of forward_batched (sizes the peer-memory
+        buffers); max_seq: KV-cache rows (0: position-0 steps)."""
         self.ctx, self.w, self.group = ctx, weights, group
-        self.p2p = None
-        if comm == "p2p" and weights.shard.G > 1:
-            self.p2p = P2PComm(ctx, weights.shard.g, weights.shard.G,
-                               max_batch * max(weights.cfg.d_model, weights.shard.vocab_rows), group)
-        elif comm not in ("nccl", "p2p"):
-            raise ValueError(f"unknown comm {comm!r}")
-        cfg, sh = weights.cfg, weights.shard
-        dev = torch.device("cuda", ctx.device)
-        self.qkv = torch.empty(sh.qkv_dim, device=dev)
-        self.mid = torch.empty(sh.ffn_dim, device=dev)
-        self.logits_loc = torch.empty(sh.vocab_rows, device=dev)
-        self.graph = None
-        self._graph_key = None
-        self._bm = 0  # batch size of the batched buffers
         self.max_seq = max_seq
-        self.pos = 0  # host copy of the device position
-        if max_seq:
-            nq_loc = sh.q_heads[1] - sh.q_heads[0]
-            nkv_loc = sh.kv_heads[1] - sh.kv_heads[0]
-            self.kc = torch.zeros(cfg.n_layers, max_seq, nkv_loc * cfg.head_dim, dtype=torch.int16, device=dev)
-            self.vc = torch.zeros_like(self.kc)
-            self.d_pos = torch.zeros(1, dtype=torch.int32, device=dev)
-            self.attn_desc = ffi.AttnDesc(nq_loc, nkv_loc, cfg.head_dim, cfg.rope_dim, cfg.rope_theta,
-                                          cfg.rope_attn_factor, c_void_p(weights.rope_factors),
-                                          weights.n_rope_factors, max_seq)
-            # O-projection input: the heads' attention output inside the window, zeros around
-            self.attn_in = torch.zeros(sh.o_k, device=dev)
+        sh = weights.shard
+        self.channel = None
+        if comm not in (None, "nccl", "p2p"):
+            raise ValueError(f"unknown comm {comm!r}")
+        if comm == "p2p" and sh.G > 1:
+            self.channel = P2PComm(ctx, sh.g, sh.G,
+                                   max_batch * max(weights.cfg.d_model, sh.vocab_rows), group)
+        elif comm == "nccl" and sh.G > 1:
+            self.channel = NcclComm(ctx, sh.g, sh.G, group)
+        d, self._keep = weights.desc(max_seq)
+        self._shard = c_shard(sh)
+        h = c_void_p()
+        ctx.check(ffi.lib().rrr_phi4_tp_create(ctx.h, ctypes.byref(d), ctypes.byref(self._shard),
+                                               self.channel.tp if self.channel else None, ctypes.byref(h)))
+        self.h = h
+
+    @staticmethod
+    def _stream(stream):
+        import torch
+        if stream is None:
+            return c_void_p(torch.cuda.current_stream().cuda_stream)
+        return c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+
+    @staticmethod
+    def _ptr(t):
+        return None if t is None else c_void_p(t if isinstance(t, int) else t.data_ptr())
+
+    def forward(self, hidden, logits, argmax=None, use_graph: bool = False, stream=None) -> None:
+        """One step on `stream` (default: the current torch stream). hidden f32[d] in/out,
+        logits f32[vocab] (full on every rank), argmax int32[1] or None. use_graph: the first
+        call runs the step and captures it; later calls with these buffers replay it."""
+        self.ctx.check(ffi.lib().rrr_phi4_forward(self.h, self._ptr(hidden), self._ptr(logits),
+                                                  self._ptr(argmax), 1 if use_graph else 0,
+                                                  self._stream(stream)))
+
+    def forward_batched(self, hidden, logits, M: int, argmax=None, use_graph: bool = False,
+                        stream=None) -> None:
+        """M tokens in one step: hidden f32 [M, d] in/out, logits f32 [M, vocab], argmax int32[M]
+        or None."""
+        self.ctx.check(ffi.lib().rrr_phi4_forward_batched(self.h, self._ptr(hidden), self._ptr(logits),
+                                                          self._ptr(argmax), M, 1 if use_graph else 0,
+                                                          self._stream(stream)))
+
+    def wait(self, timeout_ms: int, stream=None) -> None:
+        """Host deadline on the step's stream (rrr_tp_wait): raises RRRError with
+        RRR_ERR_TIMEOUT / RRR_ERR_NCCL (the communicator aborted) on failure."""
+        if self.channel is None:
+            raise ValueError("no communicator")
+        self.ctx.check(ffi.lib().rrr_tp_wait(self.channel.tp, self._stream(stream), timeout_ms))
 
     def set_position(self, pos: int) -> None:
         """KV-cache decode: position of the next token (KVCache.len)."""
-        if not 0 <= pos < self.max_seq:
-            raise ValueError(f"position {pos} outside the cache of {self.max_seq} rows")
-        self.d_pos.fill_(pos)
-        self.pos = pos
+        self.ctx.check(ffi.lib().rrr_phi4_set_position(self.h, pos, None))
 
-    def _cache(self, l):
-        kv = self.kc[l].data_ptr(), self.vc[l].data_ptr()
-        return c_void_p(kv[0]), c_void_p(kv[1])
-
-    def steps(self, hidden, logits, argmax, stream=None):
-        """The step as a generator: launches the kernels on `stream` (default: the current
-        torch stream) and yields at each exchange ("all_reduce", t) -- sum t over the
-        ranks in place -- and ("all_gather", out, part) -- out = concatenation of every
-        rank's part. hidden: f32[d] (in/out); logits: f32[vocab]; argmax: int32[1] or None."""
-        L, ctx, cfg, sh, w = ffi.lib(), self.ctx, self.w.cfg, self.w.shard, self.w
-        torch = self.torch
-        st = c_void_p(stream if stream is not None else torch.cuda.current_stream().cuda_stream)
-        d, hd = cfg.d_model, cfg.head_dim
-        hp = c_void_p(hidden.data_ptr())
-        res = hp if sh.g == 0 else None
-        nq_loc = sh.q_heads[1] - sh.q_heads[0]
-        nkv_loc = sh.kv_heads[1] - sh.kv_heads[0]
-        qkv_p, mid_p = c_void_p(self.qkv.data_ptr()), c_void_p(self.mid.data_ptr())
-        if self.max_seq:
-            if self.pos >= self.max_seq:
-                raise ValueError(f"position {self.pos} is past the cache of {self.max_seq} rows")
-            ad, dpos = ctypes.byref(self.attn_desc), c_void_p(self.d_pos.data_ptr())
-            attn_out = c_void_p(self.attn_in.data_ptr() + 4 * sh.o_k_offset)
-        for l, e in enumerate(w.layers):
-            pn = ffi.GemvPrologue(1, e["attn_norm"], cfg.rms_eps, 0, 0, 0, 0)
-            ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.qkv_type, c_void_p(e["qkv"]), hp, qkv_p, d,
-                                       sh.qkv_dim, None, ctypes.byref(pn), st))
-            if self.max_seq:
-                kc, vc = self._cache(l)
-                ctx.check(L.rrr_rope_attention_f16kv(ctx.h, ad, qkv_p, 0, dpos, kc, vc, attn_out, st))
-                ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.o_type, c_void_p(e["o_proj"]),
-                                           c_void_p(self.attn_in.data_ptr()), hp, sh.o_k, d, res, None, st))
-            else:
-                pv = ffi.GemvPrologue(3, None, 0.0, nq_loc, nkv_loc, hd, sh.o_k_offset)
-                ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.o_type, c_void_p(e["o_proj"]), qkv_p, hp, sh.o_k,
-                                           d, res, ctypes.byref(pv), st))
-            if sh.G > 1:
-                yield ("all_reduce", hidden)
-            pf = ffi.GemvPrologue(1, e["ffn_norm"], cfg.rms_eps, 0, 0, 0, 0)
-            ctx.check(L.rrr_gemv_kq_swiglu(ctx.h, cfg.gate_up_type, c_void_p(e["gate_up"]), hp, mid_p,
-                                           d, sh.ffn_dim, ctypes.byref(pf), st))
-            ctx.check(L.rrr_gemv_kq_ex(ctx.h, cfg.down_type, c_void_p(e["down"]), mid_p, hp, sh.ffn_dim,
-                                       d, res, None, st))
-            if sh.G > 1:
-                yield ("all_reduce", hidden)
-        lp = c_void_p(self.logits_loc.data_ptr() if sh.G > 1 else logits.data_ptr())
-        ctx.check(L.rrr_logits_f32(ctx.h, c_void_p(w.w_out), hp, lp, sh.vocab_rows, d,
-                                   cfg.logits_chunk_rows, c_void_p(w.output_norm), cfg.rms_eps, st))
-        if sh.G > 1:
-            yield ("all_gather", logits, self.logits_loc)
-        if argmax is not None:
-            ctx.check(L.rrr_argmax_f32(ctx.h, c_void_p(logits.data_ptr()), cfg.vocab_size,
-                                       c_void_p(argmax.data_ptr()), st))
-        if self.max_seq:
-            ctx.check(L.rrr_position_advance(ctx.h, c_void_p(self.d_pos.data_ptr()), 1, st))
-            self.pos += 1
-
-    def _issue(self, hidden, logits, argmax):
-        """The step with its exchanges as torch.distributed collectives (NCCL) or as the
-        peer-memory kernels."""
-        st = c_void_p(self.torch.cuda.current_stream().cuda_stream)
-        for op in self.steps(hidden, logits, argmax):
-            self._exchange(op, st)
-
-    def close(self) -> None:
-        self.release_graph()
-        if self.p2p is not None:
-            self.p2p.close()
-            self.p2p = None
-
-    def _ensure_batch(self, M: int) -> None:
-        if self._bm >= M:
-            return
-        torch = self.torch
-        cfg, sh = self.w.cfg, self.w.shard
-        dev = torch.device("cuda", self.ctx.device)
-        self.b_xn = torch.empty(M, cfg.d_model, dtype=torch.int16, device=dev)       # bf16 bits
-        self.b_qkv = torch.empty(M, sh.qkv_dim, device=dev)
-        self.b_a = torch.empty(M, sh.o_k, dtype=torch.int16, device=dev)             # bf16 bits
-        self.b_gu = torch.empty(M, 2 * sh.ffn_dim, device=dev)
-        self.b_mid = torch.empty(M, sh.ffn_dim, dtype=torch.int16, device=dev)       # bf16 bits
-        self.b_xnorm = torch.empty(M, cfg.d_model, device=dev)
-        self.b_logits_loc = torch.empty(M, sh.vocab_rows, device=dev)
-        if self.max_seq:
-            self.b_attn = torch.empty(M, (sh.q_heads[1] - sh.q_heads[0]) * cfg.head_dim, device=dev)
-        self._bm = M
-
-    def steps_batched(self, hidden, logits, M: int, stream=None):
-        """M tokens (the batched-prefill call sites, phi4.rs:1198-1445, with every GEMM on
-        the tensor cores): at position 0 each (max_seq = 0), or a prefill of M consecutive
-        positions from the current one (max_seq > 0). hidden f32 [M, d] (in/out), logits
-        f32 [M, vocab]. Yields at each exchange like steps(); the logits exchange is
-        ("all_gather_rows", out [M, vocab], part [M, vocab/G], M)."""
-        L, ctx, cfg, sh, w = ffi.lib(), self.ctx, self.w.cfg, self.w.shard, self.w
-        torch = self.torch
-        self._ensure_batch(M)
-        st = c_void_p(stream if stream is not None else torch.cuda.current_stream().cuda_stream)
-        d, hd = cfg.d_model, cfg.head_dim
-        hp = c_void_p(hidden.data_ptr())
-        res = hp if sh.g == 0 else None
-        nq_loc = sh.q_heads[1] - sh.q_heads[0]
-        nkv_loc = sh.kv_heads[1] - sh.kv_heads[0]
-        xn, qkv, a = c_void_p(self.b_xn.data_ptr()), c_void_p(self.b_qkv.data_ptr()), c_void_p(self.b_a.data_ptr())
-        gu, mid = c_void_p(self.b_gu.data_ptr()), c_void_p(self.b_mid.data_ptr())
-        if self.max_seq:
-            if self.pos + M > self.max_seq:
-                raise ValueError(f"positions {self.pos}..{self.pos + M - 1} exceed the cache of "
-                                 f"{self.max_seq} rows")
-            ad, dpos = ctypes.byref(self.attn_desc), c_void_p(self.d_pos.data_ptr())
-            att = c_void_p(self.b_attn.data_ptr())
-        for l, e in enumerate(w.layers):
-            ctx.check(L.rrr_rmsnorm_bf16(ctx.h, hp, c_void_p(e["attn_norm"]), xn, M, d, cfg.rms_eps, st))
-            ctx.check(L.rrr_gemm_kq_batched(ctx.h, cfg.qkv_type, c_void_p(e["qkv"]), xn, qkv, M, d,
-                                            sh.qkv_dim, st))
-            if self.max_seq:
-                kc, vc = self._cache(l)
-                ctx.check(L.rrr_rope_kv_store(ctx.h, ad, qkv, sh.qkv_dim, M, 0, dpos, kc, vc, st))
-                ctx.check(L.rrr_attention_f16kv(ctx.h, ad, qkv, sh.qkv_dim, M, 0, dpos, kc, vc, att, st))
-                ctx.check(L.rrr_window_bf16(ctx.h, att, a, M, nq_loc * hd, sh.o_k, sh.o_k_offset, st))
-            else:
-                ctx.check(L.rrr_gqa_v_bf16(ctx.h, qkv, a, M, nq_loc, nkv_loc, hd, sh.o_k, sh.o_k_offset, st))
-            ctx.check(L.rrr_gemm_kq_batched_ex(ctx.h, cfg.o_type, c_void_p(e["o_proj"]), a, hp, M, sh.o_k,
-                                               d, res, st))
-            if sh.G > 1:
-                yield ("all_reduce", hidden)
-            ctx.check(L.rrr_rmsnorm_bf16(ctx.h, hp, c_void_p(e["ffn_norm"]), xn, M, d, cfg.rms_eps, st))
-            ctx.check(L.rrr_gemm_kq_batched(ctx.h, cfg.gate_up_type, c_void_p(e["gate_up"]), xn, gu, M, d,
-                                            2 * sh.ffn_dim, st))
-            ctx.check(L.rrr_silu_gate_bf16(ctx.h, gu, mid, M, sh.ffn_dim, st))
-            ctx.check(L.rrr_gemm_kq_batched_ex(ctx.h, cfg.down_type, c_void_p(e["down"]), mid, hp, M,
-                                               sh.ffn_dim, d, res, st))
-            if sh.G > 1:
-                yield ("all_reduce", hidden)
-        lp = self.b_logits_loc if sh.G > 1 else logits
-        ctx.check(L.rrr_logits_f32_batched(ctx.h, c_void_p(w.w_out), hp, c_void_p(self.b_xnorm.data_ptr()),
-                                           c_void_p(lp.data_ptr()), M, sh.vocab_rows, d,
-                                           c_void_p(w.output_norm), cfg.rms_eps, st))
-        if sh.G > 1:
-            yield ("all_gather_rows", logits, self.b_logits_loc[:M], M)
-        if self.max_seq:
-            ctx.check(L.rrr_position_advance(ctx.h, dpos, M, st))
-            self.pos += M
-
-    def _exchange(self, op, st) -> None:
-        dist = self.dist
-        if self.p2p is not None:
-            if op[0] == "all_reduce":
-                self.p2p.all_reduce(op[1], st)
-            elif op[0] == "all_gather":
-                self.p2p.all_gather(op[1], op[2], st)
-            else:
-                self.ctx.check(ffi.lib().rrr_comm_allgather_rows_f32(
-                    self.p2p.h, c_void_p(op[1].data_ptr()), c_void_p(op[2].data_ptr()), op[3],
-                    op[2].numel() // op[3], st))
-        elif op[0] == "all_reduce":
-            dist.all_reduce(op[1], group=self.group)
-        elif op[0] == "all_gather":
-            dist.all_gather_into_tensor(op[1], op[2], group=self.group)
-        else:
-            G, M = self.w.shard.G, op[3]
-            tmp = self.torch.empty(G * op[2].numel(), device=op[2].device)
-            dist.all_gather_into_tensor(tmp, op[2].reshape(-1), group=self.group)
-            op[1].view(M, G, -1).copy_(tmp.view(G, M, -1).permute(1, 0, 2))
-
-    def forward_batched(self, hidden, logits, M: int, use_graph: bool = False) -> None:
-        """One batched step of M tokens on the current stream (see steps_batched); with
-        use_graph the step is captured on the first call for these tensors and M."""
-        torch = self.torch
-        if not use_graph:
-            st = c_void_p(torch.cuda.current_stream().cuda_stream)
-            for op in self.steps_batched(hidden, logits, M):
-                self._exchange(op, st)
-            return
-        key = ("b", hidden.data_ptr(), logits.data_ptr(), M)
-        if self.max_seq and self.pos + M > self.max_seq:
-            raise ValueError(f"positions {self.pos}..{self.pos + M - 1} exceed the cache of "
-                             f"{self.max_seq} rows")
-        if self.graph is None or self._graph_key != key:
-            self.release_graph()
-            saved = hidden.clone()
-            p0 = self.pos
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                for op in self.steps_batched(hidden, logits, M):
-                    self._exchange(op, c_void_p(s.cuda_stream))
-            torch.cuda.current_stream().wait_stream(s)
-            hidden.copy_(saved)
-            if self.max_seq:  # the warm-up wrote these positions' cache rows: run them again
-                self.set_position(p0)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, capture_error_mode="relaxed"):
-                st = c_void_p(torch.cuda.current_stream().cuda_stream)
-                for op in self.steps_batched(hidden, logits, M):
-                    self._exchange(op, st)
-            self.pos = p0
-            self.graph, self._graph_key = g, key
-        self.graph.replay()
-        if self.max_seq:
-            self.pos += M
+    @property
+    def pos(self) -> int:
+        n = ctypes.c_int()
+        self.ctx.check(ffi.lib().rrr_phi4_position(self.h, ctypes.byref(n)))
+        return n.value
 
     def launches_per_step(self) -> int:
         """Kernels of this library per step (NCCL collectives not counted; the peer-memory
         exchanges are)."""
-        cfg = self.w.cfg
-        n = 4 * cfg.n_layers + -(-self.w.shard.vocab_rows // cfg.logits_chunk_rows) + 1
-        if self.max_seq:
-            n += cfg.n_layers + 1  # fused RoPE + KV + attention per layer, position advance
-        if self.p2p is not None:
-            n += 2 * cfg.n_layers + 1
-        return n
+        n = ctypes.c_int()
+        self.ctx.check(ffi.lib().rrr_phi4_launches_per_step(self.h, ctypes.byref(n)))
+        return n.value
 
-    def forward(self, hidden, logits, argmax=None, use_graph: bool = False) -> None:
-        """One step on the current stream. hidden / logits / argmax are torch tensors on
-        this rank's device; with use_graph the step is captured on the first call for these
-        tensors and replayed afterwards."""
-        if not use_graph:
-            self._issue(hidden, logits, argmax)
-            return
-        torch = self.torch
-        key = (hidden.data_ptr(), logits.data_ptr(), None if argmax is None else argmax.data_ptr())
-        if self.max_seq and self.pos >= self.max_seq:
-            raise ValueError(f"position {self.pos} is past the cache of {self.max_seq} rows")
-        if self.graph is None or self._graph_key != key:
-            self.release_graph()
-            saved = hidden.clone()
-            p0 = self.pos
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                # warm-up outside the capture (first collectives set up the communicator)
-                self._issue(hidden, logits, argmax)
-            torch.cuda.current_stream().wait_stream(s)
-            hidden.copy_(saved)
-            if self.max_seq:  # the warm-up wrote this position's cache row: decode it again
-                self.set_position(p0)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, capture_error_mode="relaxed"):
-                self._issue(hidden, logits, argmax)
-            self.pos = p0
-            self.graph, self._graph_key = g, key
-        self.graph.replay()
-        if self.max_seq:
-            self.pos += 1
-
-    def release_graph(self) -> None:
-        """Drop the captured graph (it holds NCCL calls: release it before the process
-        group is destroyed)."""
-        if self.graph is not None:
-            self.graph.reset()
-            self.graph = None
-            self._graph_key = None
+    def close(self) -> None:
+        """Destroys the rank's step (its graphs hold the collectives: before the process
+        group goes) and its channel (collective for the peer-memory one)."""
+        if self.h:
+            ffi.lib().rrr_phi4_destroy(self.h)
+            self.h = None
+        if self.channel is not None:
+            self.channel.close()
+            self.channel = None
 
 
-def emulate_step(decoders, hiddens, logits_list, argmaxes=None, batch: int = 0) -> None:
-    """Runs the ranks' steps of one process (all shards on the current device) in lockstep,
-    doing each exchange with torch ops: the sum of the ranks' tensors for an all-reduce,
-    the concatenation for an all-gather. batch > 0: the batched step of that many tokens.
-    For checking the split on one GPU."""
-    import torch
-    if batch:
-        gens = [dec.steps_batched(h, lg, batch) for dec, h, lg in zip(decoders, hiddens, logits_list)]
-    else:
-        gens = [dec.steps(h, lg, None if argmaxes is None else argmaxes[i])
-                for i, (dec, h, lg) in enumerate(zip(decoders, hiddens, logits_list))]
-    while True:
-        ops = []
-        for gi in gens:
-            try:
-                ops.append(next(gi))
-            except StopIteration:
-                ops.append(None)
-        if all(o is None for o in ops):
-            return
-        if any(o is None for o in ops):
-            raise RuntimeError("ranks disagree on the exchange sequence")
-        if ops[0][0] == "all_reduce":
-            total = torch.stack([o[1] for o in ops]).sum(0)
-            for o in ops:
-                o[1].copy_(total)
-        elif ops[0][0] == "all_gather":
-            full = torch.cat([o[2] for o in ops])
-            for o in ops:
-                o[1].copy_(full)
-        else:
-            M = ops[0][3]
-            full = torch.cat([o[2].reshape(M, -1) for o in ops], dim=1)
-            for o in ops:
-                o[1].view(M, -1).copy_(full)
+def emulate_step(decoders, hiddens, logits_list, argmaxes=None, batch: int = 0, stream=None) -> None:
+    """Runs the G ranks of one split (decoders made with comm=None, all on the current GPU)
+    in lockstep with local exchanges (rrr_phi4_tp_forward_emulated): sums in rank order,
+    concatenation for the logits. batch > 0: the batched step of that many tokens. For
+    checking the split on one GPU."""
+    G = len(decoders)
+    ranks = (c_void_p * G)(*[dec.h.value for dec in decoders])
+    hs = (c_void_p * G)(*[h.data_ptr() for h in hiddens])
+    lgs = (c_void_p * G)(*[lg.data_ptr() for lg in logits_list])
+    ams = None
+    if argmaxes is not None:
+        ams = (c_void_p * G)(*[a.data_ptr() if a is not None else None for a in argmaxes])
+    ctx = decoders[0].ctx
+    ctx.check(ffi.lib().rrr_phi4_tp_forward_emulated(ranks, G, hs, lgs, ams, batch,
+                                                     TPDecoder._stream(stream)))

@@ -65,6 +65,22 @@ def test_exchange_wait_expires_when_a_rank_never_arrives(rrr, ctx, oracle):
         assert rc == -7, rrr.ffi.last_error(ctx.h)                   # RRR_ERR_TIMEOUT
         assert code.value == 5                                       # exchange wait gave up
         assert 0.04 < elapsed < 5.0, elapsed
+        # the host deadline of the tensor-parallel channel (rrr_tp_wait) ends before the
+        # device's own 400 ms limit; the kernel then gives up by itself
+        tpc = c_void_p()
+        ctx.check(L.rrr_tp_comm_p2p(comm, ctypes.byref(tpc)))
+        ctx.check(L.rrr_set_wait_limit(ctx.h, 400_000_000))
+        torch.cuda.synchronize()
+        t0 = time.time()
+        ctx.check(L.rrr_comm_allreduce_f32(comm, c_void_p(x.data_ptr()), 4096, None))
+        rc = L.rrr_tp_wait(tpc, None, 30)
+        waited = time.time() - t0
+        assert rc == -7 and "30 ms" in rrr.ffi.last_error(ctx.h), rrr.ffi.last_error(ctx.h)
+        assert waited < 0.3, waited
+        rc = L.rrr_check_device_error(ctx.h, ctypes.byref(code))
+        assert rc == -7 and code.value == 5
+        assert time.time() - t0 > 0.35
+        L.rrr_tp_comm_destroy(tpc)
         # the context and the GPU still answer: a GEMV checked against the oracle
         ctx.check(L.rrr_set_wait_limit(ctx.h, 0))
         rng = np.random.default_rng(5)
@@ -87,6 +103,38 @@ def test_exchange_wait_expires_when_a_rank_never_arrives(rrr, ctx, oracle):
         if peer.is_alive():
             peer.kill()
     assert peer.exitcode == 0
+
+
+@pytest.mark.gpu
+def test_tp_wait_with_a_one_rank_nccl_communicator(rrr, ctx):
+    """NCCL loaded at run time by the library: a 1-rank communicator, a tensor-parallel
+    rank of G = 1 on it, one step, and rrr_tp_wait returning on the completed stream."""
+    import torch
+    phi4 = importlib.import_module("recursive-routing-racer-rs_b200.phi4")
+    L = rrr.ffi.lib()
+    uid = ctypes.create_string_buffer(128)
+    ctx.check(L.rrr_tp_nccl_unique_id(uid))
+    tpc = c_void_p()
+    ctx.check(L.rrr_tp_comm_nccl(ctx.h, uid, 0, 1, ctypes.byref(tpc)))
+    cfg = phi4.ModelConfig(n_layers=1, vocab_size=4096)
+    w = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, 1, 0), seed=2)
+    d, keep = w.desc()
+    sh = tp.c_shard(w.shard)
+    m = c_void_p()
+    ctx.check(L.rrr_phi4_tp_create(ctx.h, ctypes.byref(d), ctypes.byref(sh), tpc, ctypes.byref(m)))
+    h = torch.randn(cfg.d_model, device="cuda")
+    lg = torch.empty(cfg.vocab_size, device="cuda")
+    ctx.check(L.rrr_phi4_forward(m, c_void_p(h.data_ptr()), c_void_p(lg.data_ptr()), None, 1, None))
+    ctx.check(L.rrr_tp_wait(tpc, None, 10000))
+    assert torch.isfinite(lg).all()
+    # a shard that is not the plan's is refused
+    bad = tp.c_shard(w.shard)
+    bad.ffn1 -= 256
+    m2 = c_void_p()
+    assert L.rrr_phi4_tp_create(ctx.h, ctypes.byref(d), ctypes.byref(bad), tpc, ctypes.byref(m2)) == -3
+    L.rrr_phi4_destroy(m)
+    L.rrr_tp_comm_destroy(tpc)
+    w.close()
 
 
 def test_wait_limit_range_is_checked(rrr):
@@ -145,3 +193,19 @@ def test_host_deadline_on_a_skipped_collective():
     assert res[0][0] and res[1][0]
     assert res[0][1] is not None and "deadline" in res[0][1]
     assert 1.5 < res[0][2] < 20.0
+
+
+def test_tp_watchdog_loop_with_fakes(tmp_path):
+    """The host watchdog of the tensor-parallel step (csrc/tp_watchdog.h, behind
+    rrr_tp_wait) compiled with g++ and run against fake stream / communicator operations:
+    completion, a stream error, an asynchronous communicator error and a missed deadline,
+    each with the communicator aborted exactly when it must be."""
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path / "test_tp_watchdog")
+    subprocess.run(["g++", "-std=c++17", "-O1", "-Wall", "-Werror",
+                    "-I", os.path.join(root, "recursive-routing-racer-rs_b200", "csrc"),
+                    os.path.join(root, "tests", "cpp", "test_tp_watchdog.cpp"), "-o", exe], check=True)
+    out = subprocess.run([exe], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert out.stdout.strip() == "ok"
