@@ -296,9 +296,21 @@ int rrr_gguf_meta_str(rrr_gguf* g, const char* key, const char** out);
 int rrr_gguf_version(rrr_gguf* g, uint32_t* version);
 int rrr_gguf_data_offset(rrr_gguf* g, uint64_t* off);
 /* Copy one tensor's raw bytes from the mapping to a new device buffer (raw, no repack;
- * the weight upload of load_weight_gpu, phi4.rs:744-771, without repack_q*k). */
+ * the weight upload of load_weight_gpu, phi4.rs:744-771, without repack_q*k): one
+ * rrr_gguf_load of one tensor. Free *dptr with rrr_free. */
 int rrr_gguf_upload(rrr_ctx* ctx, rrr_gguf* g, const char* name, void** dptr,
                     uint64_t* n_bytes);
+/* Upload n tensors into ONE new device allocation (each 256-byte aligned, in the order
+ * given): dptrs[i] receives tensor i's device address (dptrs[0] is the allocation: free it
+ * with rrr_free to release all), n_bytes[i] (may be NULL) its size, *seconds (may be NULL)
+ * the wall time. The bytes go from the mapping into two reusable pinned buffers (32 MB,
+ * filled by 8 host threads) and from there to the device with cudaMemcpyAsync on the
+ * file's copy stream, each DMA overlapping the host copy of the next chunk; the call
+ * returns when the data is on the device. Replaces load_weight_gpu's per-tensor upload
+ * into mapped memory (phi4.rs:744-771). The staging stays with the file (rrr_gguf_close
+ * frees it) and serves one device. */
+int rrr_gguf_load(rrr_ctx* ctx, rrr_gguf* g, const char* const* names, int n, void** dptrs,
+                  uint64_t* n_bytes, double* seconds);
 
 /* ---- decode attention at real positions (per-layer glue between the QKV and the
  *      O-projection GEMVs of forward_gpu / forward_dynamic: phi4.rs:1115-1121,

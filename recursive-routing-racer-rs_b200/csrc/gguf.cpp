@@ -9,14 +9,22 @@
 //    instead of panicking, and unknown value types are an error (the reference skips one
 //    byte, gguf.rs:115).
 //  * Tensor byte sizes follow the same per-type table (gguf.rs:173-195).
+//  * Uploads go through reusable pinned staging (two buffers, host copies from the mapping
+//    by several threads, cudaMemcpyAsync on a copy stream, each DMA overlapping the host
+//    copy of the next chunk) instead of per-tensor synchronous copies from pageable
+//    memory; rrr_gguf_load places many tensors in one device allocation.
+#include <cuda_runtime.h>
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <map>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "capi_internal.h"
@@ -120,7 +128,18 @@ uint64_t type_bytes(uint32_t t, uint64_t n) {
 
 }  // namespace
 
+// Pinned staging of the uploads: two host buffers, a copy stream and an event per buffer.
+struct Staging {
+  static constexpr size_t kChunk = 32u << 20;  // bytes per staged copy
+  static constexpr int kThreads = 8;           // host threads copying out of the mapping
+  void* pinned[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  cudaStream_t stream = nullptr;
+  int device = -1;
+};
+
 struct rrr_gguf {
+  Staging staging;
   int fd = -1;
   const uint8_t* map = nullptr;
   size_t size = 0;
@@ -215,6 +234,19 @@ int rrr_gguf_open(const char* path, rrr_gguf** out) {
 
 int rrr_gguf_close(rrr_gguf* g) {
   if (!g) return RRR_OK;
+  Staging& st = g->staging;
+  if (st.stream) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(st.device);
+    cudaStreamSynchronize(st.stream);
+    cudaStreamDestroy(st.stream);
+    for (int b = 0; b < 2; ++b) {
+      if (st.done[b]) cudaEventDestroy(st.done[b]);
+      if (st.pinned[b]) cudaFreeHost(st.pinned[b]);
+    }
+    cudaSetDevice(cur);
+  }
   if (g->map) munmap(const_cast<uint8_t*>(g->map), g->size);
   if (g->fd >= 0) ::close(g->fd);
   delete g;
@@ -283,24 +315,83 @@ int rrr_gguf_data_offset(rrr_gguf* g, uint64_t* off) {
 }
 
 int rrr_gguf_upload(rrr_ctx* ctx, rrr_gguf* g, const char* name, void** dptr, uint64_t* n_bytes) {
+  if (!name) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gguf_upload: null argument");
+  uint64_t nb = 0;
+  const int rc = rrr_gguf_load(ctx, g, &name, 1, dptr, &nb, nullptr);
+  if (rc == RRR_OK && n_bytes) *n_bytes = nb;
+  return rc;
+}
+
+int rrr_gguf_load(rrr_ctx* ctx, rrr_gguf* g, const char* const* names, int n, void** dptrs,
+                  uint64_t* n_bytes, double* seconds) {
   if (!ctx) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null context");
-  if (!g || !name || !dptr) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gguf_upload: null argument");
-  *dptr = nullptr;
-  rrr_gguf_tensor t;
-  if (rrr_gguf_find_tensor(g, name, &t) != RRR_OK)
-    return set_error(ctx, RRR_ERR_INVALID_ARG, "Tensor not found: %s", name);
+  if (!g || !names || !dptrs || n < 1) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gguf_load: bad arguments");
+  for (int i = 0; i < n; ++i) dptrs[i] = nullptr;
+  std::vector<rrr_gguf_tensor> ts(n);
+  std::vector<size_t> offs(n);
+  size_t total = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!names[i] || rrr_gguf_find_tensor(g, names[i], &ts[i]) != RRR_OK)
+      return set_error(ctx, RRR_ERR_INVALID_ARG, "Tensor not found: %s", names[i] ? names[i] : "(null)");
+    offs[i] = total;
+    total += (ts[i].n_bytes + 255) & ~(uint64_t)255;  // 256-byte aligned tensors
+  }
   int rc = bind_device(ctx);
   if (rc) return rc;
-  void* d = nullptr;
-  cudaError_t e = cudaMalloc(&d, t.n_bytes ? t.n_bytes : 1);
-  if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_gguf_upload: cudaMalloc");
-  e = cudaMemcpy(d, t.data, t.n_bytes, cudaMemcpyHostToDevice);
-  if (e != cudaSuccess) {
-    cudaFree(d);
-    return cuda_error(ctx, e, "rrr_gguf_upload: copy");
+  const auto t0 = std::chrono::steady_clock::now();
+  Staging& st = g->staging;
+  cudaError_t e = cudaSuccess;
+  if (st.device != ctx->device) {
+    // first upload on this device: pinned buffers, events, a copy stream (kept until close)
+    if (st.stream) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gguf_load: the file's staging belongs to another device");
+    for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+      e = cudaHostAlloc(&st.pinned[b], Staging::kChunk, cudaHostAllocDefault);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&st.done[b], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_gguf_load: staging");
+    st.device = ctx->device;
   }
-  *dptr = d;
-  if (n_bytes) *n_bytes = t.n_bytes;
+  void* arena = nullptr;
+  e = cudaMalloc(&arena, total ? total : 256);
+  if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_gguf_load: cudaMalloc");
+  char* base = static_cast<char*>(arena);
+  int b = 0;
+  bool used[2] = {false, false};
+  for (int i = 0; i < n && e == cudaSuccess; ++i) {
+    const uint8_t* src = static_cast<const uint8_t*>(ts[i].data);
+    for (uint64_t done = 0; done < ts[i].n_bytes && e == cudaSuccess;) {
+      const size_t len = (size_t)std::min<uint64_t>(Staging::kChunk, ts[i].n_bytes - done);
+      // the buffer's previous DMA must have finished before it is overwritten
+      if (used[b]) e = cudaEventSynchronize(st.done[b]);
+      if (e != cudaSuccess) break;
+      char* dst = static_cast<char*>(st.pinned[b]);
+      const uint8_t* from = src + done;
+      const size_t part = (len + Staging::kThreads - 1) / Staging::kThreads;
+      std::vector<std::thread> th;
+      for (int k = 1; k < Staging::kThreads && (size_t)k * part < len; ++k)
+        th.emplace_back([=] { memcpy(dst + k * part, from + k * part, std::min(part, len - k * part)); });
+      memcpy(dst, from, std::min(part, len));
+      for (auto& t : th) t.join();
+      e = cudaMemcpyAsync(base + offs[i] + done, dst, len, cudaMemcpyHostToDevice, st.stream);
+      if (e == cudaSuccess) e = cudaEventRecord(st.done[b], st.stream);
+      used[b] = true;
+      done += len;
+      b ^= 1;
+    }
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st.stream);
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(st.stream);
+    cudaFree(arena);
+    return cuda_error(ctx, e, "rrr_gguf_load: copy");
+  }
+  for (int i = 0; i < n; ++i) {
+    dptrs[i] = base + offs[i];
+    if (n_bytes) n_bytes[i] = ts[i].n_bytes;
+  }
+  if (seconds)
+    *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
   return RRR_OK;
 }
 

@@ -125,6 +125,8 @@ PROTOS = {
     "rrr_gguf_version": (c_int, [vp, POINTER(c_uint32)]),
     "rrr_gguf_data_offset": (c_int, [vp, POINTER(c_uint64)]),
     "rrr_gguf_upload": (c_int, [vp, vp, c_char_p, POINTER(vp), POINTER(c_uint64)]),
+    "rrr_gguf_load": (c_int, [vp, vp, POINTER(c_char_p), c_int, POINTER(vp), POINTER(c_uint64),
+                              POINTER(ctypes.c_double)]),
     "rrr_phi4_create": (c_int, [vp, POINTER(Phi4Desc), POINTER(vp)]),
     "rrr_phi4_forward": (c_int, [vp, vp, vp, vp, c_int, vp]),
     "rrr_phi4_forward_batched": (c_int, [vp, vp, vp, vp, c_int, c_int, vp]),

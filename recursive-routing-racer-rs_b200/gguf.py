@@ -53,6 +53,18 @@ class GGUFModel:
         ffi.check(ffi.lib().rrr_gguf_open(path.encode(), ctypes.byref(h)), None)
         return cls(h)
 
+    def load_tensors(self, ctx: ffi.Context, names):
+        """rrr_gguf_load: the named tensors into one device allocation through the file's
+        pinned staging. Returns (device pointers, sizes, seconds); rrr_free of pointers[0]
+        releases all of them."""
+        n = len(names)
+        arr = (ctypes.c_char_p * n)(*[nm.encode() for nm in names])
+        ptrs = (ctypes.c_void_p * n)()
+        sizes = (ctypes.c_uint64 * n)()
+        secs = ctypes.c_double()
+        ctx.check(ffi.lib().rrr_gguf_load(ctx.h, self.h, arr, n, ptrs, sizes, ctypes.byref(secs)))
+        return [p for p in ptrs], [int(x) for x in sizes], secs.value
+
     def _find(self, name: str) -> ffi.GGUFTensor:
         t = ffi.GGUFTensor()
         self._check(ffi.lib().rrr_gguf_find_tensor(self.h, name.encode(), ctypes.byref(t)))

@@ -142,3 +142,46 @@ def test_upload_and_gemv_from_gguf(rrr, ctx, oracle, gfile):
         assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-4
         ctx.check(L.rrr_free(ctx.h, c_void_p(dptr)))
     g.close()
+
+
+@pytest.mark.gpu
+def test_gguf_load_many_tensors_through_pinned_staging(rrr, ctx, tmp_path):
+    """rrr_gguf_load: several tensors, one of 100 MB (four 32 MB staging chunks, both pinned
+    buffers reused twice) and several not multiples of the chunk, into one device
+    allocation; every byte on the device equals the file's, twice in a row (the staging is
+    reused by the second call)."""
+    import torch
+    from ctypes import c_char_p, c_double, c_uint64, c_void_p
+    from gguf import GGMLQuantizationType as T
+    path = str(tmp_path / "load.gguf")
+    rng = np.random.default_rng(9)
+    w = gguf.GGUFWriter(path, "phi3")
+    data = {}
+    for name, rows, nb in [("a.weight", 3, 1), ("big.weight", 2048 * 2, 171),   # 100.9 MB Q4_K
+                           ("c.weight", 77, 5), ("d.weight", 1, 12)]:
+        raw = rng.integers(0, 256, size=(rows, nb * 144), dtype=np.uint8)
+        w.add_tensor(name, raw, raw_dtype=T.Q4_K)
+        data[name] = raw.reshape(-1)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    g = rrr.GGUFModel.load(path)
+    L = rrr.ffi.lib()
+    names = list(data)
+    arr = (c_char_p * len(names))(*[n.encode() for n in names])
+    for _ in range(2):
+        ptrs = (c_void_p * len(names))()
+        sizes = (c_uint64 * len(names))()
+        secs = c_double()
+        ctx.check(L.rrr_gguf_load(ctx.h, g.h, arr, len(names), ptrs, sizes, ctypes.byref(secs)))
+        assert ptrs[0] is not None and all(p % 256 == 0 for p in ptrs)
+        for i, n in enumerate(names):
+            assert sizes[i] == data[n].nbytes
+            host = np.empty(data[n].nbytes, np.uint8)
+            ctx.check(L.rrr_d2h(ctx.h, c_void_p(host.ctypes.data), c_void_p(ptrs[i]), host.nbytes, None))
+            ctx.check(L.rrr_sync(ctx.h, None))
+            assert np.array_equal(host, data[n]), n
+        assert secs.value > 0
+        ctx.check(L.rrr_free(ctx.h, c_void_p(ptrs[0])))
+    g.close()
