@@ -453,8 +453,9 @@ def run_ours(args, rank, world, local_rank):
         tl = torch.empty(cfg.vocab_size, device="cuda")
         ta = torch.zeros(1, dtype=torch.int32, device="cuda")
 
-        def time_tp(comm):
-            tdec = tpm.TPDecoder(ctx, tw, comm=comm)
+        def time_tp(comm, fused=True):
+            tdec = tpm.TPDecoder(ctx, tw, comm=comm, fused=fused)
+            is_fused = comm == "p2p" and tdec.fused
             for _ in range(max(3, args.warmup)):
                 tdec.forward(th, tl, ta, use_graph=True)
             barrier()
@@ -467,10 +468,13 @@ def run_ours(args, rank, world, local_rank):
             t = max_over_ranks(t0e.elapsed_time(t1e) / dsteps)
             n_l = tdec.launches_per_step()
             tdec.close()
-            return t, n_l
+            return t, n_l, is_fused
 
-        tms, tl_p2p = time_tp("p2p")
-        tms_nccl, _ = time_tp("nccl")
+        # the all-reduces fused into the GEMVs (peer-memory pushes), the exchange kernels
+        # between the GEMVs, and NCCL collectives
+        tms, tl_p2p, tp_fused = time_tp("p2p")
+        tms_unf, tl_unf, _ = time_tp("p2p", fused=False)
+        tms_nccl, _, _ = time_tp("nccl")
         # at real positions: KV caches of the rank's heads, positions 1024 .. 1024 + steps
         kdec = tpm.TPDecoder(ctx, tw, comm="p2p", max_seq=2048)
         kdec.set_position(1024 - max(3, args.warmup))
@@ -503,10 +507,13 @@ def run_ours(args, rank, world, local_rank):
         # the tensor-parallel decode step over all ranks (peer-memory exchanges;
         # NCCL beside it), batch 1 at position 0 and at positions 1024+, and batch 64
         tp_decode = {"n_gpus": world, "tok_s": round(1e3 / tms, 2), "ms_per_token": round(tms, 4),
+                     "fused_exchanges": tp_fused,
+                     "tok_s_exchange_kernels": round(1e3 / tms_unf, 2),
                      "tok_s_nccl": round(1e3 / tms_nccl, 2),
                      "kv_tok_s": round(1e3 / tkms, 2), "batch64_tok_s": round(BM * 1e3 / tbms, 1),
                      "GBps_per_rank": round(tw.shard_bytes() / tms / 1e6, 1),
-                     "exchanges_per_token": 2 * cfg.n_layers + 1, "launches_per_token": tl_p2p}
+                     "exchange_kernels_per_token": (3 if tp_fused else 2 * cfg.n_layers + 1),
+                     "launches_per_token": tl_p2p, "launches_per_token_exchange_kernels": tl_unf}
         tw.close()
     # ---------------- end to end through the C ABI with host buffers (pinned): copy every
     # x of the step in, replay the prebuilt table, copy every y out, synchronise

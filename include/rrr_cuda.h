@@ -437,6 +437,17 @@ int rrr_phi4_destroy(rrr_phi4* m);
 typedef struct rrr_comm rrr_comm;
 int rrr_comm_create(rrr_ctx* ctx, int rank, int world, int64_t max_elems, rrr_comm** out,
                     void* ipc_handle_out /* 64 bytes */);
+/* The same with a fused-exchange region of `fused_words` 8-byte words after the exchange
+ * slots, in the same IPC-shared allocation. A tensor-parallel rank made on this channel
+ * (rrr_phi4_tp_create) fuses the all-reduces of its one-token step into the GEMVs when the
+ * region holds 2 * n_layers * world * d_model words and every peer is on another GPU: the
+ * O-projection and down GEMVs push their partial rows, tagged with the step's epoch, into
+ * the peers' regions and the next RMSNorm GEMV sums them in rank order in its prologue (the
+ * bits of the exchange kernel's all-reduce; no exchange kernels between the GEMVs). The
+ * step epoch lives in the channel, so rank models made one after another on it stay in
+ * step; one rank model at a time per channel. */
+int rrr_comm_create_ex(rrr_ctx* ctx, int rank, int world, int64_t max_elems, int64_t fused_words,
+                       rrr_comm** out, void* ipc_handle_out /* 64 bytes */);
 int rrr_comm_connect(rrr_comm* comm, const void* ipc_handles /* world x 64 bytes */);
 int rrr_comm_allreduce_f32(rrr_comm* comm, float* x, int64_t n, void* stream);
 int rrr_comm_allgather_f32(rrr_comm* comm, float* out, const float* part, int64_t n_per_rank,
@@ -511,6 +522,9 @@ int rrr_tp_comm_destroy(rrr_tp_comm* comm);
  * captured in its CUDA graph). Every rank must run the same calls in the same order. */
 int rrr_phi4_tp_create(rrr_ctx* ctx, const rrr_phi4_desc* desc, const rrr_tp_shard* shard,
                        rrr_tp_comm* comm, rrr_phi4** out);
+/* 1 when the one-token step's all-reduces are fused into its GEMVs (rrr_comm_create_ex),
+ * else 0. */
+int rrr_phi4_tp_fused(rrr_phi4* m, int* fused);
 /* All G ranks of one split on the calling process's GPU, run in lockstep with the
  * exchanges done by local kernels (sums in rank order): for checking the split on one GPU.
  * ranks[r] are rrr_phi4_tp_create models of ranks r = 0..G-1 of one context; hidden[r],

@@ -33,6 +33,13 @@ int tp_allreduce(rrr_tp_comm* c, float* x, int64_t n, void* stream);
 int tp_allgather_rows(rrr_tp_comm* c, float* out, const float* part, int rows, int64_t npr,
                       void* stream);
 void comm_info(const rrr_comm* c, rrr_ctx** ctx, int* rank, int* world, int64_t* max_elems);
+// The fused-exchange regions of every rank of a connected communicator (bases[r]: rank r's,
+// mapped into this process) and the step epoch of the fused exchanges (device counter,
+// zero at creation); returns the regions' size in 8-byte words, 0 when there is none or a
+// peer shares this rank's GPU.
+int64_t comm_fused(const rrr_comm* c, unsigned long long** bases, unsigned** epoch);
+// The rrr_comm of a peer-memory channel (NULL for NCCL).
+rrr_comm* tp_comm_p2p_of(rrr_tp_comm* c);
 // Argument rules of one single-token GEMV (rrr_gemv_kq_ex; swiglu: rrr_gemv_kq_swiglu
 // with N = F).
 int check_gemv(rrr_ctx* ctx, int qtype, const void* w, const float* x, float* y, int K, int N,

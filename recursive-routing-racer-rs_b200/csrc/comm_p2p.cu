@@ -2,7 +2,9 @@
 // NVLink peer memory, for the tensor-parallel decode step (one process per GPU).
 //
 // Every rank owns an exchange buffer, mapped into the other ranks' processes through CUDA
-// IPC handles: slots[2][world][max_elems] of 8-byte words. Each word carries one value
+// IPC handles: a 256-byte header (the owner's GPU UUID and region sizes, read by the peers
+// when they connect), then slots[2][world][max_elems] of 8-byte words, then the optional
+// fused-exchange region of the decode step's GEMVs. Each word carries one value
 // and the epoch of the call that wrote it (value bits low, epoch high), stored and loaded
 // as one naturally aligned 64-bit access (single-copy atomic), so the receiver waits on
 // the data itself: no fences and no separate flags, one NVLink trip per exchange. A call
@@ -36,40 +38,25 @@ namespace {
 constexpr int kMaxCtas = 64;
 constexpr int kMaxWorld = 8;
 constexpr int kThreadsX = 256;  // few registers: co-resident with a finishing GEMV
-constexpr int kDevErrCommTimeout = 5;
+
+constexpr size_t kHeaderBytes = 256;
+
+// What a rank's buffer says about its owner (at offset 0; the peers read it at connect).
+struct BufHeader {
+  unsigned char uuid[16];  // the owner's GPU
+  int64_t max_elems, fused_words;
+  int32_t world, rank;
+};
 
 struct Peers {
   unsigned long long* slots[kMaxWorld];  // each rank's buffer (this rank's own at index rank)
 };
 
-__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // The value of word p once its epoch is e; gives up (ok = false) after the context's wait
 // limit (wait_limit_ns).
 __device__ __forceinline__ float wait_word(const unsigned long long* p, unsigned e, bool& ok,
                                            int* err) {
-  unsigned long long w = ld_relaxed_sys_u64(p);
-  if ((unsigned)(w >> 32) != e && ok) {
-    const uint64_t t0 = globaltimer_ns();
-    const uint64_t limit = wait_limit_ns(err);
-    for (int i = 0;; ++i) {
-      w = ld_relaxed_sys_u64(p);
-      if ((unsigned)(w >> 32) == e) break;
-      if ((i & 63) == 63 && globaltimer_ns() - t0 > limit) {
-        atomicCAS(err, 0, kDevErrCommTimeout);
-        ok = false;
-        break;
-      }
-    }
-  }
-  return __uint_as_float((unsigned)w);
+  return __uint_as_float((unsigned)wait_tagged(p, ld_relaxed_sys_u64(p), e, ok, err));
 }
 
 // mode 0: x[i] = sum over ranks (in place allowed); mode 1: all-gather, element i of rank
@@ -123,12 +110,15 @@ struct rrr_comm {
   rrr_ctx* ctx = nullptr;
   int rank = 0, world = 0;
   int64_t max_elems = 0;
+  int64_t fused_words = 0;  // words of the fused-exchange region after the slots
   char* local = nullptr;  // this rank's exchange buffer
-  size_t bytes = 0;
+  size_t bytes = 0;       // slots + fused region
+  size_t slot_bytes = 0;  // the exchange kernels' slots (the fused region starts here)
   unsigned* counters = nullptr;
   std::vector<char*> mapped;  // peers' buffers (nullptr at this rank's index)
   rrr::Peers peers{};
   bool connected = false;
+  bool distinct_devices = false;  // every peer's buffer lives on another GPU
 };
 
 using namespace rrr;
@@ -144,13 +134,28 @@ void comm_info(const rrr_comm* c, rrr_ctx** ctx, int* rank, int* world, int64_t*
   *world = c->world;
   *max_elems = c->max_elems;
 }
+
+int64_t comm_fused(const rrr_comm* c, unsigned long long** bases, unsigned** epoch) {
+  if (!c->connected || c->fused_words == 0 || !c->distinct_devices) return 0;
+  *epoch = c->counters + kMaxCtas;
+  for (int r = 0; r < c->world; ++r)
+    bases[r] = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(c->peers.slots[r]) +
+                                                     c->slot_bytes);
+  return c->fused_words;
+}
 }  // namespace rrr
 
 extern "C" {
 
 int rrr_comm_create(rrr_ctx* ctx, int rank, int world, int64_t max_elems, rrr_comm** out,
                     void* handle_out) {
+  return rrr_comm_create_ex(ctx, rank, world, max_elems, 0, out, handle_out);
+}
+
+int rrr_comm_create_ex(rrr_ctx* ctx, int rank, int world, int64_t max_elems, int64_t fused_words,
+                       rrr_comm** out, void* handle_out) {
   if (!ctx) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null context");
+  if (fused_words < 0) return set_error(ctx, RRR_ERR_BAD_SHAPE, "rrr_comm_create_ex: fused_words >= 0");
   if (!out || !handle_out) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_comm_create: null argument");
   *out = nullptr;
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || max_elems < 1)
@@ -163,11 +168,23 @@ int rrr_comm_create(rrr_ctx* ctx, int rank, int world, int64_t max_elems, rrr_co
   c->rank = rank;
   c->world = world;
   c->max_elems = (max_elems + 3) / 4 * 4;
-  c->bytes = data_bytes(world, c->max_elems);
-  cudaError_t e = cudaMalloc(&c->local, c->bytes);
+  c->slot_bytes = data_bytes(world, c->max_elems);
+  c->fused_words = (fused_words + 31) / 32 * 32;
+  c->bytes = kHeaderBytes + c->slot_bytes + (size_t)c->fused_words * sizeof(unsigned long long);
+  BufHeader hdr{};
+  cudaDeviceProp prop{};
+  cudaError_t e = cudaGetDeviceProperties(&prop, ctx->device);
+  memcpy(hdr.uuid, &prop.uuid, 16);
+  hdr.max_elems = c->max_elems;
+  hdr.fused_words = c->fused_words;
+  hdr.world = world;
+  hdr.rank = rank;
+  if (e == cudaSuccess) e = cudaMalloc(&c->local, c->bytes);
   if (e == cudaSuccess) e = cudaMemset(c->local, 0, c->bytes);
-  if (e == cudaSuccess) e = cudaMalloc(&c->counters, kMaxCtas * sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, kMaxCtas * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemcpy(c->local, &hdr, sizeof hdr, cudaMemcpyHostToDevice);
+  // the exchange CTAs' call counters, then the fused exchanges' step epoch
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, (kMaxCtas + 1) * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, (kMaxCtas + 1) * sizeof(unsigned));
   cudaIpcMemHandle_t h;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->local);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -207,7 +224,42 @@ int rrr_comm_connect(rrr_comm* c, const void* handles) {
       c->mapped[r] = static_cast<char*>(p);
       base = c->mapped[r];
     }
-    c->peers.slots[r] = reinterpret_cast<unsigned long long*>(base);
+    c->peers.slots[r] = reinterpret_cast<unsigned long long*>(base + kHeaderBytes);
+  }
+  // The peers' headers: the same layout everywhere, and whose GPU each buffer is on. Kernels
+  // that wait on one another's stores may only run on different GPUs: the fused exchanges
+  // are enabled only then (the exchange kernels' waits stay bounded either way).
+  BufHeader mine{};
+  cudaError_t e = cudaMemcpy(&mine, c->local, sizeof mine, cudaMemcpyDeviceToHost);
+  c->distinct_devices = true;
+  for (int r = 0; r < c->world && e == cudaSuccess; ++r) {
+    if (r == c->rank) continue;
+    BufHeader h{};
+    e = cudaMemcpy(&h, c->mapped[r], sizeof h, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) break;
+    if (h.world != c->world || h.rank != r || h.max_elems != c->max_elems ||
+        h.fused_words != c->fused_words) {
+      for (char*& p : c->mapped)
+        if (p) {
+          cudaIpcCloseMemHandle(p);
+          p = nullptr;
+        }
+      return set_error(c->ctx, RRR_ERR_INVALID_ARG,
+                       "rrr_comm_connect: handle %d is rank %d of %d with %lld elements and %lld "
+                       "fused words; this rank expects rank %d of %d with %lld and %lld",
+                       r, (int)h.rank, (int)h.world, (long long)h.max_elems,
+                       (long long)h.fused_words, r, c->world, (long long)c->max_elems,
+                       (long long)c->fused_words);
+    }
+    if (memcmp(h.uuid, mine.uuid, 16) == 0) c->distinct_devices = false;
+  }
+  if (e != cudaSuccess) {
+    for (char*& p : c->mapped)
+      if (p) {
+        cudaIpcCloseMemHandle(p);
+        p = nullptr;
+      }
+    return cuda_error(c->ctx, e, "rrr_comm_connect: reading the peers' headers");
   }
   c->connected = true;
   return RRR_OK;

@@ -29,6 +29,11 @@
 //    and stores silu(gate) * up (the `silu_gate` shader, phi4.rs:1368-1373, fused).
 //  * Programmatic dependent launch: the producer starts streaming weights before
 //    griddepcontrol.wait; x is read and y written only after it.
+//  * Tensor-parallel step on peer memory (GemvFuse): the RMSNORM prologue can take its input
+//    as the rank-order sum of the G ranks' tagged partial rows (the all-reduce of the
+//    previous O-projection / down, waited for word by word), and the plain epilogue can push
+//    each finished row, tagged, to every rank instead of storing it: the exchange kernels
+//    between the GEMVs disappear.
 #include <algorithm>
 #include <cstdlib>
 
@@ -64,6 +69,12 @@ struct GemvParams {
   int row_stride, stage_bytes, nstages, dig_stride;
   int off_bars, off_dig, off_xscale, off_xsum, off_red, off_gate, off_misc;
   int* err;
+  // fused tensor-parallel exchange (GemvFuse; G = 0: off)
+  const unsigned long long* sum_in;
+  float* h_out;
+  unsigned long long* push[kMaxTpRanks];
+  int G;
+  const unsigned* epoch;
 };
 
 __device__ __forceinline__ void mma_u8s8(int& d0, int& d1, int& d2, int& d3, uint32_t a0,
@@ -349,8 +360,10 @@ __device__ __forceinline__ void block_q6(const uint8_t* b0, const uint8_t* b1, i
 
 // ---------------------------------------------------------------- x preparation
 // Raw inputs of elements k0 .. k0+7 (k0 a multiple of 8): v = x (after the GQA index map
-// or bf16 widening), a = gamma (RMSNORM) or up (SILU_GATE).
-__device__ __forceinline__ void load_raw8(const GemvParams& p, int k0, float v[8], float a[8]) {
+// or bf16 widening, or the sum of the ranks' tagged rows of epoch `tag` under GemvFuse), a =
+// gamma (RMSNORM) or up (SILU_GATE). `ok` turns false when a tagged word never arrived.
+__device__ __forceinline__ void load_raw8(const GemvParams& p, int k0, float v[8], float a[8],
+                                          unsigned tag, bool& ok) {
   if (p.mode == kXBf16) {
     const uint4 r = *reinterpret_cast<const uint4*>(p.xb + k0);
     const uint32_t u[4] = {r.x, r.y, r.z, r.w};
@@ -373,10 +386,29 @@ __device__ __forceinline__ void load_raw8(const GemvParams& p, int k0, float v[8
     const int head = kh / p.hd, e = kh % p.hd;
     kx = p.n_q * p.hd + p.n_kv * p.hd + (head / hpk) * p.hd + e;
   }
-  const float4 x0 = *reinterpret_cast<const float4*>(p.x + kx);
-  const float4 x1 = *reinterpret_cast<const float4*>(p.x + kx + 4);
-  v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
-  v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+  if (p.sum_in) {
+    // rank order, like the exchange kernel's all-reduce: the same bits on every rank
+    for (int r = 0; r < p.G; ++r) {
+      const unsigned long long* src = p.sum_in + (size_t)r * p.K + k0;
+      unsigned long long w[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ld_relaxed_sys_v2_u64(src + 2 * i, w[2 * i], w[2 * i + 1]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float f = __uint_as_float((unsigned)wait_tagged(src + i, w[i], tag, ok, p.err));
+        v[i] = r == 0 ? f : v[i] + f;
+      }
+    }
+    if (p.h_out && blockIdx.x == 0) {
+      *reinterpret_cast<float4*>(p.h_out + k0) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(p.h_out + k0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  } else {
+    const float4 x0 = *reinterpret_cast<const float4*>(p.x + kx);
+    const float4 x1 = *reinterpret_cast<const float4*>(p.x + kx + 4);
+    v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+    v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+  }
   const float* aux = p.mode == RRR_X_RMSNORM ? p.gamma + k0
                      : p.mode == RRR_X_SILU_GATE ? p.x + p.K + k0 : nullptr;
   if (aux) {
@@ -422,8 +454,8 @@ __device__ __forceinline__ uint32_t gather_byte(uint32_t a, uint32_t b, uint32_t
 constexpr int kPrepGroup = 2;
 
 template <bool FRAG>
-__device__ void prepare_x(const GemvParams& p, int8_t* dig, float* xscale, float* xsum,
-                          float* misc, int warp, int lane) {
+__device__ __forceinline__ void prepare_x(const GemvParams& p, int8_t* dig, float* xscale, float* xsum,
+                          float* misc, int warp, int lane, unsigned tag, bool& ok) {
   constexpr int NPW = kGroups * kNW;  // every consumer warp of the CTA takes part
   float ssq = 0.f;
   for (int bg = warp; bg < p.nb; bg += kPrepGroup * NPW) {
@@ -433,7 +465,7 @@ __device__ void prepare_x(const GemvParams& p, int8_t* dig, float* xscale, float
     const int ng = min(kPrepGroup, (p.nb - bg + NPW - 1) / NPW);
 #pragma unroll
     for (int g = 0; g < kPrepGroup; ++g)
-      if (g < ng) load_raw8(p, (bg + g * NPW) * 256 + lane * 8, vg[g], ag[g]);
+      if (g < ng) load_raw8(p, (bg + g * NPW) * 256 + lane * 8, vg[g], ag[g], tag, ok);
     float m[kPrepGroup], s8[kPrepGroup];
 #pragma unroll
     for (int g = 0; g < kPrepGroup; ++g) {
@@ -537,50 +569,284 @@ __device__ __forceinline__ int tile_rows(const GemvParams& p, int wt) {
   return min(kTileRows, lim - wt * kTileRows);
 }
 
+// ---------------------------------------------------------------- per-GEMV pipelines
+// A group's position in its ring.
+struct RingPos {
+  int s = 0;          // stage index
+  uint32_t ph = 0;    // phase parity of stage s
+  int issued = 0;     // producer: stages issued so far
+  int ts = 0, ss = 0; // consumers: row-tile and stage sequence numbers
+};
+
+// One producer / consumer group's shared memory (the ring and the tile reductions are the
+// group's; the x digits and sums are the CTA's).
+struct GroupSmem {
+  uint64_t* full;
+  uint64_t* empty;
+  uint8_t* ring;
+  int8_t* dig;
+  float* xscale;
+  float* xsum;
+  float* misc;
+  float* red;
+  float* gate;
+  int* cnt;
+  volatile int* abort_flag;
+  int nstages, stage_bytes;
+};
+
+__device__ __forceinline__ GroupSmem group_smem(uint8_t* smem, const GemvParams& p, int grp) {
+  GroupSmem g;
+  g.full = reinterpret_cast<uint64_t*>(smem + p.off_bars) + grp * 2 * p.nstages;
+  g.empty = g.full + p.nstages;
+  g.ring = smem + (size_t)grp * p.nstages * p.stage_bytes;
+  g.dig = reinterpret_cast<int8_t*>(smem + p.off_dig);
+  g.xscale = reinterpret_cast<float*>(smem + p.off_xscale);
+  g.xsum = reinterpret_cast<float*>(smem + p.off_xsum);
+  g.misc = reinterpret_cast<float*>(smem + p.off_misc + 16);
+  g.red = reinterpret_cast<float*>(smem + p.off_red) + grp * kSlots * kNW * kTileRows;
+  g.gate = reinterpret_cast<float*>(smem + p.off_gate) + grp * kSlots * kTileRows;
+  g.cnt = reinterpret_cast<int*>(smem + p.off_misc + 16 + kGroups * kNW * 4) + grp * kSlots;
+  g.abort_flag = reinterpret_cast<volatile int*>(smem + p.off_misc);
+  g.nstages = p.nstages;
+  g.stage_bytes = p.stage_bytes;
+  return g;
+}
+
+// Barrier initialisation of the CTA (thread 0): a full barrier (one arrival + bytes) and an
+// empty barrier (kNW consumer warps) per stage and group.
+__device__ __forceinline__ void init_cta_smem(uint8_t* smem, const GemvParams& p) {
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bars);
+  for (int g = 0; g < kGroups; ++g)
+    for (int s = 0; s < p.nstages; ++s) {
+      mbar_init(&bars[g * 2 * p.nstages + s], 1);
+      mbar_init(&bars[g * 2 * p.nstages + p.nstages + s], kNW);
+    }
+  *reinterpret_cast<volatile int*>(smem + p.off_misc) = 0;
+  int* cnt0 = reinterpret_cast<int*>(smem + p.off_misc + 16 + kGroups * kNW * 4);
+  for (int i = 0; i < kGroups * kSlots; ++i) cnt0[i] = 0;
+  fence_mbarrier_init();
+}
+
+// Producer warp: streams the group's row tiles of one GEMV (tiles vb, vb + vstride, ...)
+// into the ring, chunk by chunk, each row of a chunk as one 1-D bulk copy. Returns false
+// when the CTA aborted (a bounded wait ran out). limit_scale stretches its waits for free
+// stages (consumers that wait for other ranks' rows or other CTAs wait longer first).
+template <int QT>
+__device__ __forceinline__ bool produce_item(const GemvParams& p, const GroupSmem& g, int vb, int vstride, int lane,
+                             RingPos& rp, uint32_t limit_scale) {
+  constexpr int BB = KQ<QT>::kBlockBytes;
+  const int n_sub = p.out_mode ? 2 : 1;
+  const long long floor_total = p.total_bytes & ~15ll;
+  for (int wt = vb; wt < p.n_tiles; wt += vstride) {
+    const int rows = tile_rows(p, wt);
+    for (int j = 0; j < n_sub; ++j) {
+      const int row0 = tile_row0(p, wt, j);
+      for (int c = 0; c < p.n_chunks; ++c) {
+        if (rp.issued >= g.nstages) {
+          int w = 1;
+          if (lane == 0) {
+            w = mbar_wait_bounded(&g.empty[rp.s], rp.ph ^ 1u, p.err, kDevErrEmptyTimeout,
+                                  limit_scale) ? 1 : 0;
+            if (!w) *g.abort_flag = 1;
+          }
+          w = __shfl_sync(0xffffffffu, w, 0);
+          if (!w || *g.abort_flag) return false;
+        }
+        const int kb0 = c * p.kc;
+        const int kcount = min(p.kc, p.nb - kb0);
+        const long long chunk = (long long)kcount * BB;
+        uint8_t* stage = g.ring + (size_t)rp.s * g.stage_bytes;
+        long long a0 = 0, a1 = 0;
+        uint32_t tx = 0;
+        if (lane < rows) {
+          const long long start = (long long)(row0 + lane) * p.row_bytes + (long long)kb0 * BB;
+          const long long end = start + chunk;
+          a0 = start & ~15ll;
+          a1 = min((end + 15) & ~15ll, floor_total);
+          if (a1 < a0) a1 = a0;
+          tx = (uint32_t)(a1 - a0);
+          // bytes after the last whole 16-B granule of the buffer: plain loads
+          for (long long q = max(a1, start); q < end; ++q)
+            stage[lane * p.row_stride + (int)(q - a0)] = p.w[q];
+        }
+        uint32_t tot = tx;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&g.full[rp.s], tot);
+        __syncwarp();
+        if (tx > 0) bulk_g2s(stage + lane * p.row_stride, p.w + a0, tx, &g.full[rp.s]);
+        ++rp.issued;
+        if (++rp.s == g.nstages) {
+          rp.s = 0;
+          rp.ph ^= 1u;
+        }
+      }
+    }
+  }
+  return true;
+}
+
+// No copy may still be in flight when the CTA exits: the producer waits for the last
+// stages it issued (the earlier ones were consumed).
+__device__ __forceinline__ void drain_ring(const GroupSmem& g, const RingPos& rp, int lane, int* err) {
+  if (lane != 0) return;
+  const int first = rp.issued > g.nstages ? rp.issued - g.nstages : 0;
+  for (int i = first; i < rp.issued; ++i)
+    mbar_wait_bounded(&g.full[i % g.nstages], (uint32_t)(i / g.nstages) & 1u, err,
+                      kDevErrDrainTimeout);
+}
+
+// Consumer warps of a group: the row tiles of one GEMV from the ring (x digits prepared),
+// each tile's warp sums reduced by the last warp to finish it, which stores the rows (y,
+// + residual; silu(gate) * up; or the tagged push to every rank).
+template <int QT, bool FRAG>
+__device__ __forceinline__ void consume_item(const GemvParams& p, const GroupSmem& g, int vb, int vstride, int cw,
+                             int lane, float inv_rms, unsigned tag, bool feed, RingPos& rp) {
+  constexpr int BB = KQ<QT>::kBlockBytes;
+  const Lane L = make_lane(lane, QT == RRR_Q4_K);
+  const int n_sub = p.out_mode ? 2 : 1;
+  const float* xsum32 = g.xsum + p.K / 16;
+  // Byte offset mod 16 of a chunk start inside its 16-byte granule (only Q6_K rows and
+  // chunks can start unaligned); 32-bit arithmetic on the residues.
+  const int rb16 = (int)(p.row_bytes & 15), cb16 = (p.kc * BB) & 15;
+  for (int wt = vb; wt < p.n_tiles; wt += vstride) {
+    const int rows = tile_rows(p, wt);
+    for (int j = 0; j < n_sub; ++j, ++rp.ts) {
+      const int row0 = tile_row0(p, wt, j);
+      float acc0 = 0.f, acc1 = 0.f;
+      for (int c = 0; c < p.n_chunks; ++c) {
+        const int cs = rp.s;
+        const uint32_t cph = rp.ph;
+        if (++rp.s == g.nstages) {
+          rp.s = 0;
+          rp.ph ^= 1u;
+        }
+        bool have = (*g.abort_flag == 0);
+        if (have) {
+          have = mbar_wait_bounded(&g.full[cs], cph, p.err, kDevErrFullTimeout);
+          if (!have) *g.abort_flag = 1;
+        }
+        if (!have) continue;
+        const int kb0 = c * p.kc;
+        const int items = min(p.kc, p.nb - kb0);
+        const uint8_t* stage = g.ring + cs * g.stage_bytes;
+        int off0 = 0, off1 = 0;
+        if (QT == RRR_Q6_K) {
+          off0 = ((row0 + L.g) * rb16 + c * cb16) & 15;
+          off1 = ((row0 + L.g + 8) * rb16 + c * cb16) & 15;
+        }
+        const uint8_t* r0 = stage + L.g * p.row_stride + off0;
+        const uint8_t* r1 = stage + (L.g + 8) * p.row_stride + off1;
+        // Whole blocks are the work items; the warp that starts the list rotates from
+        // stage to stage so leftover blocks (12 per stage for K = 3072) spread over warps.
+        const int w0 = (cw + rp.ss * items) % kNW;
+        ++rp.ss;
+        for (int bi = w0; bi < items; bi += kNW) {
+          const uint8_t* q0 = r0 + bi * BB;
+          const uint8_t* q1 = r1 + bi * BB;
+          if constexpr (QT == RRR_Q6_K) {
+            const bool al = __all_sync(0xffffffffu, (((uintptr_t)q0 | (uintptr_t)q1) & 3) == 0);
+            const bool m2 = __all_sync(0xffffffffu, ((uintptr_t)q0 & 3) == 2 && ((uintptr_t)q1 & 3) == 2);
+            if (al)
+              block_q6<0>(q0, q1, kb0 + bi, g.dig, p.dig_stride, g.xscale, g.xsum, L, acc0, acc1);
+            else if (m2)
+              block_q6<2>(q0, q1, kb0 + bi, g.dig, p.dig_stride, g.xscale, g.xsum, L, acc0, acc1);
+            else
+              block_q6<1>(q0, q1, kb0 + bi, g.dig, p.dig_stride, g.xscale, g.xsum, L, acc0, acc1);
+          } else {
+            block_q45<QT, FRAG>(q0, q1, kb0 + bi, g.dig, p.dig_stride, g.xscale, xsum32, L, acc0, acc1);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&g.empty[cs]);
+      }
+      // Row sums of this warp (over the 4 lanes of a row), parked in slot ts % kSlots; the
+      // last warp to finish the tile (shared counter) adds the warps' sums in warp order
+      // and stores the rows: no CTA-wide barrier, warps run ahead into the next tile.
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+      const int slot = rp.ts % kSlots;
+      float* rb = g.red + slot * kNW * kTileRows;
+      if (L.tig == 0) {
+        rb[cw * kTileRows + L.g] = acc0;
+        rb[cw * kTileRows + L.g + 8] = acc1;
+      }
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        __threadfence_block();
+        last = atomicAdd(&g.cnt[slot], 1) == kNW - 1;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence_block();
+        if (lane < rows && *g.abort_flag == 0) {
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < kNW; ++w) v += rb[w * kTileRows + lane];
+          v *= inv_rms;
+          if (p.out_mode == 0) {
+            const int row = row0 + lane;
+            if (p.residual) v = p.residual[row] + v;
+            if (!p.push[0]) {
+              p.y[row] = v;
+            } else if (feed) {
+              const unsigned long long wv = ((unsigned long long)tag << 32) | __float_as_uint(v);
+#pragma unroll
+              for (int r = 0; r < kMaxTpRanks; ++r)
+                if (r < p.G) st_relaxed_sys_u64(p.push[r] + row, wv);
+            }
+          } else if (j == 0) {
+            g.gate[slot * kTileRows + lane] = v;
+          } else {
+            // gate of this work tile was finalised (by some warp) before every warp
+            // arrived here
+            const float gv = g.gate[((rp.ts - 1) % kSlots) * kTileRows + lane];
+            const float sg = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
+            p.y[wt * kTileRows + lane] = __fmul_rn(sg, v);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) g.cnt[slot] = 0;
+      }
+    }
+  }
+}
+
+// Consumers: the GEMV input of one GEMV (digits, scales, sums; the ranks' rows summed under
+// GemvFuse), then the row scale of its RMSNorm. All consumer warps of the CTA take part.
+template <bool FRAG>
+__device__ __forceinline__ float prepare_item(const GemvParams& p, const GroupSmem& g, int warp,
+                                              int lane, unsigned tag) {
+  bool xok = true;
+  prepare_x<FRAG>(p, g.dig, g.xscale, g.xsum, g.misc, warp, lane, tag, xok);
+  named_barrier(1, kGroups * kNW * 32);
+  return row_scale(p, g.misc);
+}
+
 // ---------------------------------------------------------------- the kernel
 template <int QT, bool FRAG>
 __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_kq_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  constexpr int BB = KQ<QT>::kBlockBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // warps [0, kGroups*kNW): consumers of group warp / kNW; then one producer per group
   const bool producer = warp >= kGroups * kNW;
   const int grp = producer ? warp - kGroups * kNW : warp / kNW;
-  const int cw = warp % kNW;  // consumer warp index within its group
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars) + grp * 2 * p.nstages;
-  uint64_t* empty = full + p.nstages;
-  uint8_t* ring = smem + (size_t)grp * p.nstages * p.stage_bytes;
-  int8_t* dig = reinterpret_cast<int8_t*>(smem + p.off_dig);
-  float* xscale = reinterpret_cast<float*>(smem + p.off_xscale);
-  float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);
-  float* xsum32 = xsum + p.K / 16;
-  float* red = reinterpret_cast<float*>(smem + p.off_red) + grp * kSlots * kNW * kTileRows;
-  float* gate = reinterpret_cast<float*>(smem + p.off_gate) + grp * kSlots * kTileRows;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.off_misc);
-  float* misc = reinterpret_cast<float*>(smem + p.off_misc + 16);
-  int* cnt = reinterpret_cast<int*>(smem + p.off_misc + 16 + kGroups * kNW * 4) + grp * kSlots;
-  const int n_sub = p.out_mode ? 2 : 1;  // row tiles per work tile
+  const GroupSmem g = group_smem(smem, p, grp);
   // this group's tiles: vb, vb + vstride, ...: group 0 of every CTA first, so that with
   // fewer tiles than groups every SM still gets work
   const int vb = grp * gridDim.x + blockIdx.x, vstride = gridDim.x * kGroups;
 
-  if (threadIdx.x == 0) {
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bars);
-    for (int g = 0; g < kGroups; ++g)
-      for (int s = 0; s < p.nstages; ++s) {
-        mbar_init(&bars[g * 2 * p.nstages + s], 1);
-        mbar_init(&bars[g * 2 * p.nstages + p.nstages + s], kNW);
-      }
-    *abort_flag = 0;
-    int* cnt0 = reinterpret_cast<int*>(smem + p.off_misc + 16 + kGroups * kNW * 4);
-    for (int i = 0; i < kGroups * kSlots; ++i) cnt0[i] = 0;
-    fence_mbarrier_init();
-  }
+  if (threadIdx.x == 0) init_cta_smem(smem, p);
   __syncthreads();
   pdl_launch_dependents();
 
+  RingPos rp;
   if (producer) {
-    // ------------------------------------------------------------ producer warp
     // First the GEMV input (and gamma) into L2, ahead of this CTA's weight stream: the
     // consumers read it after the preceding grid has finished, by which time the weight
     // copies of every CTA fill the memory queues.
@@ -591,181 +857,26 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_kq_kernel(const GemvP
       const void* xs = p.mode == kXBf16 ? (const void*)p.xb
                        : p.mode == RRR_X_GQA_V ? (const void*)(p.x + (p.n_q + p.n_kv) * p.hd)
                        : (const void*)p.x;
-      for (uint32_t o = 0; o < xb; o += 16384) bulk_prefetch_l2((const char*)xs + o, min(16384u, xb - o));
+      if (!p.sum_in)  // (the ranks' rows arrive while this kernel waits for them)
+        for (uint32_t o = 0; o < xb; o += 16384) bulk_prefetch_l2((const char*)xs + o, min(16384u, xb - o));
       if (p.mode == RRR_X_RMSNORM)
         for (uint32_t o = 0; o < (uint32_t)p.K * 4; o += 16384)
           bulk_prefetch_l2((const char*)p.gamma + o, min(16384u, (uint32_t)p.K * 4 - o));
     }
-    const long long floor_total = p.total_bytes & ~15ll;
-    int issued = 0, s = 0;
-    uint32_t ph = 0;
-    bool ok = true;
-    for (int wt = vb; wt < p.n_tiles && ok; wt += vstride) {
-      const int rows = tile_rows(p, wt);
-      for (int j = 0; j < n_sub && ok; ++j) {
-        const int row0 = tile_row0(p, wt, j);
-        for (int c = 0; c < p.n_chunks; ++c) {
-          if (issued >= p.nstages) {
-            int w = 1;
-            if (lane == 0) {
-              w = mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, kDevErrEmptyTimeout) ? 1 : 0;
-              if (!w) *abort_flag = 1;
-            }
-            w = __shfl_sync(0xffffffffu, w, 0);
-            if (!w || *abort_flag) { ok = false; break; }
-          }
-          const int kb0 = c * p.kc;
-          const int kcount = min(p.kc, p.nb - kb0);
-          const long long chunk = (long long)kcount * BB;
-          uint8_t* stage = ring + (size_t)s * p.stage_bytes;
-          long long a0 = 0, a1 = 0;
-          uint32_t tx = 0;
-          if (lane < rows) {
-            const long long start = (long long)(row0 + lane) * p.row_bytes + (long long)kb0 * BB;
-            const long long end = start + chunk;
-            a0 = start & ~15ll;
-            a1 = min((end + 15) & ~15ll, floor_total);
-            if (a1 < a0) a1 = a0;
-            tx = (uint32_t)(a1 - a0);
-            // bytes after the last whole 16-B granule of the buffer: plain loads
-            for (long long q = max(a1, start); q < end; ++q)
-              stage[lane * p.row_stride + (int)(q - a0)] = p.w[q];
-          }
-          uint32_t tot = tx;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-          __syncwarp();
-          if (lane == 0) mbar_arrive_expect_tx(&full[s], tot);
-          __syncwarp();
-          if (tx > 0) bulk_g2s(stage + lane * p.row_stride, p.w + a0, tx, &full[s]);
-          ++issued;
-          if (++s == p.nstages) {
-            s = 0;
-            ph ^= 1u;
-          }
-        }
-      }
-    }
-    // No copy may still be in flight when the CTA exits.
-    if (lane == 0) {
-      const int first = issued > p.nstages ? issued - p.nstages : 0;
-      for (int i = first; i < issued; ++i)
-        mbar_wait_bounded(&full[i % p.nstages], (uint32_t)(i / p.nstages) & 1u, p.err,
-                          kDevErrDrainTimeout);
-    }  // (runs once per CTA)
+    // (consumers that wait for the ranks' rows first get twice the limit, so that a
+    // missing rank is reported as such)
+    produce_item<QT>(p, g, vb, vstride, lane, rp, p.sum_in ? 2u : 1u);
+    drain_ring(g, rp, lane, p.err);
     return;
   }
 
-  // -------------------------------------------------------------- consumer warps
   pdl_wait();
-  prepare_x<FRAG>(p, dig, xscale, xsum, misc, warp, lane);
-  named_barrier(1, kGroups * kNW * 32);
-  const float inv_rms = row_scale(p, misc);
-
-  const Lane L = make_lane(lane, QT == RRR_Q4_K);
-
-  // Byte offset mod 16 of a chunk start inside its 16-byte granule (only Q6_K rows and
-  // chunks can start unaligned); 32-bit arithmetic on the residues.
-  const int rb16 = (int)(p.row_bytes & 15), cb16 = (p.kc * BB) & 15;
-  int s = 0, ts = 0, ss = 0;  // stage index, row-tile sequence, stage sequence
-  uint32_t ph = 0;    // phase parity of stage s
-  for (int wt = vb; wt < p.n_tiles; wt += vstride) {
-    const int rows = tile_rows(p, wt);
-    for (int j = 0; j < n_sub; ++j, ++ts) {
-      const int row0 = tile_row0(p, wt, j);
-      float acc0 = 0.f, acc1 = 0.f;
-      for (int c = 0; c < p.n_chunks; ++c) {
-        const int cs = s;
-        const uint32_t cph = ph;
-        if (++s == p.nstages) {
-          s = 0;
-          ph ^= 1u;
-        }
-        bool have = (*abort_flag == 0);
-        if (have) {
-          have = mbar_wait_bounded(&full[cs], cph, p.err, kDevErrFullTimeout);
-          if (!have) *abort_flag = 1;
-        }
-        if (!have) continue;
-        const int kb0 = c * p.kc;
-        const int items = min(p.kc, p.nb - kb0);
-        const uint8_t* stage = ring + cs * p.stage_bytes;
-        int off0 = 0, off1 = 0;
-        if (QT == RRR_Q6_K) {
-          off0 = ((row0 + L.g) * rb16 + c * cb16) & 15;
-          off1 = ((row0 + L.g + 8) * rb16 + c * cb16) & 15;
-        }
-        const uint8_t* r0 = stage + L.g * p.row_stride + off0;
-        const uint8_t* r1 = stage + (L.g + 8) * p.row_stride + off1;
-        // Whole blocks are the work items; the warp that starts the list rotates from
-        // stage to stage so leftover blocks (12 per stage for K = 3072) spread over warps.
-        const int w0 = (cw + ss * items) % kNW;
-        ++ss;
-        for (int bi = w0; bi < items; bi += kNW) {
-          const uint8_t* q0 = r0 + bi * BB;
-          const uint8_t* q1 = r1 + bi * BB;
-          if constexpr (QT == RRR_Q6_K) {
-            const bool al = __all_sync(0xffffffffu, (((uintptr_t)q0 | (uintptr_t)q1) & 3) == 0);
-            const bool m2 = __all_sync(0xffffffffu, ((uintptr_t)q0 & 3) == 2 && ((uintptr_t)q1 & 3) == 2);
-            if (al)
-              block_q6<0>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
-            else if (m2)
-              block_q6<2>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
-            else
-              block_q6<1>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum, L, acc0, acc1);
-          } else {
-            block_q45<QT, FRAG>(q0, q1, kb0 + bi, dig, p.dig_stride, xscale, xsum32, L, acc0, acc1);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[cs]);
-      }
-      // Row sums of this warp (over the 4 lanes of a row), parked in slot ts % kSlots; the
-      // last warp to finish the tile (shared counter) adds the warps' sums in warp order
-      // and stores the rows: no CTA-wide barrier, warps run ahead into the next tile.
-      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-      const int slot = ts % kSlots;
-      float* rb = red + slot * kNW * kTileRows;
-      if (L.tig == 0) {
-        rb[cw * kTileRows + L.g] = acc0;
-        rb[cw * kTileRows + L.g + 8] = acc1;
-      }
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) {
-        __threadfence_block();
-        last = atomicAdd(&cnt[slot], 1) == kNW - 1;
-      }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        __threadfence_block();
-        if (lane < rows && *abort_flag == 0) {
-          float v = 0.f;
-#pragma unroll
-          for (int w = 0; w < kNW; ++w) v += rb[w * kTileRows + lane];
-          v *= inv_rms;
-          if (p.out_mode == 0) {
-            const int row = row0 + lane;
-            if (p.residual) v = p.residual[row] + v;
-            p.y[row] = v;
-          } else if (j == 0) {
-            gate[slot * kTileRows + lane] = v;
-          } else {
-            // gate of this work tile was finalised (by some warp) before every warp
-            // arrived here
-            const float g = gate[((ts - 1) % kSlots) * kTileRows + lane];
-            const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-            p.y[wt * kTileRows + lane] = __fmul_rn(sg, v);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) cnt[slot] = 0;
-      }
-    }
-  }
+  // fused exchange: this step's epoch, and whether this rank still feeds its peers (no
+  // error recorded by an earlier kernel, e.g. a wait that ran out)
+  const unsigned tag = p.G ? *p.epoch + 1u : 0u;
+  const bool feed = p.push[0] && *reinterpret_cast<volatile int*>(p.err) == 0;
+  const float inv_rms = prepare_item<FRAG>(p, g, warp, lane, tag);
+  consume_item<QT, FRAG>(p, g, vb, vstride, warp % kNW, lane, inv_rms, tag, feed, rp);
 }
 
 // Shared-memory layout of one launch. FRAG: the x digits are stored as ready-made per-lane
@@ -878,6 +989,32 @@ cudaError_t launch_any(const LaunchEnv& env, int qtype, GemvParams& p) {
   }
 }
 
+// ---------------------------------------------------------------- launch parameters (host)
+// The kernel parameters of one GEMV from its description (shapes and layout follow).
+void fill_params(GemvParams& p, const GemvDesc& d) {
+  p.w = static_cast<const uint8_t*>(d.w);
+  p.x = d.x;
+  p.y = d.y;
+  p.residual = d.swiglu ? nullptr : d.residual;
+  p.out_mode = d.swiglu ? 1 : 0;
+  p.mode = d.pro.mode;
+  p.gamma = d.pro.gamma;
+  p.eps = d.pro.eps;
+  p.n_q = d.pro.n_q_heads;
+  p.n_kv = d.pro.n_kv_heads;
+  p.hd = d.pro.head_dim;
+  p.k_off = d.pro.mode == RRR_X_GQA_V ? d.pro.k_offset : 0;
+  p.K = d.K;
+  p.N = d.swiglu ? 2 * d.N : d.N;
+  if (d.fuse.G >= 1) {
+    p.sum_in = d.fuse.sum_in;
+    p.h_out = d.fuse.h_out;
+    for (int r = 0; r < kMaxTpRanks; ++r) p.push[r] = r < d.fuse.G ? d.fuse.push[r] : nullptr;
+    p.G = d.fuse.G;
+    p.epoch = d.fuse.epoch;
+  }
+}
+
 // ---------------------------------------------------------------- layout self-test
 // m16n8k32 u8 x s8 -> s32 through mma_u8s8 with A[r][k] = (r*7 + k*3) & 0xFF,
 // B[k][n] = ((k*5 + n*11) & 0xFF) - 128, against the expected products.
@@ -911,41 +1048,37 @@ __global__ void mma_selftest_kernel(int* ok) {
 
 cudaError_t launch_gemv_kq(const LaunchEnv& env, int qtype, const void* w, const float* x,
                            float* y, int K, int N, const float* residual,
-                           const rrr_gemv_prologue* pro) {
+                           const rrr_gemv_prologue* pro, const GemvFuse* fuse) {
+  GemvDesc d;
+  d.qtype = qtype;
+  d.w = w;
+  d.x = x;
+  d.y = y;
+  d.K = K;
+  d.N = N;
+  d.residual = residual;
+  if (pro) d.pro = *pro;
+  if (fuse) d.fuse = *fuse;
   GemvParams p = {};
-  p.w = static_cast<const uint8_t*>(w);
-  p.x = x;
-  p.y = y;
-  p.residual = residual;
-  p.mode = pro ? pro->mode : RRR_X_PLAIN;
-  p.gamma = pro ? pro->gamma : nullptr;
-  p.eps = pro ? pro->eps : 0.f;
-  p.n_q = pro ? pro->n_q_heads : 0;
-  p.n_kv = pro ? pro->n_kv_heads : 0;
-  p.hd = pro ? pro->head_dim : 0;
-  p.k_off = pro && pro->mode == RRR_X_GQA_V ? pro->k_offset : 0;
-  p.K = K;
-  p.N = N;
+  fill_params(p, d);
   return launch_any(env, qtype, p);
 }
 
 cudaError_t launch_gemv_kq_swiglu(const LaunchEnv& env, int qtype, const void* w,
                                   const float* x, float* y, int K, int F,
-                                  const rrr_gemv_prologue* pro) {
+                                  const rrr_gemv_prologue* pro, const GemvFuse* fuse) {
+  GemvDesc d;
+  d.qtype = qtype;
+  d.w = w;
+  d.x = x;
+  d.y = y;
+  d.K = K;
+  d.N = F;
+  d.swiglu = true;
+  if (pro) d.pro = *pro;
+  if (fuse) d.fuse = *fuse;
   GemvParams p = {};
-  p.w = static_cast<const uint8_t*>(w);
-  p.x = x;
-  p.y = y;
-  p.out_mode = 1;
-  p.mode = pro ? pro->mode : RRR_X_PLAIN;
-  p.gamma = pro ? pro->gamma : nullptr;
-  p.eps = pro ? pro->eps : 0.f;
-  p.n_q = pro ? pro->n_q_heads : 0;
-  p.n_kv = pro ? pro->n_kv_heads : 0;
-  p.hd = pro ? pro->head_dim : 0;
-  p.k_off = pro && pro->mode == RRR_X_GQA_V ? pro->k_offset : 0;
-  p.K = K;
-  p.N = 2 * F;
+  fill_params(p, d);
   return launch_any(env, qtype, p);
 }
 

@@ -22,10 +22,42 @@ struct LaunchEnv {
 
 // Shape limits of the K-quant GEMV (checked by the C ABI before launching).
 constexpr int kGemvMaxK = 16384;
+constexpr int kMaxTpRanks = 8;
+
+// The tensor-parallel exchange of a decode step fused into its GEMVs (peer-memory channel
+// with a fused region, ranks on distinct GPUs). Every exchange site has, in every rank's
+// region, one slot of K tagged words (value low, step epoch high) per source rank.
+//  * sum_in (prologue, RMSNORM mode): the GEMV input is the sum, in rank order, of the G
+//    slots sum_in[r*K ...] once they carry the step's epoch; CTA 0 also stores it to h_out.
+//  * push (epilogue, plain output): each finished row, tagged, goes to push[r][row] for
+//    r < G (this rank's slot of the site in every rank's region) instead of y; a rank whose
+//    device error flag is set pushes nothing, so its peers' waits run out too.
+// The step's epoch is *epoch + 1 (read after the preceding kernels have completed).
+struct GemvFuse {
+  const unsigned long long* sum_in = nullptr;
+  float* h_out = nullptr;
+  unsigned long long* push[kMaxTpRanks] = {};
+  int G = 0;
+  const unsigned* epoch = nullptr;
+};
 
 cudaError_t launch_gemv_kq(const LaunchEnv& env, int qtype, const void* w, const float* x,
                            float* y, int K, int N, const float* residual,
-                           const rrr_gemv_prologue* pro);
+                           const rrr_gemv_prologue* pro, const GemvFuse* fuse = nullptr);
+
+// One GEMV: the arguments of launch_gemv_kq (swiglu: of launch_gemv_kq_swiglu, N = F output
+// rows of a 2F-row weight).
+struct GemvDesc {
+  int qtype = 0;
+  const void* w = nullptr;
+  const float* x = nullptr;
+  float* y = nullptr;
+  int K = 0, N = 0;
+  const float* residual = nullptr;
+  rrr_gemv_prologue pro{};  // mode RRR_X_PLAIN
+  bool swiglu = false;
+  GemvFuse fuse;            // G = 0: no fused exchange
+};
 // GEMV with a bf16 input vector (one token of the batched path when M < 16).
 cudaError_t launch_gemv_kq_bf16(const LaunchEnv& env, int qtype, const void* w,
                                 const uint16_t* x, float* y, int K, int N,
@@ -49,7 +81,7 @@ cudaError_t launch_argmax_rows(const LaunchEnv& env, const float* x, int n, long
 // gate_up GEMV with the SwiGLU epilogue: W has 2F rows [gate; up], y[i] = silu(gate_i) * up_i.
 cudaError_t launch_gemv_kq_swiglu(const LaunchEnv& env, int qtype, const void* w,
                                   const float* x, float* y, int K, int F,
-                                  const rrr_gemv_prologue* pro);
+                                  const rrr_gemv_prologue* pro, const GemvFuse* fuse = nullptr);
 cudaError_t launch_matmul_f32(const LaunchEnv& env, const float* A, const float* B, float* C,
                               int M, int K, int N);
 cudaError_t launch_fill_kquant(const LaunchEnv& env, int qtype, void* dst, int64_t rows,
@@ -126,7 +158,6 @@ cudaError_t launch_embed_rows(const LaunchEnv& env, int type, const void* table,
 // (G <= 8) summed in rank order into every bufs[r]; parts[r] [rows][npr] gathered into
 // every outs[r] [rows][G * npr]; and the NCCL row all-gather's reorder, tmp [G][rows][npr]
 // -> out [rows][G * npr].
-constexpr int kMaxTpRanks = 8;
 cudaError_t launch_local_allreduce(const LaunchEnv& env, float* const* bufs, int G, int64_t n);
 cudaError_t launch_local_allgather_rows(const LaunchEnv& env, const float* const* parts,
                                         float* const* outs, int G, int rows, int64_t npr);
@@ -134,5 +165,11 @@ cudaError_t launch_rows_from_ranks(const LaunchEnv& env, const float* tmp, float
                                    int rows, int64_t npr);
 // *d_pos += delta after the preceding kernels of the stream have completed.
 cudaError_t launch_pos_advance(const LaunchEnv& env, int* d_pos, int delta);
+// The end of a step's fused exchanges (tp_exchange.cu): out[i] = sum over ranks, in rank
+// order, of slots[r*n + i] once they carry the epoch *epoch + 1 (bounded waits), then
+// *epoch += 1 by a second launch once every reader of this step's epoch has completed.
+cudaError_t launch_fused_sum(const LaunchEnv& env, const unsigned long long* slots, float* out,
+                             int n, int G, const unsigned* epoch);
+cudaError_t launch_epoch_advance(const LaunchEnv& env, unsigned* epoch);
 
 }  // namespace rrr

@@ -14,6 +14,15 @@
 // kernel), O-proj (residual epilogue), gate_up (SwiGLU), down (residual); the position
 // lives on the device and a one-thread kernel advances it at the end of the step, so one
 // captured graph serves every position.
+//
+// A tensor-parallel rank (rrr_phi4_tp_create) all-reduces the hidden state after each
+// O-projection and down and all-gathers the logits. On a peer-memory channel with a fused
+// region (rrr_comm_create_ex, ranks on distinct GPUs) the one-token step fuses the
+// all-reduces into the GEMVs instead (GemvFuse): O-projection / down push their partial rows,
+// tagged with the step's epoch, to every rank, and the next RMSNorm GEMV (gate_up, the next
+// layer's QKV) sums the ranks' rows in rank order in its prologue. Exchange site s = 2l
+// (O-projection of layer l) or 2l+1 (down); each rank's region holds [site][rank][d_model]
+// words. The last site is summed by one small kernel, which is followed by the epoch advance.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -33,6 +42,9 @@ struct rrr_phi4 {
   rrr_tp_shard sh{};
   rrr_tp_comm* comm = nullptr;
   int q_loc = 0, kv_loc = 0, f_loc = 0, v_loc = 0;
+  bool fused = false;                            // all-reduces fused into the GEMVs
+  unsigned long long* fz_base[kMaxTpRanks] = {};  // each rank's fused region, mapped here
+  unsigned* fz_epoch = nullptr;                   // the step epoch (the channel's, on this GPU)
   float* qkv = nullptr;      // f32[qkv_dim of the shard]
   float* mid = nullptr;      // f32[ffn of the shard]: silu(gate) * up
   float* logits_loc = nullptr;  // f32[vocab rows of the shard] (G > 1)
@@ -76,6 +88,42 @@ struct rrr_phi4 {
 // in lockstep with local exchanges in between.
 static int phi4_segments(const rrr_phi4* m) { return 2 * m->d.n_layers + 2; }
 
+// The fused exchange that a GEMV of the one-token step takes part in: the sum of site
+// `site`'s rows in its prologue (the sum also stored to h_out), or the push of its rows to
+// site `site`.
+static GemvFuse phi4_fuse_sum(const rrr_phi4* m, int site, float* h_out) {
+  GemvFuse f;
+  f.G = m->sh.G;
+  f.epoch = m->fz_epoch;
+  f.sum_in = m->fz_base[m->sh.g] + (size_t)site * m->sh.G * m->d.d_model;
+  f.h_out = h_out;
+  return f;
+}
+static GemvFuse phi4_fuse_push(const rrr_phi4* m, int site) {
+  GemvFuse f;
+  f.G = m->sh.G;
+  f.epoch = m->fz_epoch;
+  for (int r = 0; r < m->sh.G; ++r)
+    f.push[r] = m->fz_base[r] + ((size_t)site * m->sh.G + m->sh.g) * m->d.d_model;
+  return f;
+}
+
+// One GEMV of the one-token step (SwiGLU epilogue when `swiglu`, N = F), checked like the
+// C ABI's rrr_gemv_kq_ex / rrr_gemv_kq_swiglu, with the fused exchange `fz` when it is not
+// null.
+static int phi4_gemv(rrr_phi4* m, int qtype, const void* w, const float* x, float* y, int K, int N,
+                     const float* residual, const rrr_gemv_prologue* pro, bool swiglu,
+                     const GemvFuse* fz, void* stream) {
+  rrr_ctx* ctx = m->ctx;
+  int rc = check_gemv(ctx, qtype, w, x, y, K, N, residual, pro, swiglu);
+  if (rc) return rc;
+  const LaunchEnv env = make_env(ctx, stream);
+  cudaError_t e = swiglu ? launch_gemv_kq_swiglu(env, qtype, w, x, y, K, N, pro, fz)
+                         : launch_gemv_kq(env, qtype, w, x, y, K, N, residual, pro, fz);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? RRR_OK : cuda_error(ctx, e, "rrr_phi4_forward: GEMV launch");
+}
+
 // Segment `seg` of the one-token step (forward_gpu, phi4.rs:1099-1196).
 static int phi4_issue_seg(rrr_phi4* m, int seg, float* hidden, float* logits, int* argmax,
                           void* stream) {
@@ -84,14 +132,23 @@ static int phi4_issue_seg(rrr_phi4* m, int seg, float* hidden, float* logits, in
   rrr_ctx* ctx = m->ctx;
   const int L = d.n_layers;
   float* res = sh.g == 0 ? hidden : nullptr;  // the residual enters the sum once
+  const bool fz = m->fused;
   int rc;
   if (seg < 2 * L) {
     const rrr_phi4_layer& Ly = m->layers[seg / 2];
     const int l = seg / 2;
+    // fused exchanges: this segment's GEMVs sum site seg - 1 and push site seg
+    GemvFuse fin, fout;
+    if (fz) {
+      if (seg > 0) fin = phi4_fuse_sum(m, seg - 1, hidden);
+      fout = phi4_fuse_push(m, seg);
+    }
+    const GemvFuse* pin = fz && seg > 0 ? &fin : nullptr;
+    const GemvFuse* pout = fz ? &fout : nullptr;
     if ((seg & 1) == 0) {
       rrr_gemv_prologue pn{RRR_X_RMSNORM, Ly.attn_norm, d.rms_eps, 0, 0, 0, 0};
-      if ((rc = rrr_gemv_kq_ex(ctx, Ly.qkv_type, Ly.w_qkv, hidden, m->qkv, d.d_model, sh.qkv_dim,
-                               nullptr, &pn, stream)))
+      if ((rc = phi4_gemv(m, Ly.qkv_type, Ly.w_qkv, hidden, m->qkv, d.d_model, sh.qkv_dim,
+                          nullptr, &pn, false, pin, stream)))
         return rc;
       if (d.max_seq > 0) {
         const size_t cache = (size_t)d.max_seq * m->kv_loc * d.head_dim;
@@ -99,23 +156,32 @@ static int phi4_issue_seg(rrr_phi4* m, int seg, float* hidden, float* logits, in
         uint16_t* vc = kc + cache;
         if ((rc = rrr_rope_attention_f16kv(ctx, &m->attn_desc, m->qkv, 0, m->d_pos, kc, vc,
                                            m->attn + sh.o_k_offset, stream)) ||
-            (rc = rrr_gemv_kq_ex(ctx, Ly.o_type, Ly.w_o, m->attn, hidden, sh.o_k, d.d_model, res,
-                                 nullptr, stream)))
+            (rc = phi4_gemv(m, Ly.o_type, Ly.w_o, m->attn, hidden, sh.o_k, d.d_model, res,
+                            nullptr, false, pout, stream)))
           return rc;
       } else {
         rrr_gemv_prologue pv{RRR_X_GQA_V, nullptr, 0.f, m->q_loc, m->kv_loc, d.head_dim, sh.o_k_offset};
-        if ((rc = rrr_gemv_kq_ex(ctx, Ly.o_type, Ly.w_o, m->qkv, hidden, sh.o_k, d.d_model, res, &pv,
-                                 stream)))
+        if ((rc = phi4_gemv(m, Ly.o_type, Ly.w_o, m->qkv, hidden, sh.o_k, d.d_model, res, &pv,
+                            false, pout, stream)))
           return rc;
       }
       return RRR_OK;
     }
     rrr_gemv_prologue pf{RRR_X_RMSNORM, Ly.ffn_norm, d.rms_eps, 0, 0, 0, 0};
-    if ((rc = rrr_gemv_kq_swiglu(ctx, Ly.gate_up_type, Ly.w_gate_up, hidden, m->mid, d.d_model,
-                                 m->f_loc, &pf, stream)))
+    if ((rc = phi4_gemv(m, Ly.gate_up_type, Ly.w_gate_up, hidden, m->mid, d.d_model, m->f_loc,
+                        nullptr, &pf, true, pin, stream)) ||
+        (rc = phi4_gemv(m, Ly.down_type, Ly.w_down, m->mid, hidden, m->f_loc, d.d_model, res,
+                        nullptr, false, pout, stream)))
       return rc;
-    return rrr_gemv_kq_ex(ctx, Ly.down_type, Ly.w_down, m->mid, hidden, m->f_loc, d.d_model, res,
-                          nullptr, stream);
+    if (fz && l == L - 1) {
+      // the last site's sum is the final hidden state; then the next step's epoch
+      const LaunchEnv env = make_env(ctx, stream);
+      cudaError_t e = launch_fused_sum(env, phi4_fuse_sum(m, seg, nullptr).sum_in, hidden, d.d_model,
+                                       sh.G, m->fz_epoch);
+      if (e == cudaSuccess) e = launch_epoch_advance(env, m->fz_epoch);
+      if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_phi4_forward: fused exchange launch");
+    }
+    return RRR_OK;
   }
   if (seg == 2 * L)
     return rrr_logits_f32(ctx, d.w_out, hidden, sh.G > 1 ? m->logits_loc : logits, m->v_loc,
@@ -208,10 +274,13 @@ static int phi4_exchange(rrr_phi4* m, int seg, float* hidden, float* logits, int
 
 static int phi4_issue(rrr_phi4* m, float* hidden, float* logits, int* argmax, void* stream) {
   int rc;
-  for (int seg = 0; seg < phi4_segments(m); ++seg)
-    if ((rc = phi4_issue_seg(m, seg, hidden, logits, argmax, stream)) ||
+  for (int seg = 0; seg < phi4_segments(m); ++seg) {
+    if ((rc = phi4_issue_seg(m, seg, hidden, logits, argmax, stream))) return rc;
+    // (the layers' all-reduces are inside the GEMVs when fused)
+    if ((!m->fused || seg >= 2 * m->d.n_layers) &&
         (rc = phi4_exchange(m, seg, hidden, logits, 1, stream)))
       return rc;
+  }
   return RRR_OK;
 }
 
@@ -353,6 +422,25 @@ static int phi4_make(rrr_ctx* ctx, const rrr_phi4_desc* desc, const rrr_tp_shard
   m->kv_loc = kv_loc;
   m->f_loc = sh.ffn1 - sh.ffn0;
   m->v_loc = sh.vocab1 - sh.vocab0;
+  if (comm && sh.G > 1 && d.n_layers > 0) {
+    rrr_comm* pc = tp_comm_p2p_of(comm);
+    unsigned long long* bases[kMaxTpRanks] = {};
+    unsigned* epoch = nullptr;
+    const int64_t words = pc ? comm_fused(pc, bases, &epoch) : 0;
+    const int64_t need = 2ll * d.n_layers * sh.G * d.d_model;
+    if (words > 0 && words < need) {
+      delete m;
+      return set_error(ctx, RRR_ERR_BAD_SHAPE,
+                       "rrr_phi4_tp_create: the channel's fused region holds %lld words, the step "
+                       "needs 2 * n_layers * world * d_model = %lld",
+                       (long long)words, (long long)need);
+    }
+    if (words > 0) {
+      m->fused = true;
+      for (int r = 0; r < sh.G; ++r) m->fz_base[r] = bases[r];
+      m->fz_epoch = epoch;
+    }
+  }
   cudaError_t e = cudaMalloc(&m->qkv, (size_t)sh.qkv_dim * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&m->mid, (size_t)m->f_loc * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&m->argmax_scratch, 64);
@@ -569,10 +657,18 @@ int rrr_phi4_tp_forward_emulated(rrr_phi4* const* ranks, int G, float* const* hi
 int rrr_phi4_launches_per_step(rrr_phi4* m, int* n) {
   if (!m || !n) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null argument");
   const int chunk = m->d.logits_chunk_rows > 0 ? m->d.logits_chunk_rows : m->v_loc;
-  *n = (m->d.max_seq > 0 ? 5 : 4) * m->d.n_layers + (m->v_loc + chunk - 1) / chunk +
-       (m->d.max_seq > 0 ? 1 : 0);
-  // the peer-memory exchanges are kernels of this library (NCCL's are not counted)
-  if (m->sh.G > 1 && m->comm && tp_comm_is_p2p(m->comm)) *n += 2 * m->d.n_layers + 1;
+  const int L = m->d.n_layers;
+  *n = (m->d.max_seq > 0 ? 5 : 4) * L + (m->v_loc + chunk - 1) / chunk + (m->d.max_seq > 0 ? 1 : 0);
+  // the peer-memory exchanges are kernels of this library (NCCL's are not counted); fused:
+  // the last site's sum, the epoch advance and the logits all-gather
+  if (m->sh.G > 1 && m->comm && tp_comm_is_p2p(m->comm))
+    *n += m->fused ? 3 : 2 * L + 1;
+  return RRR_OK;
+}
+
+int rrr_phi4_tp_fused(rrr_phi4* m, int* fused) {
+  if (!m || !fused) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null argument");
+  *fused = m->fused ? 1 : 0;
   return RRR_OK;
 }
 

@@ -17,6 +17,7 @@ enum DeviceErr : int {
   kDevErrFullTimeout = 1,   // a consumer gave up waiting for a bulk copy
   kDevErrEmptyTimeout = 2,  // the producer gave up waiting for consumers to free a stage
   kDevErrDrainTimeout = 3,  // copies still in flight at exit did not complete in time
+  kDevErrCommTimeout = 5,   // an exchange gave up waiting for a peer rank's data
   kDevErrPosition = 6,      // a position outside the cache, or a token id outside the table
 };
 
@@ -34,6 +35,44 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// Tagged exchange words between ranks (peer memory over NVLink): value bits low, epoch of the
+// step or call that stored them high. A naturally aligned 64-bit access is single-copy
+// atomic, so a reader that sees the epoch sees the value stored with it: no fences, no
+// separate flags. A vector access is a set of such 64-bit accesses.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void ld_relaxed_sys_v2_u64(const unsigned long long* p,
+                                                      unsigned long long& a,
+                                                      unsigned long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Word p once its epoch is e (w: a value already loaded from p). Gives up after the
+// context's wait limit: records kDevErrCommTimeout, clears ok and returns what it last read;
+// once ok is false the caller's later words are not waited for.
+__device__ __forceinline__ unsigned long long wait_tagged(const unsigned long long* p,
+                                                          unsigned long long w, unsigned e,
+                                                          bool& ok, int* err) {
+  if ((unsigned)(w >> 32) == e || !ok) return w;
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(err);
+  for (int i = 0;; ++i) {
+    w = ld_relaxed_sys_u64(p);
+    if ((unsigned)(w >> 32) == e) return w;
+    if ((i & 63) == 63 && globaltimer_ns() - t0 > limit) {
+      if (err) atomicCAS(err, 0, (int)kDevErrCommTimeout);
+      ok = false;
+      return w;
+    }
+  }
 }
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -90,12 +129,13 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
 }
 
 // Waits for phase `parity` of `bar` to complete. Gives up after the context's wait limit
-// (wait_limit_ns): records `code` in *err (first error wins) and returns false.
+// (wait_limit_ns) times `limit_scale`: records `code` in *err (first error wins) and returns
+// false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
-                                                  int code) {
+                                                  int code, uint32_t limit_scale = 1) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = wait_limit_ns(err);
+  const uint64_t limit = wait_limit_ns(err) * limit_scale;
   while (true) {
     if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
     if (globaltimer_ns() - t0 > limit) {

@@ -80,6 +80,7 @@ namespace rrr {
 int tp_comm_world(const rrr_tp_comm* c) { return c ? c->world : 1; }
 int tp_comm_rank(const rrr_tp_comm* c) { return c ? c->rank : 0; }
 bool tp_comm_is_p2p(const rrr_tp_comm* c) { return c && c->p2p; }
+rrr_comm* tp_comm_p2p_of(rrr_tp_comm* c) { return c ? c->p2p : nullptr; }
 
 int tp_allreduce(rrr_tp_comm* c, float* x, int64_t n, void* stream) {
   if (c->p2p) return rrr_comm_allreduce_f32(c->p2p, x, n, stream);

@@ -2,7 +2,8 @@
 // collective between processes: the exchanges of the one-GPU emulation of a G-rank split
 // (all ranks' buffers on this GPU, summed in rank order like the peer-memory all-reduce,
 // so the emulated step has the bits of the peer-memory one) and the reorder after an NCCL
-// all-gather of row-split logits. Plain grid-stride kernels; the sizes are small (3072
+// all-gather of row-split logits; and the end of a step's fused exchanges (the last
+// site's sum, the epoch advance). Plain grid-stride kernels; the sizes are small (3072
 // floats per all-reduce, one row of logits per token).
 #include <cuda_runtime.h>
 
@@ -57,6 +58,31 @@ __global__ void rows_from_ranks_kernel(const float* tmp, float* out, int G, int 
   }
 }
 
+// out[i] = sum over ranks in rank order of the tagged words slots[r*n + i] of epoch
+// *epoch + 1 (the order and the bits of the exchange kernel's all-reduce).
+__global__ void fused_sum_kernel(const unsigned long long* slots, float* out, int n, int G,
+                                 const unsigned* epoch, int* err) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const unsigned e = *epoch + 1u;
+  bool ok = true;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned long long* p = slots + i;
+    float acc = __uint_as_float((unsigned)wait_tagged(p, ld_relaxed_sys_u64(p), e, ok, err));
+    for (int r = 1; r < G; ++r) {
+      p += n;
+      acc += __uint_as_float((unsigned)wait_tagged(p, ld_relaxed_sys_u64(p), e, ok, err));
+    }
+    out[i] = acc;
+  }
+}
+
+__global__ void epoch_advance_kernel(unsigned* epoch) {
+  pdl_launch_dependents();
+  pdl_wait();
+  if (threadIdx.x == 0) *epoch += 1u;
+}
+
 int grid_for(int64_t n, int sms) {
   return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * 8));
 }
@@ -83,6 +109,17 @@ cudaError_t launch_local_allgather_rows(const LaunchEnv& env, const float* const
   return rrr_launch_pdl(local_allgather_rows_kernel,
                         dim3(grid_for((int64_t)rows * G * npr, env.sm_count)), dim3(256), 0,
                         env.stream, env.pdl, a, b, G, rows, npr);
+}
+
+cudaError_t launch_fused_sum(const LaunchEnv& env, const unsigned long long* slots, float* out,
+                             int n, int G, const unsigned* epoch) {
+  if (G < 1 || G > kMaxTpRanks || n < 1) return cudaErrorInvalidValue;
+  return rrr_launch_pdl(fused_sum_kernel, dim3((n + 255) / 256), dim3(256), 0, env.stream, env.pdl,
+                        slots, out, n, G, epoch, env.d_err);
+}
+
+cudaError_t launch_epoch_advance(const LaunchEnv& env, unsigned* epoch) {
+  return rrr_launch_pdl(epoch_advance_kernel, dim3(1), dim3(32), 0, env.stream, env.pdl, epoch);
 }
 
 cudaError_t launch_rows_from_ranks(const LaunchEnv& env, const float* tmp, float* out, int G,

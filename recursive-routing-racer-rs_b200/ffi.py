@@ -141,6 +141,7 @@ PROTOS = {
     "rrr_tp_wait": (c_int, [vp, vp, c_int]),
     "rrr_tp_comm_destroy": (c_int, [vp]),
     "rrr_phi4_tp_create": (c_int, [vp, POINTER(Phi4Desc), POINTER(TPShard), vp, POINTER(vp)]),
+    "rrr_phi4_tp_fused": (c_int, [vp, POINTER(c_int)]),
     "rrr_phi4_tp_forward_emulated": (c_int, [POINTER(vp), c_int, POINTER(vp), POINTER(vp), POINTER(vp),
                                              c_int, vp]),
     "rrr_position_advance": (c_int, [vp, vp, c_int, vp]),
@@ -157,6 +158,7 @@ PROTOS = {
     "rrr_fill_f32_normal": (c_int, [vp, vp, c_int64, c_float, c_float, c_uint64, vp]),
     "rrr_fill_f32_uniform": (c_int, [vp, vp, c_int64, c_float, c_float, c_uint64, vp]),
     "rrr_comm_create": (c_int, [vp, c_int, c_int, c_int64, POINTER(vp), vp]),
+    "rrr_comm_create_ex": (c_int, [vp, c_int, c_int, c_int64, c_int64, POINTER(vp), vp]),
     "rrr_comm_connect": (c_int, [vp, vp]),
     "rrr_comm_allreduce_f32": (c_int, [vp, vp, c_int64, vp]),
     "rrr_comm_allgather_f32": (c_int, [vp, vp, vp, c_int64, vp]),

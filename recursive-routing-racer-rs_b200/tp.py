@@ -209,15 +209,17 @@ def all_reduce_with_deadline(t, timeout_s: float, group=None) -> None:
 class P2PComm:
     """The C ABI's NVLink peer-memory exchanges (rrr_comm_*) for one rank; the 64-byte IPC
     handles are swapped with torch.distributed.all_gather_object. `tp` is its
-    rrr_tp_comm for rrr_phi4_tp_create."""
+    rrr_tp_comm for rrr_phi4_tp_create. fused_words > 0 adds the fused-exchange region
+    (rrr_comm_create_ex) that lets a rank's step push its partial rows from the GEMVs."""
 
-    def __init__(self, ctx: ffi.Context, rank: int, world: int, max_elems: int, group=None):
+    def __init__(self, ctx: ffi.Context, rank: int, world: int, max_elems: int, group=None,
+                 fused_words: int = 0):
         import torch.distributed as dist
         L = ffi.lib()
         self.ctx, self.group = ctx, group
         h = c_void_p()
         buf = ctypes.create_string_buffer(64)
-        ctx.check(L.rrr_comm_create(ctx.h, rank, world, max_elems, ctypes.byref(h), buf))
+        ctx.check(L.rrr_comm_create_ex(ctx.h, rank, world, max_elems, fused_words, ctypes.byref(h), buf))
         self.h = h
         handles = [None] * world
         dist.all_gather_object(handles, bytes(buf.raw), group=group)
@@ -277,10 +279,11 @@ class TPDecoder:
     comm = None with G > 1: the rank is only run through emulate_step."""
 
     def __init__(self, ctx: ffi.Context, weights: SyntheticPhi4TP, group=None, comm: str | None = None,
-                 max_batch: int = 1, max_seq: int = 0):
+                 max_batch: int = 1, max_seq: int = 0, fused: bool = True):
         """comm: "nccl" (rrr_tp_comm_nccl), "p2p" (rrr_comm_* kernels over NVLink peer
         memory) or None; max_batch: the largest M of forward_batched (sizes the peer-memory
-        buffers); max_seq: KV-cache rows (0: position-0 steps)."""
+        buffers); max_seq: KV-cache rows (0: position-0 steps); fused: on "p2p", fuse the
+        one-token step's all-reduces into its GEMVs (taken when every rank has its own GPU)."""
         self.ctx, self.w, self.group = ctx, weights, group
         self.max_seq = max_seq
         sh = weights.shard
@@ -288,8 +291,9 @@ class TPDecoder:
         if comm not in (None, "nccl", "p2p"):
             raise ValueError(f"unknown comm {comm!r}")
         if comm == "p2p" and sh.G > 1:
+            fw = 2 * weights.cfg.n_layers * sh.G * weights.cfg.d_model if fused else 0
             self.channel = P2PComm(ctx, sh.g, sh.G,
-                                   max_batch * max(weights.cfg.d_model, sh.vocab_rows), group)
+                                   max_batch * max(weights.cfg.d_model, sh.vocab_rows), group, fw)
         elif comm == "nccl" and sh.G > 1:
             self.channel = NcclComm(ctx, sh.g, sh.G, group)
         d, self._keep = weights.desc(max_seq)
@@ -342,6 +346,13 @@ class TPDecoder:
         n = ctypes.c_int()
         self.ctx.check(ffi.lib().rrr_phi4_position(self.h, ctypes.byref(n)))
         return n.value
+
+    @property
+    def fused(self) -> bool:
+        """Whether the one-token step's all-reduces run inside its GEMVs."""
+        n = ctypes.c_int()
+        self.ctx.check(ffi.lib().rrr_phi4_tp_fused(self.h, ctypes.byref(n)))
+        return bool(n.value)
 
     def launches_per_step(self) -> int:
         """Kernels of this library per step (NCCL collectives not counted; the peer-memory

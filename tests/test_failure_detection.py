@@ -137,6 +137,76 @@ def test_tp_wait_with_a_one_rank_nccl_communicator(rrr, ctx):
     w.close()
 
 
+def _fused_stall_rank(rank, port, q):
+    """Two ranks on two GPUs with the all-reduces fused into the GEMVs; rank 1 makes its
+    model but never steps, so rank 0's prologues wait for rows that never come."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    rrr = importlib.import_module("recursive-routing-racer-rs_b200")
+    phi4 = importlib.import_module("recursive-routing-racer-rs_b200.phi4")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+    L = rrr.ffi.lib()
+    ctx = rrr.Context(rank)
+    cfg = phi4.ModelConfig(n_layers=2, vocab_size=4096)
+    w = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, 2, rank), seed=3)
+    dec = tp.TPDecoder(ctx, w, comm="p2p")
+    res = None
+    if rank == 0:
+        ctx.check(L.rrr_set_wait_limit(ctx.h, 50_000_000))          # 50 ms
+        h = torch.randn(cfg.d_model, device="cuda")
+        lg = torch.empty(cfg.vocab_size, device="cuda")
+        torch.cuda.synchronize()
+        t0 = time.time()
+        dec.forward(h, lg)
+        code = ctypes.c_int(0)
+        rc = L.rrr_check_device_error(ctx.h, ctypes.byref(code))
+        elapsed = time.time() - t0
+        ctx.check(L.rrr_set_wait_limit(ctx.h, 0))
+        # the context still works afterwards
+        x = torch.ones(1 << 20, device="cuda")
+        ok_after = float(x.sum().item()) == float(1 << 20) and ctx.device_error() == 0
+        res = (dec.fused, rc, code.value, elapsed, ok_after)
+    dist.barrier()
+    dec.close()
+    w.close()
+    q.put((rank, res))
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_fused_exchange_wait_expires_when_a_rank_never_steps():
+    """The fused exchange's waits (tagged rows in the GEMV prologue, the last site's sum) are
+    bounded like the exchange kernel's: with a 50 ms limit the step ends in well under a
+    second, the device flag holds the exchange code (5, not the weight stream's) and the
+    GPU keeps working. Needs two GPUs (fused exchanges run only between distinct GPUs)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    spawn = mp.get_context("spawn")
+    q = spawn.Queue()
+    port = _free_port()
+    procs = [spawn.Process(target=_fused_stall_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(2):
+        r, res = q.get(timeout=240)
+        out[r] = res
+    for p in procs:
+        p.join(60)
+        if p.is_alive():
+            p.kill()
+        assert p.exitcode == 0
+    fused, rc, code, elapsed, ok_after = out[0]
+    assert fused
+    assert rc == -7 and code == 5, (rc, code)
+    assert 0.04 < elapsed < 5.0, elapsed
+    assert ok_after
+
+
 def test_wait_limit_range_is_checked(rrr):
     """Out-of-range limits are rejected; no GPU is needed to reach the check."""
     L = rrr.ffi.lib()

@@ -350,6 +350,78 @@ def test_dispatch_by_name_and_batch(rrr, ctx, oracle, G):
         bb.free()
 
 
+def test_prebuilt_table_dependent_gemvs(rrr, ctx, oracle, G):
+    """A prebuilt table of consecutive matmul_q{4,5,6}k dispatches where each GEMV reads what
+    the previous one wrote (stream order is the reference's barrier after each dispatch): a
+    dependent run of mixed quant types with K up to 4096 and a ragged row count, an rmsnorm
+    dispatch, then 70 more GEMVs; every output against the oracle applied to the device's
+    own inputs."""
+    eng = rrr.ComputeEngine.__new__(rrr.ComputeEngine)
+    eng.ctx = ctx
+    rng = np.random.default_rng(81)
+    bufs = []
+
+    def buf(n_bytes):
+        b = eng.alloc_buffer(n_bytes)
+        bufs.append(b)
+        return b
+
+    def weight(qt, K, N):
+        raw = oracle.random_blocks(qt, N * (K // 256), rng)
+        w = buf(raw.nbytes)
+        eng.upload(w, raw)
+        return raw, w
+
+    x0 = rng.standard_normal(3072).astype(np.float32)
+    bx = buf(3072 * 4)
+    eng.upload(bx, x0)
+    # (qtype, K, N, input buffer index or "x0")
+    spec = [(13, 3072, 2048), (14, 2048, 4096), (14, 4096, 768), (12, 768, 1000), (12, 768, 512)]
+    tbl = eng.prebuilt_batch()
+    ins, outs, raws = [], [], []
+    prev = bx
+    for i, (qt, K, N) in enumerate(spec):
+        raw, w = weight(qt, K, N)
+        out = buf(N * 4)
+        src = prev if i != 4 else outs[2]          # the ragged GEMV and the next both read y[2]
+        tbl.add(*rrr.kquant_dispatch(src, w, out, rrr.QType(qt), K, N)[:4])
+        ins.append(src)
+        outs.append(out)
+        raws.append(raw)
+        prev = out
+    gam = rng.uniform(0.5, 1.5, 512).astype(np.float32)
+    bg, bn = buf(512 * 4), buf(512 * 4)
+    eng.upload(bg, gam)
+    tbl.add("rmsnorm", [outs[4], bg, bn], [512 * 4] * 3, rrr.push_u32(1, 512))
+    raw5, w5 = weight(13, 512, 256)
+    many, odd = [], {}
+    for j in range(70):
+        out = buf(256 * 4)
+        if j % 2 == 0:
+            tbl.add(*rrr.kquant_dispatch(bn, w5, out, rrr.QType(13), 512, 256)[:4])
+        else:
+            odd[j], w = weight(12, 3072, 256)
+            tbl.add(*rrr.kquant_dispatch(bx, w, out, rrr.QType(12), 3072, 256)[:4])
+        many.append(out)
+    for _ in range(2):
+        tbl.launch()
+        eng.sync()
+    assert ctx.device_error() == 0
+    host = lambda b, n: (lambda a: (eng.download(b, a), a)[1])(np.empty(n, np.float32))
+    for i, (qt, K, N) in enumerate(spec):
+        xi = x0 if i == 0 else host(ins[i], K)
+        assert rel_l2(host(outs[i], N), oracle.gemv_kq(qt, raws[i], xi, K, N)) < TOL, i
+    normed = host(bn, 512)
+    assert rel_l2(normed, oracle.rms_norm(host(outs[4], 512), gam, 1e-5)) < 1e-6
+    ref5 = oracle.gemv_kq(13, raw5, normed, 512, 256)
+    for j in range(70):
+        ref = ref5 if j % 2 == 0 else oracle.gemv_kq(12, odd[j], x0, 3072, 256)
+        assert rel_l2(host(many[j], 256), ref) < TOL, j
+    tbl.close()
+    for b in bufs:
+        b.free()
+
+
 @pytest.mark.parametrize("qt", QTYPES)
 @pytest.mark.parametrize("M", [1, 5, 16, 37])
 def test_gemm_batched(rrr, ctx, oracle, G, qt, M):

@@ -5,7 +5,9 @@
   GPU) equals the 1-GPU rrr_phi4_forward step at G = 2, 4 and 8 (8: O-proj windows that
   cut super-blocks) within 1e-4 relative L2 (only the summation order differs);
 * with 2+ GPUs: the run with one process per GPU, eager and as a CUDA graph, with the
-  exchanges as NCCL collectives or as the peer-memory kernels, equals the 1-GPU step.
+  exchanges as NCCL collectives, as the peer-memory kernels, or fused into the GEMVs
+  (peer-memory pushes from the O-projection / down epilogues, sums in the next prologue),
+  equals the 1-GPU step; the fused step has the bits of the unfused one.
 """
 import importlib
 import os
@@ -145,7 +147,10 @@ def _nccl_rank(rank, world, port, q, comm, max_seq=0):
         gen = torch.Generator(device="cuda").manual_seed(5)
         hidden0 = torch.randn(cfg.d_model, device="cuda", generator=gen)
         w = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, world, rank), seed=seed)
-        dec = tp.TPDecoder(ctx, w, comm=comm, max_seq=max_seq)
+        fused = comm == "p2p"
+        dec = tp.TPDecoder(ctx, w, comm="p2p" if comm.startswith("p2p") else comm, max_seq=max_seq,
+                           fused=fused)
+        assert dec.fused == fused
         lg = torch.empty(cfg.vocab_size, device="cuda")
         am = torch.zeros(1, dtype=torch.int32, device="cuda")
         results = []
@@ -181,9 +186,11 @@ def _nccl_rank(rank, world, port, q, comm, max_seq=0):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("comm,max_seq", [("nccl", 0), ("p2p", 0), ("nccl", 16), ("p2p", 16)])
+@pytest.mark.parametrize("comm,max_seq", [("nccl", 0), ("p2p", 0), ("p2p-unfused", 0), ("nccl", 16),
+                                          ("p2p", 16), ("p2p-unfused", 16)])
 def test_tp_nccl_two_gpus(comm, max_seq):
-    """comm = nccl: torch.distributed collectives; p2p: the rrr_comm_* peer-memory kernels.
+    """comm = nccl: torch.distributed collectives; p2p: the all-reduces fused into the
+    GEMVs over peer memory; p2p-unfused: the rrr_comm_* peer-memory exchange kernels.
     max_seq > 0: three decode steps at positions 0, 1, 2 with the KV caches (eager, then
     captured and replayed), against the 1-GPU KV step."""
     import torch
@@ -206,3 +213,75 @@ def test_tp_nccl_two_gpus(comm, max_seq):
     assert res[-1] == 0
     for rh, rl, same in res[:-1]:
         assert rh < 1e-4 and rl < 1e-4 and same
+
+
+# ------------------------------------------------------------------ fused vs unfused
+def _fused_rank(rank, world, port, q, max_seq):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    rrr = importlib.import_module("recursive-routing-racer-rs_b200")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        ctx = rrr.Context(rank)
+        cfg = phi4.ModelConfig(n_layers=3, vocab_size=8192)
+        gen = torch.Generator(device="cuda").manual_seed(9)
+        tokens = [torch.randn(cfg.d_model, device="cuda", generator=gen) for _ in range(4)]
+        w = tp.SyntheticPhi4TP(ctx, cfg, tp.plan(cfg, world, rank), seed=21)
+        runs, flags, launches = [], [], []
+        for fused in (False, True):
+            dec = tp.TPDecoder(ctx, w, comm="p2p", max_seq=max_seq, fused=fused)
+            flags.append(dec.fused)
+            launches.append(dec.launches_per_step())
+            lg = torch.empty(cfg.vocab_size, device="cuda")
+            am = torch.zeros(1, dtype=torch.int32, device="cuda")
+            h = torch.empty(cfg.d_model, device="cuda")  # one buffer: the graph keeps it
+            out = []
+            # eager, captured, replayed, replayed: four tokens (positions 0..3 with a cache)
+            for i, use_graph in enumerate((False, True, True, True)):
+                h.copy_(tokens[i])
+                dec.forward(h, lg, am, use_graph=use_graph)
+                torch.cuda.synchronize()
+                out.append((h.cpu().numpy().copy(), lg.cpu().numpy().copy(), int(am.item())))
+            runs.append(out)
+            dec.close()
+        same = all(np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]) and a[2] == b[2]
+                   for a, b in zip(runs[0], runs[1]))
+        q.put((rank, flags, launches, same, ctx.device_error()))
+        w.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("max_seq", [0, 8])
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_fused_exchange_bits_equal_unfused(world, max_seq):
+    """One process per GPU: the one-token step with the all-reduces fused into the GEMVs
+    (rank-order sums of tagged peer rows in the RMSNorm prologue) gives the same bits as the
+    step with the exchange kernels, eager and replayed from its CUDA graph, at world 2, 4, 8
+    (as many as the box has), with and without a KV cache, in fewer launches."""
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = _free_port()
+    procs = [mpc.Process(target=_fused_rank, args=(r, world, port, q, max_seq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+        assert p.exitcode == 0
+    for _ in range(world):
+        rank, flags, launches, same, err = q.get(timeout=10)
+        assert flags == [False, True], (rank, flags)
+        assert launches[1] < launches[0], launches
+        assert same, rank
+        assert err == 0
