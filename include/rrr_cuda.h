@@ -86,6 +86,18 @@ int rrr_check_device_error(rrr_ctx* ctx, int* code);
  * [1e5, 6e10] ns. No reference counterpart (the reference's fence waits are unbounded,
  * engine.rs:312,369). */
 int rrr_set_wait_limit(rrr_ctx* ctx, uint64_t ns);
+/* Device-side timeline of the single-token K-quant GEMVs (tracing; the reference has none).
+ * With `bytes` of device memory set, every GEMV launch of this context (rrr_gemv_kq*,
+ * named dispatches, prebuilt tables, the decode steps) is given one 64-byte record per CTA,
+ * assigned on the host at launch or capture time, round-robin over the buffer (a launch
+ * that does not fit in the rest of the buffer starts again at record 0; a graph replays
+ * into the records of its capture). u64 fields, %globaltimer ns: [0] CTA start, [1] first
+ * weight copy issued, [2] grid dependency resolved, [3] GEMV input prepared, [4] rows
+ * stored, [5] last weight copy issued, [6] qtype << 56 | K << 28 | N, [7] launch sequence
+ * number << 16 | CTA index. buffer = NULL turns it off (the default). */
+int rrr_set_trace(rrr_ctx* ctx, void* buffer, int64_t bytes);
+/* The next record the tracer will assign and the GEMV launches traced since rrr_set_trace. */
+int rrr_trace_position(rrr_ctx* ctx, int64_t* next_record, int64_t* launches);
 /* Programmatic dependent launch (default on): each kernel of the library may start while
  * the previous kernel on its stream finishes (weights stream early; inputs are read after
  * the grid dependency wait). enable = 0 serialises every launch (a debugging aid). */

@@ -52,6 +52,12 @@ LaunchEnv rrr::make_env(rrr_ctx* ctx, void* stream) {
   env.sm_count = ctx->sm_count;
   env.d_err = ctx->d_err;
   env.pdl = ctx->pdl;
+  if (ctx->trace) {
+    env.trace = ctx->trace;
+    env.trace_cap = ctx->trace_cap;
+    env.trace_next = &ctx->trace_next;
+    env.trace_seq = &ctx->trace_seq;
+  }
   return env;
 }
 
@@ -304,6 +310,25 @@ int rrr_set_wait_limit(rrr_ctx* ctx, uint64_t ns) {
   const unsigned long long v = ns;
   RRR_LAUNCH_CHECK(ctx, cudaMemcpy(ctx->d_err + rrr::kWaitLimitSlot, &v, sizeof v, cudaMemcpyHostToDevice),
                    "rrr_set_wait_limit: write");
+  return RRR_OK;
+}
+
+int rrr_set_trace(rrr_ctx* ctx, void* buffer, int64_t bytes) {
+  RRR_CHECK_CTX(ctx);
+  if (buffer && (bytes < 64 || (reinterpret_cast<uintptr_t>(buffer) & 7)))
+    return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_set_trace: need an 8-byte aligned buffer of >= 64 bytes");
+  ctx->trace = static_cast<unsigned long long*>(buffer);
+  ctx->trace_cap = buffer ? bytes / 64 : 0;
+  ctx->trace_next = 0;
+  ctx->trace_seq = 0;
+  return RRR_OK;
+}
+
+int rrr_trace_position(rrr_ctx* ctx, int64_t* next_record, int64_t* launches) {
+  RRR_CHECK_CTX(ctx);
+  if (!next_record || !launches) return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_trace_position: null argument");
+  *next_record = ctx->trace_next;
+  *launches = ctx->trace_seq;
   return RRR_OK;
 }
 

@@ -13,6 +13,10 @@ struct rrr_ctx {
   int* d_err = nullptr;  // 256 B: [0] device error flag written by kernels whose bounded
                          // waits give up; [64..79] argmax key + counter (kept zeroed)
   bool pdl = true;       // launch kernels with programmatic dependent launch
+  // GEMV timeline (rrr_set_trace): device records of 8 u64, the next record and the launch
+  // sequence number, assigned on the host at launch (or capture) time
+  unsigned long long* trace = nullptr;
+  int64_t trace_cap = 0, trace_next = 0, trace_seq = 0;
   std::string last_error;
   void* argmax_scratch() { return reinterpret_cast<char*>(d_err) + 64; }
 };

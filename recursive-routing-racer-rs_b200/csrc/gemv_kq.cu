@@ -75,6 +75,9 @@ struct GemvParams {
   unsigned long long* push[kMaxTpRanks];
   int G;
   const unsigned* epoch;
+  // timeline records of this launch (rrr_set_trace; null: off): 8 u64 per CTA
+  unsigned long long* trace;
+  unsigned long long trace_tag;  // launch sequence number << 16
 };
 
 __device__ __forceinline__ void mma_u8s8(int& d0, int& d1, int& d2, int& d3, uint32_t a0,
@@ -473,17 +476,20 @@ __device__ __forceinline__ void prepare_x(const GemvParams& p, int8_t* dig, floa
       s8[g] = 0.f;
       if (g < ng) {
         ssq += finish8(p, vg[g], ag[g]);
+        const float* v = vg[g];
+        // max |v| as a tree (NaN ignored as by the sequential fmaxf from 0)
+        const float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        const float b = fmaxf(fmaxf(fabsf(v[4]), fabsf(v[5])), fmaxf(fabsf(v[6]), fabsf(v[7])));
+        m[g] = fmaxf(fmaxf(a, b), 0.f);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          m[g] = fmaxf(m[g], fabsf(vg[g][i]));
-          s8[g] += vg[g][i];
-        }
+        for (int i = 0; i < 8; ++i) s8[g] += v[i];
       }
     }
+    // the block maximum over the warp in one integer reduction: non-negative floats order
+    // like their bit patterns
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int g = 0; g < kPrepGroup; ++g) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], o));
+    for (int g = 0; g < kPrepGroup; ++g)
+      m[g] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m[g])));
     float s16[kPrepGroup], s32[kPrepGroup];
 #pragma unroll
     for (int g = 0; g < kPrepGroup; ++g) s16[g] = s8[g] + __shfl_xor_sync(0xffffffffu, s8[g], 1);
@@ -546,8 +552,10 @@ __device__ __forceinline__ void prepare_x(const GemvParams& p, int8_t* dig, floa
       if (lane == 0) xscale[b] = m[g] > 0.f ? __uint_as_float((uint32_t)(127 + E - 20) << 23) : 0.f;
     }
   }
-  ssq = warp_sum(ssq);
-  if (lane == 0) misc[warp] = ssq;
+  if (p.mode == RRR_X_RMSNORM) {
+    ssq = warp_sum(ssq);
+    if (lane == 0) misc[warp] = ssq;
+  }
 }
 
 // 1/rms of the RMSNORM input from the warps' sums of x^2 (after the barrier that follows
@@ -841,6 +849,8 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_kq_kernel(const GemvP
   // fewer tiles than groups every SM still gets work
   const int vb = grp * gridDim.x + blockIdx.x, vstride = gridDim.x * kGroups;
 
+  unsigned long long* const tr = p.trace ? p.trace + 8 * (size_t)blockIdx.x : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer_ns();
   if (threadIdx.x == 0) init_cta_smem(smem, p);
   __syncthreads();
   pdl_launch_dependents();
@@ -865,18 +875,30 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_kq_kernel(const GemvP
     }
     // (consumers that wait for the ranks' rows first get twice the limit, so that a
     // missing rank is reported as such)
+    if (tr && grp == 0 && lane == 0) tr[1] = globaltimer_ns();
     produce_item<QT>(p, g, vb, vstride, lane, rp, p.sum_in ? 2u : 1u);
+    if (tr && grp == 0 && lane == 0) tr[5] = globaltimer_ns();
     drain_ring(g, rp, lane, p.err);
     return;
   }
 
   pdl_wait();
+  if (tr && threadIdx.x == 0) tr[2] = globaltimer_ns();
   // fused exchange: this step's epoch, and whether this rank still feeds its peers (no
   // error recorded by an earlier kernel, e.g. a wait that ran out)
   const unsigned tag = p.G ? *p.epoch + 1u : 0u;
   const bool feed = p.push[0] && *reinterpret_cast<volatile int*>(p.err) == 0;
   const float inv_rms = prepare_item<FRAG>(p, g, warp, lane, tag);
+  if (tr && threadIdx.x == 0) tr[3] = globaltimer_ns();
   consume_item<QT, FRAG>(p, g, vb, vstride, warp % kNW, lane, inv_rms, tag, feed, rp);
+  if (tr) {
+    named_barrier(1, kGroups * kNW * 32);
+    if (threadIdx.x == 0) {
+      tr[4] = globaltimer_ns();
+      tr[6] = ((unsigned long long)QT << 56) | ((unsigned long long)p.K << 28) | (unsigned long long)p.N;
+      tr[7] = p.trace_tag | blockIdx.x;
+    }
+  }
 }
 
 // Shared-memory layout of one launch. FRAG: the x digits are stored as ready-made per-lane
@@ -951,7 +973,14 @@ cudaError_t launch_k(const LaunchEnv& env, const GemvParams& p, int smem) {
   // kMinCtas CTAs per SM (two producers and 16 consumer warps per SM); each CTA runs
   // kGroups producer/consumer groups, so it needs at least kGroups tiles to be busy
   const int grid = std::max(1, std::min(p.n_tiles, std::min(per_sm, kMinCtas) * env.sm_count));
-  return rrr_launch_pdl(kern, dim3(grid), dim3(kThreads), smem, env.stream, env.pdl, p);
+  GemvParams q = p;
+  if (env.trace && grid <= env.trace_cap) {
+    if (*env.trace_next + grid > env.trace_cap) *env.trace_next = 0;
+    q.trace = env.trace + 8 * (size_t)*env.trace_next;
+    q.trace_tag = (unsigned long long)(*env.trace_seq)++ << 16;
+    *env.trace_next += grid;
+  }
+  return rrr_launch_pdl(kern, dim3(grid), dim3(kThreads), smem, env.stream, env.pdl, q);
 }
 
 template <int QT>

@@ -18,6 +18,12 @@ struct LaunchEnv {
   int sm_count;
   int* d_err;  // device error flag of the context
   bool pdl;    // launch with programmatic stream serialisation
+  // GEMV timeline of the context (rrr_set_trace; null: off): records, their number, the
+  // next free record and the launch counter (host memory of the context)
+  unsigned long long* trace = nullptr;
+  int64_t trace_cap = 0;
+  int64_t* trace_next = nullptr;
+  int64_t* trace_seq = nullptr;
 };
 
 // Shape limits of the K-quant GEMV (checked by the C ABI before launching).

@@ -142,6 +142,8 @@ PROTOS = {
     "rrr_tp_comm_destroy": (c_int, [vp]),
     "rrr_phi4_tp_create": (c_int, [vp, POINTER(Phi4Desc), POINTER(TPShard), vp, POINTER(vp)]),
     "rrr_phi4_tp_fused": (c_int, [vp, POINTER(c_int)]),
+    "rrr_set_trace": (c_int, [vp, vp, c_int64]),
+    "rrr_trace_position": (c_int, [vp, POINTER(c_int64), POINTER(c_int64)]),
     "rrr_phi4_tp_forward_emulated": (c_int, [POINTER(vp), c_int, POINTER(vp), POINTER(vp), POINTER(vp),
                                              c_int, vp]),
     "rrr_position_advance": (c_int, [vp, vp, c_int, vp]),

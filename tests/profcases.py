@@ -10,6 +10,7 @@ DRAM figures of a capture are those of the bench's per-GEMV lines.
     python tests/profcases.py gemm --m 256    # batched tcgen05 GEMM
     python tests/profcases.py attn --pos 1024 # RoPE + KV + attention
     python tests/profcases.py batched --m 64  # M-token decode step
+    python tests/profcases.py timeline        # GEMV phase timeline (rrr_set_trace), no ncu
 """
 import argparse
 import importlib
@@ -112,8 +113,83 @@ def case_batched(ctx, L, torch, args):
         dec.forward_batched(h.data_ptr(), lg.data_ptr(), args.m, am.data_ptr(), False)
 
 
+def case_timeline(ctx, L, torch, args):
+    """The GEMV timeline (rrr_set_trace) of the graph-replayed decode step (--layers, position
+    0, or the KV-cache step at --pos with --max-seq) and of the bench's table of independent
+    GEMVs: per GEMV kind, the medians over the middle layers of each phase (us from the
+    launch's first CTA start) and of the gap from the previous launch's last stored row."""
+    import ctypes
+    import json
+    import numpy as np
+    phi4 = importlib.import_module(_PKG + ".phi4")
+    trace = importlib.import_module(_PKG + ".trace")
+    cfg = phi4.ModelConfig(n_layers=args.layers)
+    m = phi4.SyntheticPhi4(ctx, cfg, seed=5)
+    names = ["qkv", "o_proj", "gate_up", "down"]
+
+    def summarise(title, launches, per_layer):
+        rows = []
+        for i, name in enumerate(names):
+            sel = [k for k in range(len(launches)) if k % per_layer == i
+                   and 4 <= k // per_layer < args.layers - 4]
+            if not sel:
+                continue
+            med = lambda key: round(float(np.median([launches[k][key] for k in sel])), 2)
+            gap = [round((launches[k]["start_ns"] - (launches[k - 1]["start_ns"] + 1e3 * launches[k - 1]["end"])) / 1e3, 2)
+                   for k in sel]
+            rows.append({"gemv": name, "shape": "%s %dx%d" % (launches[sel[0]]["qtype"], launches[sel[0]]["N"],
+                                                              launches[sel[0]]["K"]),
+                         "ctas": launches[sel[0]]["ctas"], "last_start": med("last_start"),
+                         "first_copy": med("first_copy"), "dependency": med("dependency"),
+                         "prepared": med("prepared"), "prepared_last": med("prepared_last"),
+                         "stored": med("stored"), "end": med("end"),
+                         "gap_after_prev": float(np.median(gap))})
+        span = (launches[-1]["start_ns"] + 1e3 * launches[-1]["end"] - launches[0]["start_ns"]) / 1e3
+        print(json.dumps({"case": title, "launches": len(launches), "span_us": round(span, 1), "gemvs": rows}))
+
+    # the decode step, replayed from its graph
+    dec = phi4.Phi4Decoder(ctx, m, max_seq=args.max_seq)
+    if args.max_seq:
+        dec.set_position(max(0, args.pos - args.rounds - 2))
+    h = torch.randn(cfg.d_model, device="cuda")
+    lg = torch.empty(cfg.vocab_size, device="cuda")
+    am = torch.zeros(1, dtype=torch.int32, device="cuda")
+    tr = trace.GemvTrace(ctx, records=1 << 16)
+    for _ in range(args.rounds + 2):
+        dec.forward(h.data_ptr(), lg.data_ptr(), am.data_ptr(), True)
+    torch.cuda.synchronize()
+    # the last 4 * layers launches are the captured graph's (the first step ran eagerly)
+    summarise("decode_step" + ("_kv_pos%d" % args.pos if args.max_seq else ""),
+              tr.launches()[-4 * cfg.n_layers:], 4)
+    tr.close()
+    dec.close()
+    # the GEMV table of the bench (independent inputs, one graph per replay)
+    rrr = importlib.import_module(_PKG)
+    X = torch.randn(cfg.n_layers * 16384, device="cuda")
+    Y = torch.empty(cfg.n_layers * 4 * 16384, device="cuda")
+    b = c_void_p()
+    ctx.check(L.rrr_batch_create(ctx.h, ctypes.byref(b)))
+    k = 0
+    for l in range(cfg.n_layers):
+        for name in names:
+            p, qt, K, N = m.layers[l][name]
+            bufs = (c_void_p * 3)(X.data_ptr() + 4 * l * 16384, p, Y.data_ptr() + 4 * k * 16384)
+            sizes = (ctypes.c_uint64 * 3)(4 * K, cfg.weight_bytes(qt, K, N), 4 * N)
+            push = ctypes.create_string_buffer(rrr.push_u32(K, N), 8)
+            ctx.check(L.rrr_batch_add(b, {12: b"matmul_q4k", 13: b"matmul_q5k", 14: b"matmul_q6k"}[qt],
+                                      bufs, sizes, 3, push, 8))
+            k += 1
+    tr = trace.GemvTrace(ctx, records=1 << 16)
+    for _ in range(args.rounds + 2):
+        ctx.check(L.rrr_batch_launch(b, None))
+    torch.cuda.synchronize()
+    summarise("gemv_table", tr.launches(), 4)
+    tr.close()
+    L.rrr_batch_destroy(b)
+
+
 CASES = {"gemv": case_gemv, "decode": case_decode, "gemm": case_gemm, "attn": case_attn,
-         "batched": case_batched}
+         "batched": case_batched, "timeline": case_timeline}
 
 
 def main(argv=None):

@@ -720,3 +720,47 @@ def test_logits_f32_batched_full_vocab(rrr, ctx, oracle, G):
         ref = oracle.gemv_f32(Wr, oracle.rms_norm(X[m], g, 1e-5))
         assert rel_l2(got[m, rows], ref) < TOL, m
     del W
+
+
+def test_gemv_timeline_trace(rrr, ctx, oracle, G):
+    """rrr_set_trace: one record per CTA of every GEMV launch with ordered phase stamps
+    (start <= dependency <= prepared <= stored; start <= first copy <= last copy), the
+    launch's shape and sequence number; tracing off assigns nothing; results unchanged."""
+    import importlib
+    import torch
+    trace = importlib.import_module("recursive-routing-racer-rs_b200.trace")
+    L = rrr.ffi.lib()
+    rng = np.random.default_rng(17)
+    shapes = [(12, 3072, 1000), (14, 2048, 300), (13, 512, 4096)]
+    data = []
+    for qt, K, N in shapes:
+        raw = oracle.random_blocks(qt, N * (K // 256), rng)
+        x = rng.standard_normal(K).astype(np.float32)
+        data.append((qt, K, N, raw, G.dev(raw), G.dev(x), G.empty_f32(N), x))
+    tr = trace.GemvTrace(ctx, records=4096)
+    for qt, K, N, raw, wd, xd, y, x in data:
+        ctx.check(L.rrr_gemv_kq(ctx.h, qt, vp(wd), vp(xd), vp(y), K, N, None, None))
+    torch.cuda.synchronize()
+    launches = tr.launches()
+    assert [(l["qtype"], l["K"], l["N"]) for l in launches] == \
+        [({12: "Q4_K", 13: "Q5_K", 14: "Q6_K"}[qt], K, N) for qt, K, N in shapes]
+    nxt, n = tr.position()
+    assert n == 3 and nxt == sum(l["ctas"] for l in launches)
+    r = tr.records().astype(np.int64)
+    assert len(r) == nxt
+    assert (r[:, 0] <= r[:, 2]).all() and (r[:, 2] <= r[:, 3]).all() and (r[:, 3] <= r[:, 4]).all()
+    has_copy = r[:, 1] > 0
+    assert has_copy.any()
+    assert (r[has_copy, 0] <= r[has_copy, 1]).all() and (r[has_copy, 1] <= r[has_copy, 5]).all()
+    assert sorted((r[:, 7] & 0xFFFF).tolist()) == sorted(
+        [c for l in launches for c in range(l["ctas"])])
+    for qt, K, N, raw, wd, xd, y, x in data:
+        assert rel_l2(G.host(y), oracle.gemv_kq(qt, raw, x, K, N)) < TOL
+    tr.close()
+    # off: nothing more is assigned
+    ctx.check(L.rrr_gemv_kq(ctx.h, 12, vp(data[0][4]), vp(data[0][5]), vp(data[0][6]), 3072, 1000, None, None))
+    torch.cuda.synchronize()
+    nxt2, n2 = ctypes.c_int64(), ctypes.c_int64()
+    ctx.check(L.rrr_trace_position(ctx.h, ctypes.byref(nxt2), ctypes.byref(n2)))
+    assert n2.value == 0 and nxt2.value == 0
+    assert ctx.device_error() == 0
