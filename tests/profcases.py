@@ -11,8 +11,10 @@ DRAM figures of a capture are those of the bench's per-GEMV lines.
     python tests/profcases.py attn --pos 1024 # RoPE + KV + attention
     python tests/profcases.py batched --m 64  # M-token decode step
     python tests/profcases.py timeline        # GEMV phase timeline (rrr_set_trace), no ncu
+    python tests/profcases.py logits --m 64 --vocab 32768   # batched logits (tcgen05 3xTF32)
 """
 import argparse
+import ctypes
 import importlib
 import os
 import sys
@@ -113,6 +115,23 @@ def case_batched(ctx, L, torch, args):
         dec.forward_batched(h.data_ptr(), lg.data_ptr(), args.m, am.data_ptr(), False)
 
 
+def case_logits(ctx, L, torch, args):
+    """Batched F32 logits of --m tokens over --vocab rows of a 3072-wide f32 matrix
+    (rrr_logits_f32_batched with the output RMSNorm: rmsnorm_kernel + logits_tc_kernel),
+    `rounds` launches."""
+    K, V, M = 3072, args.vocab, args.m
+    W = torch.empty(V * K, device="cuda")
+    ctx.check(L.rrr_fill_f32_normal(ctx.h, c_void_p(W.data_ptr()), V * K, 0.0, 0.02, 11, None))
+    gamma = torch.rand(K, device="cuda") + 0.5
+    x = torch.randn(M, K, device="cuda")
+    xn = torch.empty(M, K, device="cuda")
+    y = torch.empty(M, V, device="cuda")
+    for _ in range(args.rounds):
+        ctx.check(L.rrr_logits_f32_batched(ctx.h, c_void_p(W.data_ptr()), c_void_p(x.data_ptr()),
+                                           c_void_p(xn.data_ptr()), c_void_p(y.data_ptr()), M, V, K,
+                                           c_void_p(gamma.data_ptr()), ctypes.c_float(1e-5), None))
+
+
 def case_timeline(ctx, L, torch, args):
     """The GEMV timeline (rrr_set_trace) of the graph-replayed decode step (--layers, position
     0, or the KV-cache step at --pos with --max-seq) and of the bench's table of independent
@@ -189,7 +208,7 @@ def case_timeline(ctx, L, torch, args):
 
 
 CASES = {"gemv": case_gemv, "decode": case_decode, "gemm": case_gemm, "attn": case_attn,
-         "batched": case_batched, "timeline": case_timeline}
+         "batched": case_batched, "timeline": case_timeline, "logits": case_logits}
 
 
 def main(argv=None):
@@ -200,6 +219,7 @@ def main(argv=None):
     ap.add_argument("--m", type=int, default=256)
     ap.add_argument("--pos", type=int, default=1024)
     ap.add_argument("--max-seq", type=int, default=0)
+    ap.add_argument("--vocab", type=int, default=32768)
     args = ap.parse_args(argv)
     import torch
     rrr = importlib.import_module(_PKG)
