@@ -370,6 +370,23 @@ def run_ours(args, rank, world, local_rank):
               "frac_of_peak": round(dec_bytes / dms / 1e6 / peak, 4),
               "launches_per_token": dec.launches_per_step() + 1, "graph": True}
     dec.close()
+    # the same step with the logits dispatched as the reference does, in 32768-row chunks
+    # (7 launches instead of 1; identical rows and bytes)
+    import dataclasses
+    cfg_c = dataclasses.replace(cfg, logits_chunk_rows=32768)
+    model.cfg, cfg0 = cfg_c, model.cfg
+    cdec = phi4.Phi4Decoder(ctx, model)
+    model.cfg = cfg0
+    for _ in range(max(3, args.warmup)):
+        cdec.forward(hidden.data_ptr(), logits.data_ptr(), am.data_ptr(), True, stream)
+    barrier()
+    d0.record(stream)
+    for _ in range(dsteps):
+        cdec.forward(hidden.data_ptr(), logits.data_ptr(), am.data_ptr(), True, stream)
+    d1.record(stream)
+    barrier()
+    decode["tok_s_logits_32768_row_chunks"] = round(1e3 / max_over_ranks(d0.elapsed_time(d1) / dsteps), 2)
+    cdec.close()
     # ---------------- decode at real positions (KV cache of 2048 rows, RoPE, attention):
     # graph replays at positions 1024 .. 1024 + steps (the position advances on the device)
     kdec = phi4.Phi4Decoder(ctx, model, max_seq=2048)
@@ -624,7 +641,8 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clk,
             "cpu_baseline": cb,
             "decode": {"tok_s": decode["tok_s"], "ms_per_token": decode["ms_per_token"],
-                       "frac_of_peak": decode["frac_of_peak"], "launches": decode["launches_per_token"]},
+                       "frac_of_peak": decode["frac_of_peak"], "launches": decode["launches_per_token"],
+                       "tok_s_logits_32768_row_chunks": decode["tok_s_logits_32768_row_chunks"]},
             "decode_kv": {"tok_s": decode_kv["tok_s"], "positions": decode_kv["positions"]},
             "tp_decode": tp_decode,
             "roofline": {"bound": "hbm", "kernel": KERNEL_NAMES[dom_name],

@@ -32,7 +32,10 @@ class ModelConfig:
     o_type: int = 12        # Q4_K
     gate_up_type: int = 12  # Q4_K
     down_type: int = 14     # Q6_K
-    logits_chunk_rows: int = 32768
+    # Rows of the F32 logits per launch; 0 = all rows in one launch. The reference dispatches
+    # 32768-row chunks (phi4.rs:866-893, a dispatch-size limit of its backend); the rows and
+    # bytes are the same either way, and one launch saves a ramp and a tail per chunk.
+    logits_chunk_rows: int = 0
 
     def qkv_dim(self) -> int:
         return self.n_heads * self.head_dim + 2 * self.n_kv_heads * self.head_dim
