@@ -122,17 +122,26 @@ struct RopeParams {
 // Pair (x0, x1) of a head rotated for position pos with the operations of apply_rope_cfg
 // (phi4.rs:241-251): freq = base / factor, angle = pos * freq, (sin, cos) * attn_factor,
 // (x0 c - x1 s, x0 s + x1 c); every product and sum rounded separately (no FMA).
-__device__ __forceinline__ void rope_pair(float& x0, float& x1, int pos, float base_freq,
-                                          float factor, float attn_factor) {
+__device__ __forceinline__ void rope_cs(int pos, float base_freq, float factor, float attn_factor,
+                                        float& cs, float& ss) {
   const float freq = __fdiv_rn(base_freq, factor);
   const float angle = __fmul_rn((float)pos, freq);
   float s, c;
   sincosf(angle, &s, &c);
-  const float cs = __fmul_rn(c, attn_factor), ss = __fmul_rn(s, attn_factor);
+  cs = __fmul_rn(c, attn_factor);
+  ss = __fmul_rn(s, attn_factor);
+}
+__device__ __forceinline__ void rope_apply(float& x0, float& x1, float cs, float ss) {
   const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, ss));
   const float y1 = __fadd_rn(__fmul_rn(x0, ss), __fmul_rn(x1, cs));
   x0 = y0;
   x1 = y1;
+}
+__device__ __forceinline__ void rope_pair(float& x0, float& x1, int pos, float base_freq,
+                                          float factor, float attn_factor) {
+  float cs, ss;
+  rope_cs(pos, base_freq, factor, attn_factor, cs, ss);
+  rope_apply(x0, x1, cs, ss);
 }
 
 // One CTA per (head of Q then K, row); thread i owns the pair (2i, 2i+1) of its head.
@@ -187,12 +196,10 @@ struct AttnParams {
   float base_freq[kMaxRopePairs];
 };
 
-__device__ __forceinline__ float ld_dsmem_f32(const float* local, uint32_t rank) {
+__device__ __forceinline__ void st_dsmem_f32(float* local, uint32_t rank, float v) {
   uint32_t ra;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_addr(local)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-  return v;
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
 
 __device__ __forceinline__ void cluster_barrier() {
@@ -209,39 +216,50 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// The CTA's positions are processed in tiles of 8192 / head_dim rows (64 for 128): the K and V rows of a tile
-// (head g) are copied into shared memory with 16-byte cp.async, double-buffered so that
-// the next tile streams in while this one is computed; an online softmax (running max
-// and sum per query head, the accumulator rescaled per tile) carries across tiles.
-// Shared memory: K [2][kTile][HD] f16 | V [2][kTile][HD] f16 | new K, V row [2][HD] f16 |
-// q [hpk][HD] f32 |
-// probabilities [hpk][kTile] | rescale [hpk] | red [groups][hpk][HD] | partial acc
-// [hpk][HD] | partial max [hpk] | partial sum [hpk].
+// The CTA's positions are processed in tiles of 8192 / head_dim rows (64 for 128): the K and
+// V rows of a tile (head g) are copied into shared memory with 16-byte cp.async,
+// double-buffered so that the next tile streams in while this one is computed. The first
+// tile is requested as soon as the position is known, before the query is read.
+//
+// Every warp runs its own online softmax over the tile's rows (R = 32 / HB rows per warp
+// step, HB >= the query heads per KV head): lane l holds dims D*l .. D*l + D - 1 of the
+// query heads (in registers, RoPE applied) and of its accumulators. A step's HB*R partial
+// dot products are reduced with one 31-shuffle transpose, after which lane i holds the score
+// of (head i / R, row i % R); each lane then takes one exponential, and the probabilities
+// are broadcast for the weighted V rows. No CTA barrier is taken inside a tile. At the end
+// the warps' partials are merged in warp order through shared memory, and the CTAs of the
+// cluster over distributed shared memory in split order.
+//
+// Shared memory: K [2][kTile][HD] f16 | V [2][kTile][HD] f16 | warp max, sum, merge weight
+// [NW][HB] each | warp accumulators [NW][hpk][HD] | CTA accumulator [hpk][HD] | CTA max,
+// sum [HB] | new K, V row [2][HD] f16 | received split maxima, sums [kMaxSplits][HB] each |
+// received accumulators [kMaxSplits][share].
 template <int HD>
 constexpr int attn_tile() { return 8192 / HD; }  // K + V double buffer = 64 KB
 
-template <int HD>
+template <int HD, int HB>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) uint8_t smraw[];
-  constexpr int LPK = HD / 8;             // lanes per key row (16 bytes each)
-  constexpr int KPW = 32 / LPK;           // keys per warp step
   constexpr int NW = kAttnThreads / 32;
-  constexpr int PAIRS = HD / 2;           // V dims per thread: 2
-  constexpr int GROUPS = kAttnThreads / PAIRS;
-  constexpr int CH = HD / 8;              // 16-byte chunks per row
+  constexpr int D = HD / 32;  // dims per lane
+  constexpr int CH = HD / 8;  // 16-byte chunks per row
+  constexpr int R = 32 / HB;  // rows per warp step
   constexpr int kTile = attn_tile<HD>();
-  const int hpk = p.hpk;
+  const int hpk = p.hpk;  // <= HB
   __half* kt = reinterpret_cast<__half*>(smraw);
   __half* vt = kt + 2 * kTile * HD;
-  __half* knew = vt + 2 * kTile * HD;
-  __half* vnew = knew + HD;
-  float* qs = reinterpret_cast<float*>(vnew + HD);
-  float* pr = qs + hpk * HD;
-  float* alpha = pr + hpk * kTile;
-  float* red = alpha + kMaxHpk;
-  float* pacc = red + GROUPS * hpk * HD;
+  float* wm = reinterpret_cast<float*>(vt + 2 * kTile * HD);
+  float* wl = wm + NW * HB;
+  float* ww = wl + NW * HB;
+  float* wacc = ww + NW * HB;
+  float* pacc = wacc + NW * hpk * HD;
   float* pmax = pacc + hpk * HD;
-  float* psum = pmax + hpk;
+  float* psum = pmax + HB;
+  __half* knew = reinterpret_cast<__half*>(psum + HB);
+  __half* vnew = knew + HD;
+  float* rm = reinterpret_cast<float*>(vnew + HD);  // [kMaxSplits][HB]
+  float* rl = rm + kMaxSplits * HB;                 // [kMaxSplits][HB]
+  float* racc = rl + kMaxSplits * HB;               // [kMaxSplits][share]
 
   const int split = blockIdx.x, g = blockIdx.y, row = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -255,12 +273,45 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   const int per = (seq + p.splits - 1) / p.splits;
   const int t0 = min(seq, split * per), t1 = min(seq, t0 + per);
   const bool own_new = p.fused && pos_ok && t1 == seq && t0 < t1;
+  const int n_tiles = (t1 - t0 + kTile - 1) / kTile;
 
+  auto issue = [&](int tile) {
+    const int base = t0 + tile * kTile, nrows = min(kTile, t1 - base);
+    __half* kd = kt + (tile & 1) * kTile * HD;
+    __half* vd = vt + (tile & 1) * kTile * HD;
+    for (int c = threadIdx.x; c < nrows * CH; c += kAttnThreads) {
+      const int r = c / CH, cc = c % CH;
+      if (own_new && base + r == pos) continue;
+      const long long src = (long long)(base + r) * kvs + (long long)g * HD + cc * 8;
+      cp_async16(kd + r * HD + cc * 8, p.kc + src);
+      cp_async16(vd + r * HD + cc * 8, p.vc + src);
+    }
+    cp_async_commit();
+  };
+  // the query heads of KV head g, this lane's dims (loads in flight while the first tile's
+  // copies are issued), then rotated (RoPE of the fused one-token path)
   const float* qrow = p.q + (long long)row * p.q_stride;
-  for (int i = threadIdx.x; i < hpk * HD; i += kAttnThreads) qs[i] = qrow[(long long)(g * hpk) * HD + i];
+  float q[HB][D];
+#pragma unroll
+  for (int j = 0; j < HB; ++j)
+#pragma unroll
+    for (int d = 0; d < D; ++d) q[j][d] = j < hpk ? qrow[(long long)(g * hpk + j) * HD + D * lane + d] : 0.f;
+  if (n_tiles > 0) issue(0);
+  if (p.fused && pos_ok) {
+#pragma unroll
+    for (int pp = 0; pp < D / 2; ++pp) {
+      const int pair = (D * lane) / 2 + pp;
+      if (pair < p.rope_pairs) {
+        float cs, ss;
+        rope_cs(pos, p.base_freq[pair], pair < p.n_factors ? p.factors[pair] : 1.0f, p.attn_factor, cs, ss);
+#pragma unroll
+        for (int j = 0; j < HB; ++j)
+          if (j < hpk) rope_apply(q[j][2 * pp], q[j][2 * pp + 1], cs, ss);
+      }
+    }
+  }
   // the CTA whose positions end at `pos` stores the token's K (rotated) and V row of KV
-  // head g into the caches, and keeps them in shared memory for its own last tile (the
-  // bulk reads skip that row)
+  // head g into the caches and keeps them for its last tile (the bulk reads skip that row)
   if (own_new) {
     const float* kr = qrow + (long long)p.nh * HD + (long long)g * HD;
     const float* vr = kr + kvs;
@@ -276,198 +327,215 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
       *reinterpret_cast<__half2*>(knew + 2 * i) = k2;
       *reinterpret_cast<__half2*>(vnew + 2 * i) = v2;
     }
-  }
-  __syncthreads();
-  if (p.fused && pos_ok) {
-    // RoPE of this cluster's query heads (every CTA of the cluster, in shared memory)
-    for (int i = threadIdx.x; i < hpk * p.rope_pairs; i += kAttnThreads) {
-      const int j = i / p.rope_pairs, q2 = i % p.rope_pairs;
-      float x0 = qs[j * HD + 2 * q2], x1 = qs[j * HD + 2 * q2 + 1];
-      rope_pair(x0, x1, pos, p.base_freq[q2], q2 < p.n_factors ? p.factors[q2] : 1.0f, p.attn_factor);
-      qs[j * HD + 2 * q2] = x0;
-      qs[j * HD + 2 * q2 + 1] = x1;
-    }
+    __syncthreads();  // (own_new is uniform over the CTA)
   }
 
-  const int n_tiles = (t1 - t0 + kTile - 1) / kTile;
-  auto issue = [&](int tile) {
-    const int base = t0 + tile * kTile, nrows = min(kTile, t1 - base);
-    __half* kd = kt + (tile & 1) * kTile * HD;
-    __half* vd = vt + (tile & 1) * kTile * HD;
-    for (int c = threadIdx.x; c < nrows * CH; c += kAttnThreads) {
-      const int r = c / CH, cc = c % CH;
-      if (own_new && base + r == pos) continue;
-      const long long src = (long long)(base + r) * kvs + (long long)g * HD + cc * 8;
-      cp_async16(kd + r * HD + cc * 8, p.kc + src);
-      cp_async16(vd + r * HD + cc * 8, p.vc + src);
-    }
-    cp_async_commit();
-  };
-  if (n_tiles > 0) issue(0);
-
-  // per-thread state: the query slice of the score lanes, and the running softmax /
-  // accumulator of the PV threads (dims 2dp, 2dp+1 of every head, positions = grp mod GROUPS)
-  const int sub = lane / LPK, kl = lane % LPK;
-  const int grp = threadIdx.x / PAIRS, dp = threadIdx.x % PAIRS;
-  float a0[kMaxHpk], a1[kMaxHpk];
+  float m[HB], l[HB], acc[HB][D];
 #pragma unroll
-  for (int j = 0; j < kMaxHpk; ++j) a0[j] = a1[j] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;  // warp j < hpk owns head j's running max / sum
-  __syncthreads();
-  float qr[kMaxHpk][8];
+  for (int j = 0; j < HB; ++j) {
+    m[j] = -INFINITY;
+    l[j] = 0.f;
 #pragma unroll
-  for (int j = 0; j < kMaxHpk; ++j)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qr[j][e] = j < hpk ? qs[j * HD + kl * 8 + e] : 0.f;
+    for (int d = 0; d < D; ++d) acc[j][d] = 0.f;
+  }
+  const int my_j = lane / R, my_r = lane % R;  // the (head, row) this lane scores after the transpose
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     if (tile + 1 < n_tiles) {
+      __syncthreads();  // every warp is done with the buffer the next tile overwrites
       issue(tile + 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();
-    const int nrows = min(kTile, t1 - (t0 + tile * kTile));
-    const __half* kb = kt + (tile & 1) * kTile * HD;
-    const __half* vb = vt + (tile & 1) * kTile * HD;
+    const int base = t0 + tile * kTile, nrows = min(kTile, t1 - base);
+    __half* kb = kt + (tile & 1) * kTile * HD;
+    __half* vb = vt + (tile & 1) * kTile * HD;
     if (own_new && tile == n_tiles - 1) {  // the new row is the last one of the CTA
-      const int r = pos - (t0 + tile * kTile);
+      const int r = pos - base;
       for (int c = threadIdx.x; c < 2 * CH; c += kAttnThreads) {
         const int cc = c % CH;
-        __half* dst = (c < CH ? kt : vt) + (tile & 1) * kTile * HD + r * HD + cc * 8;
+        __half* dst = (c < CH ? kb : vb) + r * HD + cc * 8;
         *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>((c < CH ? knew : vnew) + cc * 8);
       }
-      __syncthreads();
     }
-    // ---- scores of the tile: LPK lanes per key, 8 dims per lane
-    for (int kb0 = warp * KPW; kb0 < nrows; kb0 += NW * KPW) {
-      const int k = kb0 + sub;
-      float kf[8];
-      if (k < nrows) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(kb + k * HD + kl * 8);
-        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+    __syncthreads();  // the tile (and the new row) is visible to every warp
+    for (int r0 = warp * R; r0 < nrows; r0 += NW * R) {
+      // partial dot products of this lane's dims: s[j*R + rr]
+      float s[HB * R];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(h2[e]);
-          kf[2 * e] = f.x;
-          kf[2 * e + 1] = f.y;
+      for (int rr = 0; rr < R; ++rr) {
+        const int r = r0 + rr;
+        float kf[D];
+        if (r < nrows) {
+          const __half2* k2 = reinterpret_cast<const __half2*>(kb + r * HD + D * lane);
+#pragma unroll
+          for (int e = 0; e < D / 2; ++e) {
+            const float2 f = __half22float2(k2[e]);
+            kf[2 * e] = f.x;
+            kf[2 * e + 1] = f.y;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < D; ++e) kf[e] = 0.f;
         }
-      } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) kf[e] = 0.f;
-      }
-#pragma unroll
-      for (int j = 0; j < kMaxHpk; ++j) {
-        if (j < hpk) {
+        for (int j = 0; j < HB; ++j) {
           float dot = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) dot = fmaf(qr[j][e], kf[e], dot);
-#pragma unroll
-          for (int o = LPK / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-          if (kl == 0 && k < nrows) pr[j * kTile + k] = dot * p.scale;
-        }
-      }
-    }
-    __syncthreads();
-    // ---- online softmax: warp j updates head j's running max / sum, writes the tile's
-    // probabilities and the accumulator's rescale factor
-    for (int j = warp; j < hpk; j += NW) {
-      float m = -INFINITY;
-      for (int i = lane; i < nrows; i += 32) m = fmaxf(m, pr[j * kTile + i]);
-      m = fmaxf(warp_max(m), m_run);
-      float l = 0.f;
-      for (int i = lane; i < nrows; i += 32) {
-        const float e = expf(pr[j * kTile + i] - m);
-        pr[j * kTile + i] = e;
-        l += e;
-      }
-      l = warp_sum(l);
-      const float sc = m_run == -INFINITY ? 0.f : expf(m_run - m);
-      l_run = l_run * sc + l;
-      m_run = m;
-      if (lane == 0) alpha[j] = sc;
-    }
-    __syncthreads();
-    // ---- weighted V of the tile
-    {
-#pragma unroll
-      for (int j = 0; j < kMaxHpk; ++j) {
-        if (j < hpk) {
-          const float sc = alpha[j];
-          a0[j] *= sc;
-          a1[j] *= sc;
-        }
-      }
-      for (int k = grp; k < nrows; k += GROUPS) {
-        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(vb + k * HD + 2 * dp));
-#pragma unroll
-        for (int j = 0; j < kMaxHpk; ++j) {
           if (j < hpk) {
-            const float w = pr[j * kTile + k];
-            a0[j] = fmaf(w, v.x, a0[j]);
-            a1[j] = fmaf(w, v.y, a1[j]);
+#pragma unroll
+            for (int e = 0; e < D; ++e) dot = fmaf(q[j][e], kf[e], dot);
+          }
+          s[j * R + rr] = dot;
+        }
+      }
+      // transpose reduction: afterwards s[0] of lane i is the full dot of (i / R, i % R)
+#pragma unroll
+      for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+          const float send = up ? s[i] : s[i + n / 2];
+          const float keep = up ? s[i + n / 2] : s[i];
+          s[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      const bool valid = my_j < hpk && r0 + my_r < nrows;
+      const float sc = valid ? s[0] * p.scale : -INFINITY;
+      // the step's max per head over its R lanes, the new running max and the rescale
+      float mx = sc;
+#pragma unroll
+      for (int o = R / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float m_old = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < HB; ++j)
+        if (j == my_j) m_old = m[j];
+      const float m_new = fmaxf(m_old, mx);
+      const float pr = valid ? expf(sc - m_new) : 0.f;
+      const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+      float ps = pr;
+#pragma unroll
+      for (int o = R / 2; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      // every lane: the heads' rescale, running max and sum, then the weighted V rows
+#pragma unroll
+      for (int j = 0; j < HB; ++j) {
+        if (j < hpk) {
+          const float a = __shfl_sync(0xffffffffu, alpha, j * R);
+          m[j] = __shfl_sync(0xffffffffu, m_new, j * R);
+          l[j] = fmaf(l[j], a, __shfl_sync(0xffffffffu, ps, j * R));
+#pragma unroll
+          for (int d = 0; d < D; ++d) acc[j][d] *= a;
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < R; ++rr) {
+        const int r = r0 + rr;
+        if (r < nrows) {
+          float vf[D];
+          const __half2* v2 = reinterpret_cast<const __half2*>(vb + r * HD + D * lane);
+#pragma unroll
+          for (int e = 0; e < D / 2; ++e) {
+            const float2 f = __half22float2(v2[e]);
+            vf[2 * e] = f.x;
+            vf[2 * e + 1] = f.y;
+          }
+#pragma unroll
+          for (int j = 0; j < HB; ++j) {
+            if (j < hpk) {
+              const float w = __shfl_sync(0xffffffffu, pr, j * R + rr);
+#pragma unroll
+              for (int d = 0; d < D; ++d) acc[j][d] = fmaf(w, vf[d], acc[j][d]);
+            }
           }
         }
       }
     }
-    __syncthreads();  // the buffer and the probabilities are rewritten next tile
   }
-  for (int j = warp; j < hpk; j += NW)
-    if (lane == 0) {
-      pmax[j] = m_run;
-      psum[j] = l_run;
-    }
+
+  // ---- the warps' partials, merged in warp order into the CTA's (max, sum, accumulator)
 #pragma unroll
-  for (int j = 0; j < kMaxHpk; ++j) {
+  for (int j = 0; j < HB; ++j) {
     if (j < hpk) {
-      red[(grp * hpk + j) * HD + 2 * dp] = a0[j];
-      red[(grp * hpk + j) * HD + 2 * dp + 1] = a1[j];
+      if (lane == 0) {
+        wm[warp * HB + j] = m[j];
+        wl[warp * HB + j] = l[j];
+      }
+#pragma unroll
+      for (int d = 0; d < D; ++d) wacc[(warp * hpk + j) * HD + D * lane + d] = acc[j][d];
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < hpk * HD; i += kAttnThreads) {
-    float s = 0.f;
+  // merge weights exp(m_w - M) of every (head, warp), one per thread
+  if (threadIdx.x < hpk * NW) {
+    const int j = threadIdx.x / NW, w = threadIdx.x % NW;
+    float M = -INFINITY;
 #pragma unroll
-    for (int gi = 0; gi < GROUPS; ++gi) s += red[gi * hpk * HD + i];
-    pacc[i] = s;
+    for (int w2 = 0; w2 < NW; ++w2) M = fmaxf(M, wm[w2 * HB + j]);
+    ww[w * HB + j] = wm[w * HB + j] == -INFINITY ? 0.f : expf(wm[w * HB + j] - M);
+    if (w == 0) pmax[j] = M;
+  }
+  __syncthreads();
+  if (threadIdx.x < hpk) {
+    const int j = threadIdx.x;
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) L = fmaf(ww[w * HB + j], wl[w * HB + j], L);
+    psum[j] = L;
+  }
+  for (int i = threadIdx.x; i < hpk * HD; i += kAttnThreads) {
+    const int j = i / HD;
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) a = fmaf(ww[w * HB + j], wacc[w * hpk * HD + i], a);
+    pacc[i] = a;
   }
 
-  // ---- merge the splits' partials over distributed shared memory, in split order
+  // ---- merge the splits' partials over distributed shared memory, in split order. Element
+  // i of the hpk*HD outputs is merged by CTA i / share. Every CTA pushes its maxima and sums
+  // to every CTA of the cluster and its accumulator elements to the CTA that merges them
+  // (remote stores, no round trip); the cluster barrier publishes them, and the merge then
+  // reads only its own shared memory. Nothing is read remotely after the barrier, so no
+  // second barrier holds the CTAs.
+  const int S = p.splits;
+  const int tot = hpk * HD;
+  const int share = (tot + S - 1) / S;
+  __syncthreads();  // the CTA's partial is complete
+  for (int t = threadIdx.x; t < S * hpk; t += kAttnThreads) {
+    const int dst = t / hpk, j = t % hpk;
+    st_dsmem_f32(rm + split * HB + j, (uint32_t)dst, pmax[j]);
+    st_dsmem_f32(rl + split * HB + j, (uint32_t)dst, psum[j]);
+  }
+  for (int i = threadIdx.x; i < tot; i += kAttnThreads)
+    st_dsmem_f32(racc + split * share + i % share, (uint32_t)(i / share), pacc[i]);
   cluster_barrier();
   if (pos_ok) {
-    const int tot = hpk * HD;
-    const int share = (tot + p.splits - 1) / p.splits;
+    // weights exp(m_s - M) of every (head, split), the sums in split order, then this CTA's
+    // elements (the warp accumulators are free again: they hold the weights)
+    float* sw = wacc;               // [HB][kMaxSplits]
+    float* sL = sw + HB * kMaxSplits;
+    if (threadIdx.x < hpk * S) {
+      const int j = threadIdx.x / S, s2 = threadIdx.x % S;
+      float M = -INFINITY;
+      for (int t = 0; t < S; ++t) M = fmaxf(M, rm[t * HB + j]);
+      const float mv = rm[s2 * HB + j];
+      sw[j * kMaxSplits + s2] = mv == -INFINITY ? 0.f : expf(mv - M);
+    }
+    __syncthreads();
+    if (threadIdx.x < hpk) {
+      const int j = threadIdx.x;
+      float L = 0.f;
+      for (int t = 0; t < S; ++t) L = fmaf(sw[j * kMaxSplits + t], rl[t * HB + j], L);
+      sL[j] = L;
+    }
+    __syncthreads();
     const int i0 = split * share, i1 = min(tot, i0 + share);
     for (int i = i0 + threadIdx.x; i < i1; i += kAttnThreads) {
       const int j = i / HD;
-      // all remote loads of the element first (independent), then the sums in split order
-      float ms[kMaxSplits], ls[kMaxSplits], as[kMaxSplits];
-#pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s) {
-        if (s < p.splits) {
-          ms[s] = ld_dsmem_f32(pmax + j, (uint32_t)s);
-          ls[s] = ld_dsmem_f32(psum + j, (uint32_t)s);
-          as[s] = ld_dsmem_f32(pacc + i, (uint32_t)s);
-        }
-      }
-      float m = -INFINITY;
-#pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s)
-        if (s < p.splits) m = fmaxf(m, ms[s]);
-      float l = 0.f, o = 0.f;
-#pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s) {
-        if (s < p.splits) {
-          const float w = ms[s] == -INFINITY ? 0.f : expf(ms[s] - m);
-          l = fmaf(w, ls[s], l);
-          o = fmaf(w, as[s], o);
-        }
-      }
-      p.out[(long long)row * p.nh * HD + (long long)g * hpk * HD + i] = o / l;
+      float o = 0.f;
+      for (int t = 0; t < S; ++t) o = fmaf(sw[j * kMaxSplits + t], racc[t * share + (i - i0)], o);
+      p.out[(long long)row * p.nh * HD + (long long)g * hpk * HD + i] = o / sL[j];
     }
   }
-  cluster_barrier();
 }
 
 __global__ void pos_advance_kernel(int* d_pos, int delta) {
@@ -476,11 +544,15 @@ __global__ void pos_advance_kernel(int* d_pos, int delta) {
   if (threadIdx.x == 0) *d_pos += delta;
 }
 
+// Query heads per KV head the kernel variant is built for (registers per lane scale with it).
+int attn_hb(int hpk) { return hpk <= 4 ? 4 : 8; }
+
 int attn_smem_bytes(int hd, int hpk) {
-  const int groups = kAttnThreads / (hd / 2);
+  constexpr int NW = kAttnThreads / 32;
+  const int hb = attn_hb(hpk);
   const int tile = 8192 / hd;
-  return 2 * 2 * 2 * tile * hd + 2 * 2 * hd +
-         4 * (hpk * hd + hpk * tile + kMaxHpk + groups * hpk * hd + hpk * hd + 2 * hpk);
+  return 2 * 2 * 2 * tile * hd + 4 * (3 * NW * hb + NW * hpk * hd + hpk * hd + 2 * hb) + 2 * 2 * hd +
+         4 * (2 * kMaxSplits * hb + hpk * hd + kMaxSplits);
 }
 
 }  // namespace
@@ -523,20 +595,25 @@ cudaError_t launch_attention_f16kv(const LaunchEnv& env, const float* q, long lo
   p.splits = attn_splits(seq_max);
   p.scale = 1.0f / sqrtf((float)hd);
   p.err = env.d_err;
+  if (p.hpk < 1 || p.hpk > kMaxHpk) return cudaErrorInvalidValue;
   const int smem = attn_smem_bytes(hd, p.hpk);
+  const int hb = attn_hb(p.hpk);
   void (*kern)(AttnParams) = nullptr;
   int hi;
-  switch (hd) {
-    case 64: kern = attention_kernel<64>; hi = 0; break;
-    case 128: kern = attention_kernel<128>; hi = 1; break;
-    case 256: kern = attention_kernel<256>; hi = 2; break;
+  switch (hd * 16 + hb) {
+    case 64 * 16 + 4: kern = attention_kernel<64, 4>; hi = 0; break;
+    case 64 * 16 + 8: kern = attention_kernel<64, 8>; hi = 1; break;
+    case 128 * 16 + 4: kern = attention_kernel<128, 4>; hi = 2; break;
+    case 128 * 16 + 8: kern = attention_kernel<128, 8>; hi = 3; break;
+    case 256 * 16 + 4: kern = attention_kernel<256, 4>; hi = 4; break;
+    case 256 * 16 + 8: kern = attention_kernel<256, 8>; hi = 5; break;
     default: return cudaErrorInvalidValue;
   }
   // Kernel attributes and the cluster-size check are done once per kernel and split count
   // (the largest shared-memory size, 8 query heads per KV head, covers every launch).
   static std::mutex mu;
-  static int dev_ready[8][3] = {};           // per device: attributes set
-  static int8_t fits[8][3][kMaxSplits + 1];  // per device: 0 unknown, 1 fits, -1 does not
+  static int dev_ready[8][6] = {};           // per device: attributes set
+  static int8_t fits[8][6][kMaxSplits + 1];  // per device: 0 unknown, 1 fits, -1 does not
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
