@@ -21,13 +21,18 @@
 // each output in a fixed order (deterministic).
 //
 // One CTA (persistent, one per SM) takes 128-row tiles of W x TN-token tiles of X in turn,
-// through a ring of stages [W | Ws | X | Xs], one 32-wide K chunk each:
+// through a ring of stages [W | X | Xs] in shared memory plus a 32-column Ws stage in
+// tensor memory, one 32-wide K chunk each:
 //   warp 0     TMA producer: per chunk one box of W (128 rows x 128 bytes) and one of X
 //              (TN rows x 128 bytes), both with the 128-byte swizzle;
-//   warps 2-5  split each chunk: Ws and Xs next to the raw values, elementwise on the
-//              swizzled bytes, so every part keeps the layout the MMA reads;
-//   warp 1     allocates TMEM (nbuf x nslot accumulator slots of 3·TN f32 columns); one thread issues the
-//              MMAs (kind::tf32, M = 128, K = 8) and tcgen05.commit's the three slots of a
+//   warps 2-5  split each chunk: Xs next to X, elementwise on the swizzled bytes (so it
+//              keeps the layout the MMA reads), and Ws into tensor memory: warp w reads the
+//              32 elements of each row of TMEM lane quarter w % 4 from the stage and stores
+//              their remainders with one tcgen05.st (Ws never passes through shared memory,
+//              which the copies, the split and the MMA operand reads otherwise saturate);
+//   warp 1     allocates TMEM (nbuf x nslot accumulator slots of 3·TN f32 columns, then
+//              the Ws stages); one thread issues the MMAs (kind::tf32, M = 128, K = 8;
+//              Ws·Xb with A from tensor memory) and tcgen05.commit's the three slots of a
 //              chunk back and each finished tile to the epilogue;
 //   warps 6-9  epilogue: tcgen05.ld of the partial columns, their sum, coalesced stores of
 //              Y (32 consecutive vocabulary rows per warp and token); with two accumulator
@@ -64,11 +69,12 @@ struct LgParams {
   int tn;                 // tokens per tile (multiple of 16, <= kMaxTokTile)
   int v_tiles, m_tiles, n_k;
   int stages;
-  uint32_t stage_bytes;   // [W 16 KB | Ws 16 KB | X tn*128 | Xs tn*128]
+  uint32_t stage_bytes;   // [W 16 KB | X tn*128 | Xs tn*128]
   uint32_t off_bar;
   uint32_t idesc_2n, idesc_n;
   uint32_t tmem_cols;
   int nbuf, nslot;        // accumulator sets (1 or 2) x K-step slots per set
+  uint32_t a_col0;        // TMEM column of the first Ws stage (32 columns per stage)
   int* err;
 };
 
@@ -152,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         mbar_arrive_expect_tx(&full[s], (uint32_t)kABytes + b_bytes);
         tma_load_2d(st, &wmap, k, vt * kRows, &full[s]);
-        tma_load_2d(st + 2 * kABytes, &xmap, k, mt * p.tn, &full[s]);
+        tma_load_2d(st + kABytes, &xmap, k, mt * p.tn, &full[s]);
       }
       __syncwarp();
       ++issued;
@@ -188,7 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t a = smem_addr(smem + (size_t)s * p.stage_bytes);
-          const uint32_t as = a + (uint32_t)kABytes, bx = a + 2u * (uint32_t)kABytes;
+          const uint32_t bx = a + (uint32_t)kABytes;
+          const uint32_t ta = tmem + p.a_col0 + 32u * (uint32_t)s;  // Ws of the stage
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk, ++step) {
             // slot j: [Wb·Xb | Wb·Xs] into its columns [0, 2tn), Ws·Xb into [2tn, 3tn)
@@ -196,8 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t d = dset + (uint32_t)j * slot_cols;
             const uint32_t acc = step >= p.nslot ? 1u : 0u;
             umma_tf32(d, sw128_desc(a + 32u * kk), sw128_desc(bx + 32u * kk), p.idesc_2n, acc);
-            umma_tf32(d + 2u * (uint32_t)p.tn, sw128_desc(as + 32u * kk), sw128_desc(bx + 32u * kk),
-                      p.idesc_n, acc);
+            umma_tf32_ta(d + 2u * (uint32_t)p.tn, ta + 8u * (uint32_t)kk, sw128_desc(bx + 32u * kk),
+                         p.idesc_n, acc);
           }
           umma_commit(&empty[s]);
         }
@@ -217,14 +224,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       uint8_t* st = smem + (size_t)s * p.stage_bytes;
-      const float4* A = reinterpret_cast<const float4*>(st);
-      float4* As = reinterpret_cast<float4*>(st + kABytes);
-#pragma unroll 4
-      for (int i = t; i < kABytes / 16; i += 128) split4(A + i, As + i);
-      const float4* B = reinterpret_cast<const float4*>(st + 2 * kABytes);
-      float4* Bs = reinterpret_cast<float4*>(st + 2 * kABytes + b_bytes);
+      // Ws: row r = 32*(warp % 4) + lane of the swizzled W box (16-byte chunk c at c ^ (r % 8))
+      {
+        const int r = 32 * (warp & 3) + lane;
+        uint32_t u[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 w = *reinterpret_cast<const float4*>(st + r * 128 + ((c ^ (r & 7)) << 4));
+          const float wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            u[4 * c + i] = __float_as_uint(
+                __fsub_rn(wv[i], __uint_as_float(__float_as_uint(wv[i]) & 0xFFFFE000u)));
+        }
+        tmem_st32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + p.a_col0 + 32u * (uint32_t)s, u);
+      }
+      const float4* B = reinterpret_cast<const float4*>(st + kABytes);
+      float4* Bs = reinterpret_cast<float4*>(st + kABytes + b_bytes);
       for (int i = t; i < (int)(b_bytes / 16); i += 128) split4(B + i, Bs + i);
+      tmem_wait_st();
       fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's async proxy
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ready[s]);
     }
@@ -300,19 +320,24 @@ cudaError_t launch_logits_tc(const LaunchEnv& env, const float* W, const float* 
   p.tn = ((M + p.m_tiles - 1) / p.m_tiles + 15) / 16 * 16;
   p.v_tiles = (V + kRows - 1) / kRows;
   p.n_k = (K + kBK - 1) / kBK;
-  p.stage_bytes = 2u * kABytes + 2u * (uint32_t)p.tn * 128u;
+  p.stage_bytes = (uint32_t)kABytes + 2u * (uint32_t)p.tn * 128u;
   const int bar_bytes = 256;
-  p.stages = std::min(kMaxStages, (kSmemBudget - 1024 - bar_bytes) / (int)p.stage_bytes);
+  const int smem_stages = std::min(kMaxStages, (kSmemBudget - 1024 - bar_bytes) / (int)p.stage_bytes);
+  // TMEM (512 columns): nbuf sets of nslot slots of 3·tn accumulator columns, then one
+  // 32-column Ws stage per ring stage. Two sets (the epilogue of a tile overlaps the next
+  // tile's MMAs) when four stages still fit beside them, else one set and more stages.
+  // (At 64 tokens, one set of two slots instead of two sets of one measured 835 against
+  // 815 µs for the step's logits.)
+  const int slot = 3 * p.tn;
+  p.nbuf = (512 - 2 * slot) / 32 >= 4 ? 2 : 1;
+  p.stages = std::min(smem_stages, (512 - p.nbuf * slot) / 32);
   if (p.stages < 2) return cudaErrorInvalidValue;
+  p.nslot = std::max(1, std::min(4, (512 - 32 * p.stages) / (p.nbuf * slot)));
+  if (p.nbuf * p.nslot * slot + 32 * p.stages > 512) return cudaErrorInvalidValue;
+  p.a_col0 = (uint32_t)(p.nbuf * p.nslot * slot);
+  p.tmem_cols = 512;
   p.off_bar = (uint32_t)p.stages * p.stage_bytes;
   const int smem = (int)p.off_bar + bar_bytes + 1024;
-  // TMEM (512 columns): nbuf sets of nslot slots of 3·tn columns; two sets (the epilogue of
-  // a tile overlaps the next tile's MMAs) when at least two slots per set still fit
-  const int slot = 3 * p.tn;
-  p.nbuf = (512 / (2 * slot) >= 2) ? 2 : 1;
-  p.nslot = std::min(4, 512 / (p.nbuf * slot));
-  if (p.nslot < 1) return cudaErrorInvalidValue;
-  p.tmem_cols = 512;
   p.idesc_2n = tf32_idesc(2 * p.tn);
   p.idesc_n = tf32_idesc(p.tn);
   p.err = env.d_err;
