@@ -9,7 +9,10 @@
 // rrr_batch mirrors the prebuilt table of pre_allocate_desc_set +
 // dispatch_batch_persistent_v2 (engine.rs:244-268, 317-370; built at phi4.rs:969-1064):
 // the recorded dispatches are captured once into a CUDA graph and replayed with one
-// launch. Stream order replaces the reference's explicit pipeline barriers.
+// launch. Stream order replaces the reference's explicit pipeline barriers. A single-token
+// GEMV dispatch whose input no earlier dispatch of the table writes prepares that input
+// before its grid dependency wait (the kernel writes its rows only after it), so the
+// preparation overlaps the tail of the dispatch before it.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -262,11 +265,42 @@ int rrr_batch_launch(rrr_batch* bt, void* stream) {
     cudaError_t e = cudaStreamBeginCapture(bt->capture_stream, cudaStreamCaptureModeRelaxed);
     if (e != cudaSuccess) return cuda_error(ctx, e, "rrr_batch_launch: begin capture");
     int first_rc = RRR_OK;
+    // byte ranges written by the dispatches so far (a single-token GEMV writes its output
+    // binding; every binding of any other dispatch counts as written)
+    std::vector<std::pair<const char*, const char*>> written;
+    auto overlaps = [&](const void* p, uint64_t n) {
+      const char* a = static_cast<const char*>(p);
+      for (const auto& w : written)
+        if (a < w.second && w.first < a + n) return true;
+      return false;
+    };
     for (const Op& op : bt->ops) {
+      bool batch = false;
+      const int qt = kq_from_name(op.name, &batch);
+      const uint32_t K = qt && !batch ? push_u32(op.push.data(), 0) : 0;
+      const uint32_t N = qt && !batch ? push_u32(op.push.data(), 1) : 0;
+      if (qt && !batch &&
+          check_gemv(ctx, qt, op.bufs[1], static_cast<const float*>(op.bufs[0]),
+                     static_cast<float*>(op.bufs[2]), (int)K, (int)N, nullptr, nullptr, false) == RRR_OK) {
+        const bool early = !overlaps(op.bufs[0], 4ull * K);
+        cudaError_t e2 = launch_gemv_kq(make_env(ctx, bt->capture_stream), qt, op.bufs[1],
+                                        static_cast<const float*>(op.bufs[0]),
+                                        static_cast<float*>(op.bufs[2]), (int)K, (int)N, nullptr,
+                                        nullptr, nullptr, early);
+        if (e2 == cudaSuccess) e2 = cudaGetLastError();
+        if (e2 != cudaSuccess && !first_rc) first_rc = cuda_error(ctx, e2, "rrr_batch_launch: GEMV");
+        const char* y = static_cast<const char*>(op.bufs[2]);
+        written.emplace_back(y, y + 4ull * N);
+        continue;
+      }
       rc = run_named(ctx, op.name.c_str(), op.bufs.data(), op.sizes.data(), (int)op.bufs.size(),
                      op.push.empty() ? nullptr : op.push.data(), (int)op.push.size(),
                      bt->capture_stream, true);
       if (rc && !first_rc) first_rc = rc;
+      for (size_t i = 0; i < op.bufs.size(); ++i) {
+        const char* b = static_cast<const char*>(op.bufs[i]);
+        written.emplace_back(b, b + op.sizes[i]);
+      }
     }
     cudaGraph_t g = nullptr;
     e = cudaStreamEndCapture(bt->capture_stream, &g);

@@ -75,6 +75,7 @@ struct GemvParams {
   unsigned long long* push[kMaxTpRanks];
   int G;
   const unsigned* epoch;
+  int x_early;  // prepare x before the grid dependency wait (x not written by overlapping kernels)
   // timeline records of this launch (rrr_set_trace; null: off): 8 u64 per CTA
   unsigned long long* trace;
   unsigned long long trace_tag;  // launch sequence number << 16
@@ -882,14 +883,24 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_kq_kernel(const GemvP
     return;
   }
 
-  pdl_wait();
-  if (tr && threadIdx.x == 0) tr[2] = globaltimer_ns();
-  // fused exchange: this step's epoch, and whether this rank still feeds its peers (no
-  // error recorded by an earlier kernel, e.g. a wait that ran out)
+  // An input that no overlapping kernel writes (x_early) is prepared while the preceding
+  // grid drains; otherwise after the grid dependency wait. One copy of the preparation code
+  // either way: only the wait moves.
+  if (!p.x_early) {
+    pdl_wait();
+    if (tr && threadIdx.x == 0) tr[2] = globaltimer_ns();
+  }
+  // fused exchange (never x_early): this step's epoch
   const unsigned tag = p.G ? *p.epoch + 1u : 0u;
-  const bool feed = p.push[0] && *reinterpret_cast<volatile int*>(p.err) == 0;
   const float inv_rms = prepare_item<FRAG>(p, g, warp, lane, tag);
   if (tr && threadIdx.x == 0) tr[3] = globaltimer_ns();
+  if (p.x_early) {
+    pdl_wait();
+    if (tr && threadIdx.x == 0) tr[2] = globaltimer_ns();
+  }
+  // whether this rank still feeds its peers (no error recorded by an earlier kernel, e.g. a
+  // wait that ran out)
+  const bool feed = p.push[0] && *reinterpret_cast<volatile int*>(p.err) == 0;
   consume_item<QT, FRAG>(p, g, vb, vstride, warp % kNW, lane, inv_rms, tag, feed, rp);
   if (tr) {
     named_barrier(1, kGroups * kNW * 32);
@@ -1035,6 +1046,8 @@ void fill_params(GemvParams& p, const GemvDesc& d) {
   p.k_off = d.pro.mode == RRR_X_GQA_V ? d.pro.k_offset : 0;
   p.K = d.K;
   p.N = d.swiglu ? 2 * d.N : d.N;
+  // (the ranks' rows of a fused exchange arrive during the grid, never early)
+  p.x_early = d.x_early && d.fuse.G < 1 ? 1 : 0;
   if (d.fuse.G >= 1) {
     p.sum_in = d.fuse.sum_in;
     p.h_out = d.fuse.h_out;
@@ -1077,7 +1090,7 @@ __global__ void mma_selftest_kernel(int* ok) {
 
 cudaError_t launch_gemv_kq(const LaunchEnv& env, int qtype, const void* w, const float* x,
                            float* y, int K, int N, const float* residual,
-                           const rrr_gemv_prologue* pro, const GemvFuse* fuse) {
+                           const rrr_gemv_prologue* pro, const GemvFuse* fuse, bool x_early) {
   GemvDesc d;
   d.qtype = qtype;
   d.w = w;
@@ -1088,6 +1101,7 @@ cudaError_t launch_gemv_kq(const LaunchEnv& env, int qtype, const void* w, const
   d.residual = residual;
   if (pro) d.pro = *pro;
   if (fuse) d.fuse = *fuse;
+  d.x_early = x_early;
   GemvParams p = {};
   fill_params(p, d);
   return launch_any(env, qtype, p);

@@ -47,9 +47,14 @@ struct GemvFuse {
   const unsigned* epoch = nullptr;
 };
 
+// x_early: the input is not written by any kernel this launch can overlap under
+// programmatic dependent launch (e.g. a prebuilt table in which no earlier dispatch writes
+// it), so the CTAs prepare it before the grid dependency wait; the rows are still stored
+// after it.
 cudaError_t launch_gemv_kq(const LaunchEnv& env, int qtype, const void* w, const float* x,
                            float* y, int K, int N, const float* residual,
-                           const rrr_gemv_prologue* pro, const GemvFuse* fuse = nullptr);
+                           const rrr_gemv_prologue* pro, const GemvFuse* fuse = nullptr,
+                           bool x_early = false);
 
 // One GEMV: the arguments of launch_gemv_kq (swiglu: of launch_gemv_kq_swiglu, N = F output
 // rows of a 2F-row weight).
@@ -63,6 +68,7 @@ struct GemvDesc {
   rrr_gemv_prologue pro{};  // mode RRR_X_PLAIN
   bool swiglu = false;
   GemvFuse fuse;            // G = 0: no fused exchange
+  bool x_early = false;     // see launch_gemv_kq
 };
 // GEMV with a bf16 input vector (one token of the batched path when M < 16).
 cudaError_t launch_gemv_kq_bf16(const LaunchEnv& env, int qtype, const void* w,

@@ -354,8 +354,9 @@ def test_prebuilt_table_dependent_gemvs(rrr, ctx, oracle, G):
     """A prebuilt table of consecutive matmul_q{4,5,6}k dispatches where each GEMV reads what
     the previous one wrote (stream order is the reference's barrier after each dispatch): a
     dependent run of mixed quant types with K up to 4096 and a ragged row count, an rmsnorm
-    dispatch, then 70 more GEMVs; every output against the oracle applied to the device's
-    own inputs."""
+    dispatch, then 70 more GEMVs, some of whose inputs no dispatch writes (those prepare
+    their input before the grid dependency wait). Replayed twice with different inputs;
+    every output against the oracle applied to the device's own inputs."""
     eng = rrr.ComputeEngine.__new__(rrr.ComputeEngine)
     eng.ctx = ctx
     rng = np.random.default_rng(81)
@@ -403,20 +404,35 @@ def test_prebuilt_table_dependent_gemvs(rrr, ctx, oracle, G):
             odd[j], w = weight(12, 3072, 256)
             tbl.add(*rrr.kquant_dispatch(bx, w, out, rrr.QType(12), 3072, 256)[:4])
         many.append(out)
-    for _ in range(2):
-        tbl.launch()
-        eng.sync()
-    assert ctx.device_error() == 0
     host = lambda b, n: (lambda a: (eng.download(b, a), a)[1])(np.empty(n, np.float32))
-    for i, (qt, K, N) in enumerate(spec):
-        xi = x0 if i == 0 else host(ins[i], K)
-        assert rel_l2(host(outs[i], N), oracle.gemv_kq(qt, raws[i], xi, K, N)) < TOL, i
-    normed = host(bn, 512)
-    assert rel_l2(normed, oracle.rms_norm(host(outs[4], 512), gam, 1e-5)) < 1e-6
-    ref5 = oracle.gemv_kq(13, raw5, normed, 512, 256)
-    for j in range(70):
-        ref = ref5 if j % 2 == 0 else oracle.gemv_kq(12, odd[j], x0, 3072, 256)
-        assert rel_l2(host(many[j], 256), ref) < TOL, j
+
+    def check(x_in):
+        for i, (qt, K, N) in enumerate(spec):
+            # stages 1-4 read the buffer an earlier stage wrote in this replay
+            xi = x_in if i == 0 else host(ins[i], K)
+            assert rel_l2(host(outs[i], N), oracle.gemv_kq(qt, raws[i], xi, K, N)) < TOL, i
+        normed = host(bn, 512)
+        assert rel_l2(normed, oracle.rms_norm(host(outs[4], 512), gam, 1e-5)) < 1e-6
+        ref5 = oracle.gemv_kq(13, raw5, normed, 512, 256)
+        for j in range(70):
+            ref = ref5 if j % 2 == 0 else oracle.gemv_kq(12, odd[j], x_in, 3072, 256)
+            assert rel_l2(host(many[j], 256), ref) < TOL, j
+
+    # replay, then replay again with a new input: every stage, the dependent ones included,
+    # must follow it (a stage that read its input before the preceding stage wrote it would
+    # still hold the first replay's values)
+    tbl.launch()
+    eng.sync()
+    assert ctx.device_error() == 0
+    check(x0)
+    first = host(outs[3], 1000)
+    x1 = rng.standard_normal(3072).astype(np.float32)
+    eng.upload(bx, x1)
+    tbl.launch()
+    eng.sync()
+    assert ctx.device_error() == 0
+    check(x1)
+    assert not np.array_equal(first, host(outs[3], 1000))
     tbl.close()
     for b in bufs:
         b.free()
