@@ -182,8 +182,17 @@ int rrr_gemm_kq_batched_ex(rrr_ctx* ctx, int qtype, const void* w_raw, const uin
  * rrr_gemm_kq_batched_ex's choice (mma.sync for 3 <= M <= 64 when every weight row is a
  * multiple of 16 bytes, tcgen05 for larger M or unaligned rows from M = 16, one GEMV per
  * token otherwise); the others force one kernel (mma.sync takes 1 <= M <= 64, tcgen05
- * M >= 16) and fail with RRR_ERR_BAD_SHAPE where it does not apply. */
-enum { RRR_GEMM_AUTO = 0, RRR_GEMM_TCGEN05 = 1, RRR_GEMM_MMA = 2, RRR_GEMM_PER_TOKEN = 3 };
+ * M >= 16) and fail with RRR_ERR_BAD_SHAPE where it does not apply. RRR_GEMM_MMA_I8 is
+ * the integer mma.sync kernel (raw quants against int8 digits of X, 1 <= M <= 64, rows of
+ * a multiple of 16 bytes); it prepares the digits in the context's scratch buffer, so two
+ * of its calls on one context must not run concurrently on different streams. */
+enum {
+  RRR_GEMM_AUTO = 0,
+  RRR_GEMM_TCGEN05 = 1,
+  RRR_GEMM_MMA = 2,
+  RRR_GEMM_PER_TOKEN = 3,
+  RRR_GEMM_MMA_I8 = 4
+};
 int rrr_gemm_kq_batched_path(rrr_ctx* ctx, int qtype, const void* w_raw, const uint16_t* x_bf16,
                              float* y, int M, int K, int N, const float* residual, int path,
                              void* stream);

@@ -208,9 +208,11 @@ int rrr_init(int device, rrr_ctx** out) {
     return cuda_error(nullptr, e, "rrr_init: cudaMalloc(error flag)");
   }
   cudaMemset(c->d_err, 0, 256);
-  e = cudaDeviceSynchronize();
+  e = cudaMalloc(&c->xdig, rrr::i8_scratch_bytes(rrr::kGemvMaxK));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     cudaFree(c->d_err);
+    if (c->xdig) cudaFree(c->xdig);
     delete c;
     return cuda_error(nullptr, e, "rrr_init: synchronize");
   }
@@ -223,6 +225,7 @@ int rrr_destroy(rrr_ctx* ctx) {
   bind_device(ctx);
   cudaDeviceSynchronize();
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->xdig) cudaFree(ctx->xdig);
   delete ctx;
   return RRR_OK;
 }
@@ -416,7 +419,7 @@ int rrr_gemm_kq_batched_ex(rrr_ctx* ctx, int qtype, const void* w, const uint16_
 int rrr_gemm_kq_batched_path(rrr_ctx* ctx, int qtype, const void* w, const uint16_t* x, float* y,
                              int M, int K, int N, const float* residual, int path, void* stream) {
   RRR_CHECK_CTX(ctx);
-  if (path < RRR_GEMM_AUTO || path > RRR_GEMM_PER_TOKEN)
+  if (path < RRR_GEMM_AUTO || path > RRR_GEMM_MMA_I8)
     return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemm_kq_batched_path: unknown path %d", path);
   int rc = check_qtype(ctx, qtype, "rrr_gemm_kq_batched");
   if (rc) return rc;
@@ -432,6 +435,16 @@ int rrr_gemm_kq_batched_path(rrr_ctx* ctx, int qtype, const void* w, const uint1
     return set_error(ctx, RRR_ERR_INVALID_ARG, "rrr_gemm_kq_batched: residual must equal Y or not overlap it");
   RRR_BIND(ctx);
   const LaunchEnv env = make_env(ctx, stream);
+  I8Plan iplan;
+  if (path == RRR_GEMM_MMA_I8) {
+    if (!plan_gemm_kq_i8(qtype, M, K, N, ctx->sm_count, &iplan))
+      return set_error(ctx, RRR_ERR_BAD_SHAPE,
+                       "rrr_gemm_kq_batched_path: the integer mma.sync kernel takes 1 <= M <= 64 "
+                       "and rows of a multiple of 16 bytes");
+    RRR_LAUNCH_CHECK(ctx, launch_gemm_kq_i8(env, qtype, w, x, y, M, K, N, iplan, residual, ctx->xdig),
+                     "rrr_gemm_kq_batched (integer mma.sync) launch");
+    return RRR_OK;
+  }
   MmaPlan mplan;
   // Automatic choice: the mma.sync kernel from 3 tokens (a 16-token tile with the rows past
   // M zero-filled by the X copy reads each weight once, where one GEMV per token reads the

@@ -17,6 +17,8 @@ struct rrr_ctx {
   // sequence number, assigned on the host at launch (or capture) time
   unsigned long long* trace = nullptr;
   int64_t trace_cap = 0, trace_next = 0, trace_seq = 0;
+  // int8 digits of the batched GEMM input (gemm_kq_i8.cu), i8_scratch_bytes(kGemvMaxK) bytes
+  void* xdig = nullptr;
   std::string last_error;
   void* argmax_scratch() { return reinterpret_cast<char*>(d_err) + 64; }
 };

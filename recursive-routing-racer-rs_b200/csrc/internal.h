@@ -144,6 +144,23 @@ cudaError_t launch_gemm_kq_mma(const LaunchEnv& env, int qtype, const void* w,
                                const uint16_t* x_bf16, float* y, int M, int K, int N,
                                const MmaPlan& plan, const float* residual);
 
+// Batched-token GEMM for 1 <= M <= 64 on integer mma.sync (gemm_kq_i8.cu): raw quants as
+// the A operand against int8 digits of X, which a preparation kernel writes into `scratch`
+// (i8_scratch_bytes(K) bytes; one GEMM at a time per scratch buffer, in stream order).
+struct I8Plan {
+  int tn;          // tokens per tile: M rounded up to 16
+  int m_tiles, n_tiles;
+  int splits;      // K splits = CTAs per cluster (1..8)
+  int stages, smem;
+  int kbs;         // super-blocks per stage
+};
+size_t i8_digit_bytes(int K);
+size_t i8_scratch_bytes(int K);
+bool plan_gemm_kq_i8(int qtype, int M, int K, int N, int sm_count, I8Plan* plan);
+cudaError_t launch_gemm_kq_i8(const LaunchEnv& env, int qtype, const void* w,
+                              const uint16_t* x_bf16, float* y, int M, int K, int N,
+                              const I8Plan& plan, const float* residual, void* scratch);
+
 // Decode attention at real positions (attention.cu).
 cudaError_t launch_rope_kv_store(const LaunchEnv& env, float* qkv, long long row_stride, int rows,
                                  int pos0, const int* d_pos, int nh, int nkv, int hd, int rope_dim,

@@ -65,7 +65,8 @@ def case_decode(ctx, L, torch, args):
 
 
 def case_gemm(ctx, L, torch, args):
-    """Batched GEMM, M = --m tokens, on gate_up Q4_K 16384x3072 and down Q6_K 3072x8192."""
+    """Batched GEMM, M = --m tokens, on gate_up Q4_K 16384x3072 and down Q6_K 3072x8192
+    (--path: RRR_GEMM_* kernel choice, 0 = automatic)."""
     shapes = [(12, 3072, 16384), (14, 8192, 3072)]
     bufs = []
     for qt, K, N in shapes:
@@ -75,8 +76,8 @@ def case_gemm(ctx, L, torch, args):
     torch.cuda.synchronize()
     for _ in range(args.rounds):
         for qt, K, N, w, x, y in bufs:
-            ctx.check(L.rrr_gemm_kq_batched(ctx.h, qt, c_void_p(w.data_ptr()), c_void_p(x.data_ptr()),
-                                            c_void_p(y.data_ptr()), args.m, K, N, None))
+            ctx.check(L.rrr_gemm_kq_batched_path(ctx.h, qt, c_void_p(w.data_ptr()), c_void_p(x.data_ptr()),
+                                                 c_void_p(y.data_ptr()), args.m, K, N, None, args.path, None))
 
 
 def case_attn(ctx, L, torch, args):
@@ -220,6 +221,7 @@ def main(argv=None):
     ap.add_argument("--pos", type=int, default=1024)
     ap.add_argument("--max-seq", type=int, default=0)
     ap.add_argument("--vocab", type=int, default=32768)
+    ap.add_argument("--path", type=int, default=0)
     args = ap.parse_args(argv)
     import torch
     rrr = importlib.import_module(_PKG)

@@ -456,7 +456,7 @@ def test_gemm_batched(rrr, ctx, oracle, G, qt, M):
         assert rel_l2(got[m], oracle.gemv_kq(qt, raw, Xf[m], K, N)) < 1e-2
 
 
-GEMM_TCGEN05, GEMM_MMA, GEMM_PER_TOKEN = 1, 2, 3   # RRR_GEMM_* of rrr_gemm_kq_batched_path
+GEMM_TCGEN05, GEMM_MMA, GEMM_PER_TOKEN, GEMM_MMA_I8 = 1, 2, 3, 4   # RRR_GEMM_* of rrr_gemm_kq_batched_path
 
 
 def _gemm_tc_case(rrr, ctx, oracle, G, qt, M, K, N, seed, repeats=1, path=GEMM_TCGEN05):
@@ -546,6 +546,54 @@ def test_gemm_mma(rrr, ctx, oracle, G, qt, M, K, N):
     assert np.array_equal(outs[1], got)
 
 
+@pytest.mark.parametrize("qt", QTYPES)
+@pytest.mark.parametrize("M,K,N", MMA_SHAPES)
+def test_gemm_mma_i8(rrr, ctx, oracle, G, qt, M, K, N):
+    """Integer mma.sync batched GEMM (raw quants against int8 digits of X, 16-token tiles) vs
+    the f32 product of the oracle's dequantised weights and the bf16 activations: within
+    1e-2 relative L2 per token row (north star) and 1e-3 over the whole output (the weights
+    are exact, X is represented to 2^-15 of its block maximum), repeat calls bit-identical."""
+    if (K // 256) * {12: 144, 13: 176, 14: 210}[qt] % 16:
+        pytest.skip("rows not a multiple of 16 bytes: the tcgen05 kernel serves this shape")
+    outs, ref = _gemm_tc_case(rrr, ctx, oracle, G, qt, M, K, N, seed=M * 5 + K + N + qt, repeats=2,
+                              path=GEMM_MMA_I8)
+    got = outs[0]
+    assert np.isfinite(got).all()
+    for m in range(M):
+        assert rel_l2(got[m], ref[m]) < 1e-2, (m, rel_l2(got[m], ref[m]))
+    assert rel_l2(got.ravel(), ref.ravel()) < 1e-3, rel_l2(got.ravel(), ref.ravel())
+    assert np.array_equal(outs[1], got)
+
+
+@pytest.mark.parametrize("qt", QTYPES)
+def test_gemm_mma_i8_residual_and_heavy_tails(rrr, ctx, oracle, G, qt):
+    """The integer kernel with the residual epilogue (Y = X W^T + R, R equal to Y) on inputs
+    with one 10^3x outlier per 256-block, and the tiles of a previous call's digits
+    overwritten by the next call (two shapes back to back on the stream)."""
+    import torch
+    L = rrr.ffi.lib()
+    rng = np.random.default_rng(77 + qt)
+    for M, K, N in ((24, 4096, 512), (7, 2048, 300)):
+        raw = oracle.random_blocks(qt, N * (K // 256), rng)
+        X = torch.randn(M, K, dtype=torch.float32)
+        for m in range(M):
+            for b in range(K // 256):
+                X[m, b * 256 + int(rng.integers(256))] = float(1e3 * rng.choice([-1.0, 1.0]))
+        X = X.to(torch.bfloat16)
+        R = rng.standard_normal((M, N)).astype(np.float32)
+        W = oracle.dequant(qt, raw, N * K).reshape(N, K).astype(np.float64)
+        ref = (X.float().numpy().astype(np.float64) @ W.T + R).astype(np.float32)
+        wd, xd = G.dev(raw), X.cuda()
+        Y = torch.from_numpy(R.copy()).cuda()
+        ctx.check(L.rrr_gemm_kq_batched_path(ctx.h, qt, vp(wd), vp(xd), vp(Y), M, K, N, vp(Y),
+                                             GEMM_MMA_I8, None))
+        got = G.host(Y).reshape(M, N)
+        assert ctx.device_error() == 0
+        for m in range(M):
+            assert rel_l2(got[m], ref[m]) < 1e-2, (M, m, rel_l2(got[m], ref[m]))
+        assert rel_l2(got.ravel(), ref.ravel()) < 1e-3
+
+
 def test_gemm_path_selection(rrr, ctx, oracle, G):
     """The mma.sync kernel rejects what it does not handle (M > 64, rows that are not a
     multiple of 16 bytes: Q6_K with K/256 not a multiple of 8); the tcgen05 kernel M < 16."""
@@ -558,6 +606,8 @@ def test_gemm_path_selection(rrr, ctx, oracle, G):
     assert L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 128, 768, 64, None, GEMM_MMA, None) == -3
     assert L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 8, 768, 64, None, GEMM_TCGEN05, None) == -3
     assert L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 8, 768, 64, None, 7, None) == -1
+    assert L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 32, 768, 64, None, GEMM_MMA_I8, None) == -3
+    assert L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 128, 768, 64, None, GEMM_MMA_I8, None) == -3
     # automatic choice still serves the Q6_K shape (tcgen05 with per-row copies)
     ctx.check(L.rrr_gemm_kq_batched_path(ctx.h, 14, vp(w), vp(x), vp(y), 32, 768, 64, None, 0, None))
     torch.cuda.synchronize()

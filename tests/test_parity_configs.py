@@ -31,7 +31,7 @@ tp = importlib.import_module("recursive-routing-racer-rs_b200.tp")
 
 TOL = 1e-4
 THREADS = max(1, min(32, os.cpu_count() or 1))
-GEMM_TCGEN05, GEMM_MMA = 1, 2
+GEMM_TCGEN05, GEMM_MMA, GEMM_MMA_I8 = 1, 2, 4
 LAYER_KEYS = (("qkv", "w_qkv", "qkv_type"), ("o_proj", "w_o", "o_type"),
               ("gate_up", "w_gate_up", "gate_up_type"), ("down", "w_down", "down_type"))
 
@@ -124,7 +124,7 @@ def test_gemm_configs3_full_shapes(rrr, ctx, oracle, name, qt, K, N):
         X = torch.randn(M, K, generator=gen).to(torch.bfloat16)
         ref = X.float().numpy().astype(np.float64) @ Wt
         xd = X.cuda()
-        paths = [0, GEMM_TCGEN05] + ([GEMM_MMA] if M <= 64 else [])
+        paths = [0, GEMM_TCGEN05] + ([GEMM_MMA, GEMM_MMA_I8] if M <= 64 else [])
         outs = {}
         for path in paths:
             reps = []
