@@ -643,9 +643,7 @@ cudaError_t launch_q(const LaunchEnv& env, const I8Plan& pl, const void* w, cons
   int8_t* dig = reinterpret_cast<int8_t*>(scratch);
   float* aux = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + i8_digit_bytes(K));
   auto kern = gemm_kq_i8_kernel<QT>;
-  // Tile shape: rows per CTA (16 per consumer warp) and K splits with the least work on
-  // the busiest SM, waves (resident clusters of each split count) x super-blocks per CTA
-  // x rows; ties go to more rows, then fewer splits.
+  // Tile shape: rows per CTA (16 per consumer warp) and K splits (choose_tile).
   const int qi = QT - RRR_Q4_K;
   cudaLaunchConfig_t cfg = {};
   cfg.stream = env.stream;
@@ -668,34 +666,26 @@ cudaError_t launch_q(const LaunchEnv& env, const I8Plan& pl, const void* w, cons
       best_ring = c.ring;
     }
   }
-  const bool cached = best_cw != 0;
-  if (!cached) {  // (first launch of this shape on this device)
+  if (best_cw == 0) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
     if (e != cudaSuccess) return e;
-  }
-  long long best_cost = -1;
-  for (int cw = kMaxCWarps; cw >= 4 && !cached; --cw) {
-    const int rows = cw * kWR;
-    const Ring rg = ring_for(QT, rows);
-    if (rg.stages == 0) continue;
-    const int base = pl.m_tiles * ((N + rows - 1) / rows);
-    cfg.blockDim = dim3((cw + 1) * 32);
-    cfg.dynamicSmemBytes = rg.smem;
-    int max_s = std::min(kMaxSplits, std::max(1, nb / 2));
-    for (int sp = 1; sp <= max_s; ++sp) {
-      const int fit = max_active_clusters((const void*)kern, cfg, sp);
-      if (fit < 1) continue;
-      const long long cost = (long long)((base + fit - 1) / fit) * ((nb + sp - 1) / sp) * rows;
-      if (best_cost < 0 || cost < best_cost) {
-        best_cost = cost;
-        best_cw = cw;
-        best_s = sp;
-        best_ring = rg;
-      }
+    TileCand cand[kMaxCWarps];
+    Ring rings[kMaxCWarps];
+    int cws[kMaxCWarps], nc = 0;
+    for (int cw = kMaxCWarps; cw >= 4; --cw) {
+      const Ring rg = ring_for(QT, cw * kWR);
+      if (rg.stages == 0) continue;
+      cand[nc] = TileCand{cw * kWR, (cw + 1) * 32, rg.smem};
+      rings[nc] = rg;
+      cws[nc++] = cw;
     }
-  }
-  if (best_cw == 0) return cudaErrorInvalidConfiguration;
-  if (best_cost >= 0) {
+    int sp = 1;
+    const int i = choose_tile((const void*)kern, env.stream, cand, nc, N, pl.m_tiles, nb,
+                              std::min(kMaxSplits, std::max(1, nb / 2)), env.sm_count, &sp);
+    if (i < 0) return cudaErrorInvalidConfiguration;
+    best_cw = cws[i];
+    best_s = sp;
+    best_ring = rings[i];
     Choice c{dev, N, nb, pl.m_tiles, best_cw, best_s, best_ring};
     if (n_chosen[qi] < 16) chosen[qi][n_chosen[qi]++] = c;
     else chosen[qi][(N + nb) % 16] = c;

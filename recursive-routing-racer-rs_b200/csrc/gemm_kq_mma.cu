@@ -47,14 +47,13 @@
 namespace rrr {
 namespace {
 
-constexpr int kRows = 256;            // weight rows per tile
+constexpr int kMaxRows = 256;         // weight rows per tile (at most; chosen per shape)
 // MT m16 tiles per consumer warp: 16 / MT consumer warps cover the 256 rows (MT = 1 for
 // TN <= 32: twice the warps to hide latency; MT = 2 for larger TN: half the X reads)
 template <int MT> constexpr int cwarps() { return 16 / MT; }
 template <int MT> constexpr int threads_for() { return (cwarps<MT>() + 1) * 32; }
 constexpr int kMaxTn = 64;
 constexpr int kMaxSplits = 8;         // portable cluster size
-constexpr int kPartStride = kRows + 4;  // floats per token row of the partial tile
 constexpr int kSmemBudget = 232448;   // 227 KB opt-in maximum on sm_100
 
 struct MmaParams {
@@ -62,8 +61,10 @@ struct MmaParams {
   const float* residual;  // optional [M, N] f32 added in the epilogue (may equal y)
   int M, N, nb, bb;       // nb super-blocks per row, bb bytes per super-block
   int tn, splits, stages, kbs, pitch;
-  uint32_t raw_bytes, stage_bytes;  // raw part of a stage (box bytes), whole stage
-  uint32_t off_tab;                 // scale table [kbs][kRows][subs + 1] float2
+  uint32_t raw_bytes, stage_bytes;  // raw part of a stage (padded to 1024 bytes), whole stage
+  uint32_t wbox_bytes;              // bytes of the weight box (rows x pitch)
+  uint32_t off_tab;                 // scale table [kbs][rows][subs + 1] float2
+  int cwarps, rows;                 // consumer warps and weight rows of a tile
   int* err;
 };
 
@@ -203,19 +204,19 @@ __global__ void __launch_bounds__(threads_for<MT>(), 1)
     gemm_kq_mma_kernel(const __grid_constant__ CUtensorMap xmap,
                        const __grid_constant__ CUtensorMap wmap, const MmaParams p) {
   constexpr int NF = TN / 8;  // n fragments of 8 tokens
-  constexpr int kCWarps = cwarps<MT>();
   constexpr int WR = 16 * MT;  // rows per consumer warp
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = smem_dyn + ((1024u - (smem_addr(smem_dyn) & 1023u)) & 1023u);
   constexpr int TS = MmaDq<QT>::kSubs + 1;  // table row stride (float2): conflict-free
   const int S = p.stages;
   float2* tab = reinterpret_cast<float2*>(smem + p.off_tab);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_tab + (size_t)p.kbs * kRows * TS * 8);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_tab + (size_t)p.kbs * p.rows * TS * 8);
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kRows, m0 = blockIdx.y * TN, z = blockIdx.z;
+  const int n0 = blockIdx.x * p.rows, m0 = blockIdx.y * TN, z = blockIdx.z;
+  const int pstride = p.rows + 4;  // floats per token row of the partial tile
   const int kb0 = (int)((long long)z * p.nb / p.splits);
   const int kb1 = (int)((long long)(z + 1) * p.nb / p.splits);
   const int n_blk = kb1 - kb0;
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(threads_for<MT>(), 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kCWarps);
+      mbar_init(&empty[s], p.cwarps);
     }
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -251,7 +252,7 @@ __global__ void __launch_bounds__(threads_for<MT>(), 1)
       const int nk = min(p.kbs, kb1 - kb);
       if (lane == 0) {
         uint8_t* dst = smem + (size_t)s * p.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], p.raw_bytes + (uint32_t)(4 * nk) * xbox);
+        mbar_arrive_expect_tx(&full[s], p.wbox_bytes + (uint32_t)(4 * nk) * xbox);
         tma_load_2d(dst, &wmap, (int)(((long long)kb * p.bb & ~15ll) >> 3), n0, &full[s]);
         for (int i = 0; i < 4 * nk; ++i)
           tma_load_2d(dst + p.raw_bytes + (uint32_t)i * xbox, &xmap, kb * 256 + 64 * i, m0, &full[s]);
@@ -348,8 +349,8 @@ __global__ void __launch_bounds__(threads_for<MT>(), 1)
       if (lane == 0) mbar_arrive(&empty[s]);
     }
     // all stages consumed by every consumer before the ring is reused for the partial tile
-    named_barrier(1, kCWarps * 32);
-    float* part = reinterpret_cast<float*>(smem);  // [TN][kPartStride]
+    named_barrier(1, p.cwarps * 32);
+    float* part = reinterpret_cast<float*>(smem);  // [TN][pstride]
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__(threads_for<MT>(), 1)
         for (int i = 0; i < 4; ++i) {
           const int row = WR * cw + 16 * mt + g + 8 * (i >> 1);
           const int tok = 8 * nf + 2 * t + (i & 1);
-          part[tok * kPartStride + row] = acc[mt][nf][i];
+          part[tok * pstride + row] = acc[mt][nf][i];
         }
   }
 
@@ -371,9 +372,10 @@ __global__ void __launch_bounds__(threads_for<MT>(), 1)
     const int per = (TN + p.splits - 1) / p.splits;
     const int j0 = z * per, j1 = min(TN, j0 + per);
     const float* part = reinterpret_cast<const float*>(smem);
-    for (int idx = tid; idx < (j1 - j0) * (kRows / 4); idx += kCWarps * 32) {
-      const int j = j0 + idx / (kRows / 4), r4 = (idx % (kRows / 4)) * 4;
-      const uint32_t la = smem_addr(part + j * kPartStride + r4);
+    const int r4n = p.rows / 4;
+    for (int idx = tid; idx < (j1 - j0) * r4n; idx += p.cwarps * 32) {
+      const int j = j0 + idx / r4n, r4 = (idx % r4n) * 4;
+      const uint32_t la = smem_addr(part + j * pstride + r4);
       float4 v = ld_dsmem_f4(la, 0);
       for (int s2 = 1; s2 < p.splits; ++s2) {
         const float4 u = ld_dsmem_f4(la, (uint32_t)s2);
@@ -407,70 +409,131 @@ __global__ void __launch_bounds__(threads_for<MT>(), 1)
 
 // ---- host side ----------------------------------------------------------------------
 
-// Stage layout: raw [kRows][pitch] (box of kbs super-blocks + envelope, pitch an odd
-// number of 16-byte units) then X [4*kbs][TN][128 B]; both multiples of 1024 bytes.
-int stage_bytes_for(int qtype, int kbs, int tn) {
-  return kRows * raw_slot_bytes(qtype, kbs) + 4 * kbs * tn * 128;
+// Stage layout: raw [rows][pitch] (box of kbs super-blocks + envelope, pitch an odd
+// number of 16-byte units) padded to 1024 bytes, then X [4*kbs][TN][128 B] (128-byte
+// swizzle, whose pattern is anchored at 1024-byte boundaries).
+int raw_part_bytes(int qtype, int kbs, int rows) {
+  return (rows * raw_slot_bytes(qtype, kbs) + 1023) & ~1023;
+}
+int stage_bytes_for(int qtype, int kbs, int tn, int rows) {
+  return raw_part_bytes(qtype, kbs, rows) + 4 * kbs * tn * 128;
 }
 // Scale table: (a / 65536, c) per row and scale group of the stage's super-blocks.
-int table_bytes_for(int qtype, int kbs) {
-  return kbs * kRows * ((qtype == RRR_Q6_K ? 16 : 8) + 1) * 8;
+int table_bytes_for(int qtype, int kbs, int rows) {
+  return kbs * rows * ((qtype == RRR_Q6_K ? 16 : 8) + 1) * 8;
+}
+
+// Ring of one tile shape: super-blocks per stage, stages and shared memory (stages 0: the
+// shape does not fit).
+struct Ring {
+  int kbs, stages, smem;
+};
+Ring ring_for(int qtype, int tn, int rows) {
+  const int fixed = 1024 + 256;
+  for (int kbs = 2; kbs >= 1; --kbs) {
+    const int sb = stage_bytes_for(qtype, kbs, tn, rows);
+    const int tb = table_bytes_for(qtype, kbs, rows);
+    int st = (kSmemBudget - fixed - tb) / sb;
+    if (st > 4) st = 4;
+    if (st >= 3 || (kbs == 1 && st >= 2)) {
+      // the partial tile [TN][rows + 4] f32 reuses the ring
+      if (tn * (rows + 4) * 4 > st * sb) return Ring{0, 0, 0};
+      return Ring{kbs, st, fixed + tb + st * sb};
+    }
+  }
+  return Ring{0, 0, 0};
 }
 
 template <int QT, int TN, int MT>
 cudaError_t launch_t(const LaunchEnv& env, const MmaPlan& pl, const void* w, const uint16_t* x,
                      float* y, int M, int K, int N, const float* residual) {
+  constexpr int WR = 16 * MT;
+  const int nb = K / 256;
+  auto kern = gemm_kq_mma_kernel<QT, TN, MT>;
+  // Tile height (WR rows per consumer warp) and K splits (choose_tile), chosen once per
+  // (device, shape).
+  struct Choice {
+    int dev, N, nb, cw, s;
+    Ring ring;
+  };
+  static thread_local Choice chosen[16];
+  static thread_local int n_chosen = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int best_cw = 0, best_s = 1;
+  Ring best_ring{0, 0, 0};
+  for (int i = 0; i < n_chosen; ++i)
+    if (chosen[i].dev == dev && chosen[i].N == N && chosen[i].nb == nb) {
+      best_cw = chosen[i].cw;
+      best_s = chosen[i].s;
+      best_ring = chosen[i].ring;
+    }
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = env.stream;
+  if (best_cw == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
+    if (e != cudaSuccess) return e;
+    TileCand cand[kMaxRows / 16];
+    Ring rings[kMaxRows / 16];
+    int cws[kMaxRows / 16], nc = 0;
+    for (int cw = cwarps<MT>(); cw >= 2; --cw) {
+      const Ring rg = ring_for(QT, TN, cw * WR);
+      if (rg.stages == 0) continue;
+      cand[nc] = TileCand{cw * WR, (cw + 1) * 32, rg.smem};
+      rings[nc] = rg;
+      cws[nc++] = cw;
+    }
+    int s = 1;
+    const int i = choose_tile((const void*)kern, env.stream, cand, nc, N, pl.m_tiles, nb,
+                              std::min(kMaxSplits, std::max(1, nb / 2)), env.sm_count, &s);
+    if (i < 0) return cudaErrorInvalidConfiguration;
+    best_cw = cws[i];
+    best_s = s;
+    best_ring = rings[i];
+    const Choice c{dev, N, nb, best_cw, best_s, best_ring};
+    if (n_chosen < 16) chosen[n_chosen++] = c;
+    else chosen[(N + nb) % 16] = c;
+  }
+  const int rows = best_cw * WR;
   CUtensorMap xmap, wmap;
   if (!encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M,
                  (uint64_t)K * 2, 64u, (uint32_t)TN, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  const long long row_bytes = (long long)(K / 256) * KQ<QT>::kBlockBytes;
-  const int pitch = raw_slot_bytes(QT, pl.kbs);
+  const long long row_bytes = (long long)nb * KQ<QT>::kBlockBytes;
+  const int pitch = raw_slot_bytes(QT, best_ring.kbs);
   if (!encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, (uint64_t)row_bytes / 8, (uint64_t)N,
-                 (uint64_t)row_bytes, (uint32_t)pitch / 8, (uint32_t)kRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+                 (uint64_t)row_bytes, (uint32_t)pitch / 8, (uint32_t)rows, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   MmaParams p{};
   p.y = y;
   p.residual = residual;
   p.M = M;
   p.N = N;
-  p.nb = K / 256;
+  p.nb = nb;
   p.bb = KQ<QT>::kBlockBytes;
   p.tn = TN;
-  p.splits = pl.splits;
-  p.stages = pl.stages;
-  p.kbs = pl.kbs;
+  p.splits = best_s;
+  p.stages = best_ring.stages;
+  p.kbs = best_ring.kbs;
   p.pitch = pitch;
-  p.raw_bytes = (uint32_t)(kRows * pitch);
-  p.stage_bytes = (uint32_t)stage_bytes_for(QT, pl.kbs, TN);
-  p.off_tab = (uint32_t)pl.stages * p.stage_bytes;
+  p.cwarps = best_cw;
+  p.rows = rows;
+  p.raw_bytes = (uint32_t)raw_part_bytes(QT, best_ring.kbs, rows);
+  p.wbox_bytes = (uint32_t)(rows * pitch);
+  p.stage_bytes = (uint32_t)stage_bytes_for(QT, best_ring.kbs, TN, rows);
+  p.off_tab = (uint32_t)best_ring.stages * p.stage_bytes;
   p.err = env.d_err;
-  auto kern = gemm_kq_mma_kernel<QT, TN, MT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
-  if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.n_tiles, pl.m_tiles, pl.splits);
-  cfg.blockDim = dim3(threads_for<MT>());
-  cfg.dynamicSmemBytes = pl.smem;
-  cfg.stream = env.stream;
+  cfg.gridDim = dim3((N + rows - 1) / rows, pl.m_tiles, best_s);
+  cfg.blockDim = dim3((best_cw + 1) * 32);
+  cfg.dynamicSmemBytes = best_ring.smem;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = pl.splits;
+  attr[0].val.clusterDim.z = best_s;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (pl.splits > 1) {
-    // clusters are placed per GPC: the plan's split count can need a second wave of
-    // clusters (e.g. 24 tiles x 6 splits on 22 resident clusters of 6); take the split
-    // count with the fewest waves x K-blocks per CTA
-    const int s = pick_splits((const void*)kern, cfg, pl.n_tiles * pl.m_tiles, K / 256, pl.splits);
-    p.splits = s;
-    cfg.gridDim.z = s;
-    attr[0].val.clusterDim.z = s;
-  }
   cfg.numAttrs = env.pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, xmap, wmap, p);
 }
@@ -497,32 +560,16 @@ bool plan_gemm_kq_mma(int qtype, int M, int K, int N, int sm_count, MmaPlan* pl)
   MmaPlan r{};
   r.tn = (M + 15) / 16 * 16;  // NF = tn / 8 even: one ldmatrix.x4 covers 2 n fragments
   r.m_tiles = (M + r.tn - 1) / r.tn;
-  r.n_tiles = (N + kRows - 1) / kRows;
-  int fixed = 1024 + 256;
-  r.kbs = 1;
-  r.stages = 0;
-  for (int kbs = 2; kbs >= 1; --kbs) {
-    const int sb = stage_bytes_for(qtype, kbs, r.tn);
-    const int st = (kSmemBudget - fixed - table_bytes_for(qtype, kbs)) / sb;
-    if (st >= 3 || kbs == 1) {
-      r.kbs = kbs;
-      r.stages = st > 4 ? 4 : st;
-      break;
-    }
-  }
-  const int sb = stage_bytes_for(qtype, r.kbs, r.tn);
-  fixed += table_bytes_for(qtype, r.kbs);
-  if (r.stages < 2) return false;
-  // the partial tile [TN][kRows + 4] f32 reuses the ring
-  if (r.tn * kPartStride * 4 > r.stages * sb) return false;
-  r.smem = fixed + r.stages * sb;
-  const int nb = K / 256;
-  const int base = r.n_tiles * r.m_tiles;
-  int splits = sm_count > 0 ? sm_count / base : 1;
-  if (splits > kMaxSplits) splits = kMaxSplits;
-  if (splits > nb / 2) splits = nb / 2;
-  if (splits < 1) splits = 1;
-  r.splits = splits;
+  // the tile height and the split count are chosen at launch from the kernel's cluster
+  // occupancy; here only whether the tallest tile fits
+  const Ring rg = ring_for(qtype, r.tn, kMaxRows);
+  if (rg.stages == 0) return false;
+  r.n_tiles = (N + kMaxRows - 1) / kMaxRows;
+  r.kbs = rg.kbs;
+  r.stages = rg.stages;
+  r.smem = rg.smem;
+  r.splits = 0;
+  (void)sm_count;
   *pl = r;
   return true;
 }

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "kquant.cuh"
@@ -317,6 +318,58 @@ inline int pick_splits(const void* kern, const cudaLaunchConfig_t& cfg, int base
       best = s;
     }
   }
+  return best;
+}
+
+// Candidate tile height of a row-tiled GEMM launch: weight rows per CTA, its block size and
+// dynamic shared memory.
+struct TileCand {
+  int rows, threads, smem;
+};
+// Picks a candidate (given tallest first) and its split count. For each height the split
+// count is pick_splits' (fewest waves x K-blocks per CTA); the tallest height whose
+// first wave puts at least 3/4 of the SMs to work in one wave wins (tall tiles re-read X
+// least and spread the fixed cost per CTA over the most rows); if no height fills the
+// GPU, the least work on the busiest SM wins: waves x CTAs per SM x K-blocks per CTA x
+// rows. Returns the index (-1: none fits) and the split count in *splits.
+inline int choose_tile(const void* kern, cudaStream_t stream, const TileCand* c, int n, int N,
+                       int m_tiles, int nb, int max_s, int sm_count, int* splits) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = stream;
+  int best = -1, best_s = 1;
+  long long best_work = -1;
+  for (int i = 0; i < n; ++i) {
+    cfg.blockDim = dim3(c[i].threads);
+    cfg.dynamicSmemBytes = c[i].smem;
+    const int base = m_tiles * ((N + c[i].rows - 1) / c[i].rows);
+    int s_best = 0, fit_best = 0;
+    long long cost_best = -1;
+    for (int s = 1; s <= max_s; ++s) {
+      const int fit = max_active_clusters(kern, cfg, s);
+      if (fit < 1) continue;
+      const long long cost = (long long)((base + fit - 1) / fit) * ((nb + s - 1) / s);
+      if (cost_best < 0 || cost < cost_best) {
+        cost_best = cost;
+        s_best = s;
+        fit_best = fit;
+      }
+    }
+    if (s_best == 0) continue;
+    const int waves = (base + fit_best - 1) / fit_best;
+    const long long first = (long long)std::min(base, fit_best) * s_best;
+    if (waves == 1 && 4 * first >= 3LL * sm_count) {
+      *splits = s_best;
+      return i;
+    }
+    const long long per_sm = (first + sm_count - 1) / sm_count;
+    const long long work = (long long)waves * per_sm * ((nb + s_best - 1) / s_best) * c[i].rows;
+    if (best_work < 0 || work < best_work) {
+      best_work = work;
+      best = i;
+      best_s = s_best;
+    }
+  }
+  *splits = best_s;
   return best;
 }
 
