@@ -180,8 +180,9 @@ int rrr_gemm_kq_batched_ex(rrr_ctx* ctx, int qtype, const void* w_raw, const uin
                            float* y, int M, int K, int N, const float* residual, void* stream);
 /* The same GEMM with the kernel chosen explicitly (tests, benchmarks): RRR_GEMM_AUTO is
  * rrr_gemm_kq_batched_ex's choice (mma.sync for 3 <= M <= 64 when every weight row is a
- * multiple of 16 bytes, tcgen05 for larger M or unaligned rows from M = 16, one GEMV per
- * token otherwise); the others force one kernel (mma.sync takes 1 <= M <= 64, tcgen05
+ * multiple of 16 bytes, the integer mma.sync kernel there when K <= 1024, tcgen05 for
+ * larger M or unaligned rows from M = 16, one GEMV per token otherwise); the others force
+ * one kernel (mma.sync takes 1 <= M <= 64, tcgen05
  * M >= 16) and fail with RRR_ERR_BAD_SHAPE where it does not apply. RRR_GEMM_MMA_I8 is
  * the integer mma.sync kernel (raw quants against int8 digits of X, 1 <= M <= 64, rows of
  * a multiple of 16 bytes); it prepares the digits in the context's scratch buffer, so two

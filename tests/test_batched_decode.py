@@ -66,11 +66,39 @@ def _bf16(a, torch):
     return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy()
 
 
+def _int8_kernel(M, qt, K):
+    """Whether the automatic choice runs the integer kernel (3 to 64 tokens, rows of a
+    multiple of 16 bytes, K <= 1024)."""
+    return (K // 256) * BB[qt] % 16 == 0 and 3 <= M <= 64 and K <= 1024
+
+
+def _digits(x):
+    """The integer kernel's form of a bf16 GEMM input: per row and 256-block, T =
+    round-half-even(x / xs) clamped to +-16383 with xs = 2^(E-14), 2^(E-1) <= max|x| < 2^E;
+    x is replaced by xs * T (|error| <= max|x| * 2^-15)."""
+    rows, K = x.shape
+    b = np.asarray(x, np.float64).reshape(rows, K // 256, 256)
+    m = np.abs(b).max(axis=2, keepdims=True)
+    _, E = np.frexp(m)
+    xs = np.ldexp(1.0, E - 14)
+    T = np.clip(np.rint(b / xs), -16383, 16383)
+    return np.where(m > 0, T * xs, 0.0).reshape(rows, K)
+
+
+def _gin(x, M, qt, K, torch):
+    """A GEMM input as its kernel sees it: bf16, then int8 digits for the integer kernel."""
+    xb = _bf16(x, torch).astype(np.float64)
+    return _digits(xb) if _int8_kernel(M, qt, K) else xb
+
+
 def _bf16_weights(M, qt, K):
     """Whether the batched GEMM of M tokens rounds the dequantised weights to bf16: the
-    tensor-core kernels do (mma.sync from 3 tokens when a weight row is a multiple of 16
-    bytes, tcgen05 from 16); one GEMV per token (M <= 2, or rows that are not a multiple
-    of 16 bytes below 16 tokens) uses the exact weights."""
+    bf16 tensor-core kernels do (mma.sync from 3 tokens when a weight row is a multiple of
+    16 bytes, tcgen05 from 16); the integer kernel (3 to 64 tokens, aligned rows, K <= 1024)
+    and one GEMV per token (M <= 2, or rows that are not a multiple of 16 bytes below 16
+    tokens) use the exact weights."""
+    if _int8_kernel(M, qt, K):
+        return False
     aligned = (K // 256) * BB[qt] % 16 == 0
     return M >= 16 or (M >= 3 and aligned)
 
@@ -78,9 +106,10 @@ def _bf16_weights(M, qt, K):
 def _bf16_reference(oracle, layers, on, wo, H0, torch):
     """The batched step with the GEMM kernels' roundings made explicit: GEMM inputs (and,
     where _bf16_weights says so, the dequantised weights) rounded to bf16 (nearest even),
-    products summed in f64, everything else in f32 with the reference's formulas
-    (rms_norm (g*x)*inv, phi4.rs:593-599; silu, :601-606; position-0 attention output = V
-    of the head's KV group)."""
+    the integer kernel's inputs then to its int8 digits (_gin), products summed in f64,
+    everything else in f32 with the reference's formulas (rms_norm (g*x)*inv,
+    phi4.rs:593-599; silu, :601-606; position-0 attention output = V of the head's KV
+    group)."""
     c = SMALL
     d, F, hd, nq, nkv = c["d_model"], c["ffn_dim"], c["head_dim"], c["n_heads"], c["n_kv_heads"]
     qkv_dim = (nq + 2 * nkv) * hd
@@ -93,16 +122,17 @@ def _bf16_reference(oracle, layers, on, wo, H0, torch):
         w = oracle.dequant(qt, L[key], N * K).reshape(N, K)
         return (_bf16(w, torch) if _bf16_weights(H0.shape[0], qt, K) else w).astype(np.float64)
 
+    M = H0.shape[0]
     for L in layers:
-        xn = _bf16(rms(H, L["attn_norm"]), torch).astype(np.float64)
-        qkv = (xn @ W(L, "w_qkv", L["qkv_type"], d, qkv_dim).T).astype(np.float32)
+        xn = rms(H, L["attn_norm"])
+        qkv = (_gin(xn, M, L["qkv_type"], d, torch) @ W(L, "w_qkv", L["qkv_type"], d, qkv_dim).T).astype(np.float32)
         v = qkv[:, (nq + nkv) * hd:]
         a = np.concatenate([v[:, (h // (nq // nkv)) * hd:(h // (nq // nkv) + 1) * hd] for h in range(nq)], 1)
-        H = (H + _bf16(a, torch).astype(np.float64) @ W(L, "w_o", L["o_type"], nq * hd, d).T).astype(np.float32)
-        xn = _bf16(rms(H, L["ffn_norm"]), torch).astype(np.float64)
-        gu = (xn @ W(L, "w_gate_up", L["gate_up_type"], d, 2 * F).T).astype(np.float32)
+        H = (H + _gin(a, M, L["o_type"], nq * hd, torch) @ W(L, "w_o", L["o_type"], nq * hd, d).T).astype(np.float32)
+        xn = rms(H, L["ffn_norm"])
+        gu = (_gin(xn, M, L["gate_up_type"], d, torch) @ W(L, "w_gate_up", L["gate_up_type"], d, 2 * F).T).astype(np.float32)
         mid = np.stack([oracle.silu_gate(r) for r in gu])
-        H = (H + _bf16(mid, torch).astype(np.float64) @ W(L, "w_down", L["down_type"], F, d).T).astype(np.float32)
+        H = (H + _gin(mid, M, L["down_type"], F, torch) @ W(L, "w_down", L["down_type"], F, d).T).astype(np.float32)
     LG = (rms(H, on).astype(np.float64) @ wo.astype(np.float64).T).astype(np.float32)
     return H, LG
 
@@ -177,8 +207,8 @@ def _bf16_reference_kv(oracle, layers, on, wo, H0, torch, pos0, kc, vc, fac):
         return (_bf16(w, torch) if _bf16_weights(M, qt, K) else w).astype(np.float64)
 
     for li, L in enumerate(layers):
-        xn = _bf16(rms(H, L["attn_norm"]), torch).astype(np.float64)
-        qkv = (xn @ W(L, "w_qkv", L["qkv_type"], d, qkv_dim).T).astype(np.float32)
+        xn = rms(H, L["attn_norm"])
+        qkv = (_gin(xn, M, L["qkv_type"], d, torch) @ W(L, "w_qkv", L["qkv_type"], d, qkv_dim).T).astype(np.float32)
         A = np.empty((M, nq * hd), np.float32)
         qs = []
         for t in range(M):
@@ -191,11 +221,11 @@ def _bf16_reference_kv(oracle, layers, on, wo, H0, torch, pos0, kc, vc, fac):
             qs.append(q)
         for t in range(M):
             A[t] = oracle.attention_f16kv(qs[t], kc[li], vc[li], pos0 + t + 1, nq, nkv, hd)
-        H = (H + _bf16(A, torch).astype(np.float64) @ W(L, "w_o", L["o_type"], nq * hd, d).T).astype(np.float32)
-        xn = _bf16(rms(H, L["ffn_norm"]), torch).astype(np.float64)
-        gu = (xn @ W(L, "w_gate_up", L["gate_up_type"], d, 2 * F).T).astype(np.float32)
+        H = (H + _gin(A, M, L["o_type"], nq * hd, torch) @ W(L, "w_o", L["o_type"], nq * hd, d).T).astype(np.float32)
+        xn = rms(H, L["ffn_norm"])
+        gu = (_gin(xn, M, L["gate_up_type"], d, torch) @ W(L, "w_gate_up", L["gate_up_type"], d, 2 * F).T).astype(np.float32)
         mid = np.stack([oracle.silu_gate(r) for r in gu])
-        H = (H + _bf16(mid, torch).astype(np.float64) @ W(L, "w_down", L["down_type"], F, d).T).astype(np.float32)
+        H = (H + _gin(mid, M, L["down_type"], F, torch) @ W(L, "w_down", L["down_type"], F, d).T).astype(np.float32)
     LG = (rms(H, on).astype(np.float64) @ wo.astype(np.float64).T).astype(np.float32)
     return H, LG
 

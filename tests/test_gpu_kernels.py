@@ -594,6 +594,29 @@ def test_gemm_mma_i8_residual_and_heavy_tails(rrr, ctx, oracle, G, qt):
         assert rel_l2(got.ravel(), ref.ravel()) < 1e-3
 
 
+@pytest.mark.parametrize("qt,K", [(12, 768), (13, 512), (14, 2048)])
+def test_gemm_auto_short_rows_take_integer_kernel(rrr, ctx, oracle, G, qt, K):
+    """The automatic choice runs the integer kernel for K <= 1024 at 3..64 tokens (the
+    O-projection shard of a 4- or 8-way split) and the bf16 kernel above: identical bits to
+    the forced path."""
+    import torch
+    L = rrr.ffi.lib()
+    N, M = 3072, 64
+    if (K // 256) * {12: 144, 13: 176, 14: 210}[qt] % 16:
+        pytest.skip("rows not a multiple of 16 bytes")
+    raw = oracle.random_blocks(qt, N * (K // 256), np.random.default_rng(K + qt))
+    wd = G.dev(raw)
+    X = torch.randn(M, K, dtype=torch.bfloat16).cuda()
+    outs = {}
+    for path in (0, GEMM_MMA, GEMM_MMA_I8):
+        Y = G.empty_f32(M * N)
+        ctx.check(L.rrr_gemm_kq_batched_path(ctx.h, qt, vp(wd), vp(X), vp(Y), M, K, N, None, path, None))
+        outs[path] = G.host(Y)
+    expect = GEMM_MMA_I8 if K <= 1024 else GEMM_MMA
+    assert np.array_equal(outs[0], outs[expect])
+    assert rel_l2(outs[GEMM_MMA_I8], outs[GEMM_MMA]) < 5e-3
+
+
 def test_gemm_path_selection(rrr, ctx, oracle, G):
     """The mma.sync kernel rejects what it does not handle (M > 64, rows that are not a
     multiple of 16 bytes: Q6_K with K/256 not a multiple of 8); the tcgen05 kernel M < 16."""
@@ -617,8 +640,9 @@ def test_gemm_path_selection(rrr, ctx, oracle, G):
 @pytest.mark.parametrize("qt,K", [(12, 1024), (13, 1024), (14, 2048), (14, 1024)])
 def test_gemm_auto_small_m(rrr, ctx, oracle, G, qt, K):
     """The automatic choice below 16 tokens: one GEMV per token for M <= 2 and for rows
-    that are not a multiple of 16 bytes (Q6_K, K = 1024), the mma.sync kernel from 3
-    tokens otherwise; each result bit-identical to the forced kernel's."""
+    that are not a multiple of 16 bytes (Q6_K, K = 1024), from 3 tokens the integer
+    mma.sync kernel for K <= 1024 and the bf16 one above; each result bit-identical to the
+    forced kernel's."""
     import torch
     N = 512
     L = rrr.ffi.lib()
@@ -626,7 +650,7 @@ def test_gemm_auto_small_m(rrr, ctx, oracle, G, qt, K):
     aligned = (K // 256) * {12: 144, 13: 176, 14: 210}[qt] % 16 == 0
     for M in (1, 2, 3, 8, 15):
         x = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).to(torch.bfloat16).cuda()
-        want = GEMM_MMA if (M >= 3 and aligned) else GEMM_PER_TOKEN
+        want = (GEMM_MMA_I8 if K <= 1024 else GEMM_MMA) if (M >= 3 and aligned) else GEMM_PER_TOKEN
         ys = []
         for path in (0, want):
             y = torch.full((M, N), float("nan"), device="cuda")
@@ -643,8 +667,8 @@ def test_gemm_auto_small_m(rrr, ctx, oracle, G, qt, K):
                                             (300, 512, 256, True)])
 def test_gemm_tc_residual(rrr, ctx, oracle, G, qt, M, K, N, inplace):
     """rrr_gemm_kq_batched_ex: Y = X W^T + R with R == Y (in place) or separate, on the
-    split-K cluster path, the single-split path, the mma.sync path below 16 tokens and the
-    per-token path."""
+    split-K cluster path, the single-split path, both mma.sync paths (bf16 and integer)
+    and the per-token path."""
     import torch
     rng = np.random.default_rng(M + K + N + qt)
     raw = oracle.random_blocks(qt, N * (K // 256), rng)
@@ -660,7 +684,8 @@ def test_gemm_tc_residual(rrr, ctx, oracle, G, qt, M, K, N, inplace):
     Y0 = Y.clone()
     R0 = Rd.clone()
     aligned_rows = (K // 256) * {12: 144, 13: 176, 14: 210}[qt] % 16 == 0
-    paths = [0] + ([GEMM_TCGEN05] if M >= 16 else []) + ([GEMM_MMA] if M <= 64 and aligned_rows else [])
+    paths = [0] + ([GEMM_TCGEN05] if M >= 16 else []) + \
+        ([GEMM_MMA, GEMM_MMA_I8] if M <= 64 and aligned_rows else [])
     if M < 16:
         paths.append(GEMM_PER_TOKEN)
     for path in paths:
