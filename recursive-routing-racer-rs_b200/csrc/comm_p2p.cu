@@ -61,7 +61,16 @@ __device__ __forceinline__ float wait_word(const unsigned long long* p, unsigned
 
 // mode 0: x[i] = sum over ranks (in place allowed); mode 1: all-gather, element i of rank
 // r's input to out[(i / npr) * world * npr + r * npr + i % npr] (npr = n: concatenation;
-// npr < n: rows of npr elements interleaved by rank, the layout of row-split logits)
+// npr < n: rows of npr elements interleaved by rank, the layout of row-split logits);
+// mode 2: the mode-0 sum in two trips (reduce-scatter, then all-gather of the sums): rank
+// s owns the slice [s*npr, (s+1)*npr) (npr = ceil(n / world)); every rank sends slice s
+// only to its owner, the owner sums it in rank order (the bits of mode 0) and sends the
+// sums to every rank. In rank r's buffer the owner's sums of slice s land in the slots of
+// source s outside slice r, which the first trip leaves unused. A CTA covers slice
+// positions [c*chunk, (c+1)*chunk) of every slice.
+// Every call runs all kMaxCtas CTAs (those past the data only advance their epoch), so
+// the epochs of all CTAs advance together and consecutive calls always use different slot
+// sets, however differently two calls map elements to CTAs.
 __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const float* in, float* out,
                                                               int64_t n, int64_t chunk, int rank,
                                                               int world, int64_t max_elems,
@@ -72,13 +81,48 @@ __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const 
   pdl_launch_dependents();
   pdl_wait();
   const int c = blockIdx.x;
-  const int64_t i0 = (int64_t)c * chunk, i1 = min(n, i0 + chunk);
+  const int64_t i0 = (int64_t)c * chunk, i1 = min(mode == 2 ? npr : n, i0 + chunk);
   __shared__ unsigned s_epoch;
   if (threadIdx.x == 0) s_epoch = counters[c] + 1;
   __syncthreads();
   const unsigned e = s_epoch;
   const int set = e & 1;
   const unsigned long long tag = (unsigned long long)e << 32;
+  const unsigned long long* base = peers.slots[rank] + (int64_t)set * world * max_elems;
+  bool ok = true;
+  if (mode == 2) {
+    // 1. slice s of this rank's input, tagged, into slot `rank` of its owner's buffer
+    for (int s = 0; s < world; ++s) {
+      unsigned long long* dst = peers.slots[s] + ((int64_t)set * world + rank) * max_elems;
+      for (int64_t j = i0 + threadIdx.x; j < i1; j += kThreadsX) {
+        const int64_t i = (int64_t)s * npr + j;
+        if (i < n) st_relaxed_sys_u64(dst + i, tag | __float_as_uint(in[i]));
+      }
+    }
+    // 2. this rank's slice: every rank's element in rank order, the sum to every rank
+    for (int64_t j = i0 + threadIdx.x; j < i1; j += kThreadsX) {
+      const int64_t i = (int64_t)rank * npr + j;
+      if (i >= n) break;
+      float acc = wait_word(base + i, e, ok, err);
+      for (int r = 1; r < world; ++r) acc += wait_word(base + (int64_t)r * max_elems + i, e, ok, err);
+      out[i] = acc;
+      for (int r = 0; r < world; ++r)
+        if (r != rank)
+          st_relaxed_sys_u64(peers.slots[r] + ((int64_t)set * world + rank) * max_elems + i,
+                             tag | __float_as_uint(acc));
+    }
+    // 3. the other slices' sums from their owners
+    for (int s = 0; s < world; ++s) {
+      if (s == rank) continue;
+      for (int64_t j = i0 + threadIdx.x; j < i1; j += kThreadsX) {
+        const int64_t i = (int64_t)s * npr + j;
+        if (i < n) out[i] = wait_word(base + (int64_t)s * max_elems + i, e, ok, err);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) counters[c] = e;
+    return;
+  }
   // 1. this rank's elements, tagged, into slot `rank` of every buffer
   for (int r = 0; r < world; ++r) {
     unsigned long long* dst = peers.slots[r] + ((int64_t)set * world + rank) * max_elems;
@@ -86,8 +130,6 @@ __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const 
       st_relaxed_sys_u64(dst + i, tag | __float_as_uint(in[i]));
   }
   // 2.-3. every rank's element, in rank order
-  const unsigned long long* base = peers.slots[rank] + (int64_t)set * world * max_elems;
-  bool ok = true;
   for (int64_t i = i0 + threadIdx.x; i < i1; i += kThreadsX) {
     if (mode == 0) {
       float acc = wait_word(base + i, e, ok, err);
@@ -275,10 +317,19 @@ static int comm_launch(rrr_comm* c, const float* in, float* out, int64_t n, int 
                      (long long)n, (long long)c->max_elems);
   int rc = bind_device(c->ctx);
   if (rc) return rc;
-  // about 2 KB of values per CTA and rank, at most kMaxCtas CTAs
-  int64_t chunk = std::max<int64_t>(512, (n + kMaxCtas - 1) / kMaxCtas);
+  // Large all-reduces from 4 ranks up take two trips (mode 2): each rank then writes about
+  // 2n tagged words instead of world * n, which pays once the saved bytes outweigh the
+  // second NVLink trip (n * (world - 2) * 8 bytes >= 2 MB, e.g. 64 tokens x 3072 at 8 ranks)
+  if (mode == 0 && c->world >= 4 && n * (c->world - 2) * 8 >= (int64_t)(2 << 20)) {
+    mode = 2;
+    npr = (n + c->world - 1) / c->world;
+  }
+  // about 2 KB of values per CTA and rank (of each slice in mode 2), at most kMaxCtas CTAs
+  // with data; all kMaxCtas CTAs run (see exchange_kernel)
+  const int64_t span = mode == 2 ? npr : n;
+  int64_t chunk = std::max<int64_t>(512, (span + kMaxCtas - 1) / kMaxCtas);
   chunk = (chunk + 3) / 4 * 4;
-  const int ctas = (int)((n + chunk - 1) / chunk);
+  const int ctas = kMaxCtas;
   const LaunchEnv env = make_env(c->ctx, stream);
   cudaError_t e = rrr_launch_pdl(exchange_kernel, dim3(ctas), dim3(kThreadsX), 0, env.stream, env.pdl,
                                  c->peers, in, out, n, chunk, c->rank, c->world, c->max_elems,

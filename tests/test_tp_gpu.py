@@ -285,3 +285,77 @@ def test_tp_fused_exchange_bits_equal_unfused(world, max_seq):
         assert launches[1] < launches[0], launches
         assert same, rank
         assert err == 0
+
+
+# ------------------------------------------------------------------ exchange kernels
+def _exchange_rank(rank, world, port, q):
+    import ctypes
+    import datetime
+    import torch
+    import torch.distributed as dist
+    rrr = importlib.import_module("recursive-routing-racer-rs_b200")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    comm = None
+    try:
+        ctx = rrr.Context(rank)
+        L = rrr.ffi.lib()
+        big = 64 * 3072
+        comm = tp.P2PComm(ctx, rank, world, max_elems=big)
+        # large (two-trip) and small (one-trip) all-reduces, with an all-gather between them
+        # that maps elements to CTAs differently; every call's inputs are known to every rank
+        calls = ["ar", "ar_small", "ar", "ag", "ar", "ar", "ar_small", "ar"]
+        results = []
+        for k, kind in enumerate(calls):
+            n = {"ar": big, "ar_small": 3072, "ag": 25000}[kind]
+            inputs = [np.random.default_rng(1000 * k + r).standard_normal(n).astype(np.float32)
+                      for r in range(world)]
+            x = torch.from_numpy(inputs[rank]).cuda()
+            if kind == "ag":
+                out = torch.empty(world * n, device="cuda")
+                ctx.check(L.rrr_comm_allgather_f32(comm.h, c_void_p(out.data_ptr()), c_void_p(x.data_ptr()),
+                                                   n, None))
+                want = np.concatenate(inputs)
+            else:
+                ctx.check(L.rrr_comm_allreduce_f32(comm.h, c_void_p(x.data_ptr()), n, None))
+                out = x
+                want = inputs[0].copy()
+                for r in range(1, world):
+                    want = want + inputs[r]  # rank order, f32
+            torch.cuda.synchronize()
+            results.append(bool(np.array_equal(out.cpu().numpy(), want)))
+        q.put((rank, results, ctx.device_error()))
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_comm_allreduce_two_trips_bits(world):
+    """The peer-memory all-reduce at 64 tokens x 3072 (two trips from 4 ranks: each rank's
+    slice summed by its owner in rank order, the sums sent back) gives every rank the bits
+    of the rank-order f32 sum, as the one-trip form does for small exchanges, across calls
+    of different sizes and an all-gather in between."""
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = _free_port()
+    procs = [mpc.Process(target=_exchange_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+        assert p.exitcode == 0
+    for _ in range(world):
+        rank, results, err = q.get(timeout=10)
+        assert all(results), (rank, results)
+        assert err == 0
