@@ -11,16 +11,17 @@
 //    int8 digits T = 128*hi + lo (lo in 0..127); xs = 2^(E-14). |x - xs*T| <= xs/2 =
 //    max|x| * 2^-15 (bf16 elements within 2^-7 of the block maximum are exact). Also the
 //    sub-block sums xs * sum(T) over 32 elements (the Q4_K / Q5_K min terms).
-//  * One CTA = one 256-row x 16-token tile over a range of K super-blocks (split-K across a
-//    thread-block cluster when the tile grid is smaller than the GPU). More than 16 tokens
-//    take more token tiles: the tiles of one row tile are neighbours in the grid, so HBM
-//    delivers each weight once and L2 the other times, and the registers stay at one
-//    tile's sums. Warp 0 streams, per stage of kbs super-blocks, one 2-D TMA box of the raw
-//    blocks of the 256 rows, the digit rows of the stage (2*kbs boxes of 128 k x 32 digit
-//    rows, 128-byte swizzle) and the stage's scales and sums (one bulk copy). The weight
-//    boxes of the first stages go out before the grid dependency wait (weights are
-//    constant); everything that depends on X after it.
-//  * Warps 1-8 own 32 rows each (two m16 tiles sharing every B fragment). Q4_K / Q5_K: per 32-weight sub-block one
+//  * One CTA = one tile of 16*w weight rows (w = 4..16 consumer warps, the height and the
+//    K split chosen per shape by choose_tile) x 16 tokens over a range of K super-blocks
+//    (split-K across a thread-block cluster when the tile grid is smaller than the GPU).
+//    More than 16 tokens take more token tiles: the tiles of one row tile are neighbours
+//    in the grid, so HBM delivers each weight once and L2 the other times, and the
+//    registers stay at one tile's sums. Warp 0 streams, per stage of kbs super-blocks, one
+//    2-D TMA box of the raw blocks of the tile's rows, the digit rows of the stage (2*kbs
+//    boxes of 128 k x 32 digit rows, 128-byte swizzle) and the stage's scales and sums (one
+//    bulk copy). The weight boxes of the first stages go out before the grid dependency
+//    wait (weights are constant); everything that depends on X after it.
+//  * Warps 1..w own 16 rows each (one m16 tile). Q4_K / Q5_K: per 32-weight sub-block one
 //    mma.sync.m16n8k32 (u8 x s8 -> s32) per 8 digit columns (4 tokens x 2 digits), the
 //    A fragment built once from the raw bytes (nibble mask, Q5_K fifth bit) and reused
 //    over every token; the 6-bit sub-block scale multiplies the s32 result (integer

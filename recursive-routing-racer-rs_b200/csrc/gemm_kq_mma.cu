@@ -12,14 +12,16 @@
 // kernel runs at the weight stream or the mma.sync rate (measured ~550 TFLOP/s bf16 on
 // B200), whichever is lower.
 //
-// One CTA = one 256-row x TN-token tile (TN = M rounded up to 16) over a range of K
+// One CTA = one tile of up to 256 weight rows x TN tokens (TN = M rounded up to 16; the
+// tile height and the K split chosen per shape by choose_tile) over a range of K
 // super-blocks (split-K across a thread-block cluster when the tile grid is smaller than
 // the GPU):
 //   warp 0     producer: per stage of `kbs` super-blocks, one 2-D TMA box of the raw
-//              blocks of the 256 rows (16-byte-aligned envelope, zero fill past the row
+//              blocks of the tile's rows (16-byte-aligned envelope, zero fill past the row
 //              end and past N) and 4*kbs TMA boxes of X (64 k x TN tokens, 128-byte
 //              swizzle) into a ring, all on the stage's full barrier;
-//   warps 1-8  32 rows each (two m16 tiles): per 64-wide K chunk, the lane's A fragments
+//   consumers  16 rows each (one m16 tile, TN <= 32) or 32 rows (two m16 tiles sharing
+//              each B fragment, TN 48 and 64): per 64-wide K chunk, the lane's A fragments
 //              (rows g, g+8; k 2t, 2t+1, 2t+8, 2t+9 of each 16-k step) are built from the
 //              raw bytes with the packed exact-offset dequantisation (q*a - b as one
 //              f32x2 FMA on 2^23 + 65536 q, one cvt to bf16x2), B fragments come from the
