@@ -27,6 +27,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <vector>
 
 #include "capi_internal.h"
@@ -52,13 +53,6 @@ struct Peers {
   unsigned long long* slots[kMaxWorld];  // each rank's buffer (this rank's own at index rank)
 };
 
-// The value of word p once its epoch is e; gives up (ok = false) after the context's wait
-// limit (wait_limit_ns).
-__device__ __forceinline__ float wait_word(const unsigned long long* p, unsigned e, bool& ok,
-                                           int* err) {
-  return __uint_as_float((unsigned)wait_tagged(p, ld_relaxed_sys_u64(p), e, ok, err));
-}
-
 // mode 0: x[i] = sum over ranks (in place allowed); mode 1: all-gather, element i of rank
 // r's input to out[(i / npr) * world * npr + r * npr + i % npr] (npr = n: concatenation;
 // npr < n: rows of npr elements interleaved by rank, the layout of row-split logits);
@@ -71,11 +65,36 @@ __device__ __forceinline__ float wait_word(const unsigned long long* p, unsigned
 // Every call runs all kMaxCtas CTAs (those past the data only advance their epoch), so
 // the epochs of all CTAs advance together and consecutive calls always use different slot
 // sets, however differently two calls map elements to CTAs.
-__global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const float* in, float* out,
-                                                              int64_t n, int64_t chunk, int rank,
-                                                              int world, int64_t max_elems,
-                                                              unsigned* counters, int mode,
-                                                              int64_t npr, int* err) {
+// The words p(u, r) = q[u] + r * rstride (u < B, r < W) once they carry epoch e, for the
+// (u, r) where valid(u, r) holds: every load first, then a bounded wait on each word that
+// had not arrived yet. B elements of a thread are collected together (4 to 8 words in
+// flight) so that its waits cost one round trip per batch instead of one per word.
+template <int W, int B, typename Valid>
+__device__ __forceinline__ void collect(const unsigned long long* const (&q)[B], int64_t rstride,
+                                        Valid valid, unsigned e, bool& ok, int* err,
+                                        float (&v)[B][W]) {
+  unsigned long long w[B][W];
+#pragma unroll
+  for (int u = 0; u < B; ++u)
+#pragma unroll
+    for (int r = 0; r < W; ++r)
+      if (valid(u, r)) w[u][r] = ld_relaxed_sys_u64(q[u] + r * rstride);
+#pragma unroll
+  for (int u = 0; u < B; ++u)
+#pragma unroll
+    for (int r = 0; r < W; ++r)
+      if (valid(u, r))
+        v[u][r] = __uint_as_float((unsigned)wait_tagged(q[u] + r * rstride, w[u][r], e, ok, err));
+}
+
+// W = world (1..kMaxWorld ranks), B = elements collected together.
+template <int W>
+__global__ void __launch_bounds__(kThreadsX, 6) exchange_kernel(Peers peers, const float* in, float* out,
+                                                                 int64_t n, int64_t chunk, int rank,
+                                                                 int64_t max_elems, unsigned* counters,
+                                                                 int mode, int64_t npr, int* err) {
+  constexpr int world = W;
+  constexpr int kBatch = W >= 4 ? 1 : 4 / W;
   // launched with programmatic dependent launch: let the next kernel (a GEMV streaming its
   // weights) start now, and wait for the kernel that produced `in`
   pdl_launch_dependents();
@@ -90,6 +109,7 @@ __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const 
   const unsigned long long tag = (unsigned long long)e << 32;
   const unsigned long long* base = peers.slots[rank] + (int64_t)set * world * max_elems;
   bool ok = true;
+  float v[kBatch][W];
   if (mode == 2) {
     // 1. slice s of this rank's input, tagged, into slot `rank` of its owner's buffer
     for (int s = 0; s < world; ++s) {
@@ -100,24 +120,47 @@ __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const 
       }
     }
     // 2. this rank's slice: every rank's element in rank order, the sum to every rank
-    for (int64_t j = i0 + threadIdx.x; j < i1; j += kThreadsX) {
-      const int64_t i = (int64_t)rank * npr + j;
-      if (i >= n) break;
-      float acc = wait_word(base + i, e, ok, err);
-      for (int r = 1; r < world; ++r) acc += wait_word(base + (int64_t)r * max_elems + i, e, ok, err);
-      out[i] = acc;
-      for (int r = 0; r < world; ++r)
-        if (r != rank)
-          st_relaxed_sys_u64(peers.slots[r] + ((int64_t)set * world + rank) * max_elems + i,
-                             tag | __float_as_uint(acc));
-    }
-    // 3. the other slices' sums from their owners
-    for (int s = 0; s < world; ++s) {
-      if (s == rank) continue;
-      for (int64_t j = i0 + threadIdx.x; j < i1; j += kThreadsX) {
-        const int64_t i = (int64_t)s * npr + j;
-        if (i < n) out[i] = wait_word(base + (int64_t)s * max_elems + i, e, ok, err);
+    const int64_t own = (int64_t)rank * npr;
+    for (int64_t jb = i0 + threadIdx.x; jb < i1; jb += kBatch * kThreadsX) {
+      const unsigned long long* q[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) q[u] = base + own + jb + u * kThreadsX;
+      auto valid = [&](int u, int) {
+        const int64_t j = jb + u * kThreadsX;
+        return j < i1 && own + j < n;
+      };
+      collect<W, kBatch>(q, max_elems, valid, e, ok, err, v);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        if (!valid(u, 0)) continue;
+        const int64_t i = own + jb + u * kThreadsX;
+        float acc = v[u][0];
+#pragma unroll
+        for (int r = 1; r < W; ++r) acc += v[u][r];
+        out[i] = acc;
+        for (int r = 0; r < world; ++r)
+          if (r != rank)
+            st_relaxed_sys_u64(peers.slots[r] + ((int64_t)set * world + rank) * max_elems + i,
+                               tag | __float_as_uint(acc));
       }
+    }
+    // 3. the other slices' sums from their owners: word (s, s*npr + j) of this buffer (for
+    // s = rank that is this rank's own first-trip word, already there and not used)
+    for (int64_t jb = i0 + threadIdx.x; jb < i1; jb += kBatch * kThreadsX) {
+      const unsigned long long* q[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) q[u] = base + jb + u * kThreadsX;
+      auto valid = [&](int u, int s) {
+        const int64_t j = jb + u * kThreadsX;
+        return j < i1 && (int64_t)s * npr + j < n;
+      };
+      collect<W, kBatch>(q, max_elems + npr, valid, e, ok, err, v);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+#pragma unroll
+        for (int s2 = 0; s2 < W; ++s2)
+          if (s2 != rank && valid(u, s2))
+            out[(int64_t)s2 * npr + jb + u * kThreadsX] = v[u][s2];
     }
     __syncthreads();
     if (threadIdx.x == 0) counters[c] = e;
@@ -129,16 +172,27 @@ __global__ void __launch_bounds__(kThreadsX) exchange_kernel(Peers peers, const 
     for (int64_t i = i0 + threadIdx.x; i < i1; i += kThreadsX)
       st_relaxed_sys_u64(dst + i, tag | __float_as_uint(in[i]));
   }
-  // 2.-3. every rank's element, in rank order
-  for (int64_t i = i0 + threadIdx.x; i < i1; i += kThreadsX) {
-    if (mode == 0) {
-      float acc = wait_word(base + i, e, ok, err);
-      for (int r = 1; r < world; ++r) acc += wait_word(base + (int64_t)r * max_elems + i, e, ok, err);
-      out[i] = acc;
-    } else {
-      float* o = out + (i / npr) * world * npr + i % npr;
-      for (int r = 0; r < world; ++r)
-        o[(int64_t)r * npr] = wait_word(base + (int64_t)r * max_elems + i, e, ok, err);
+  // 2.-3. every rank's element: their sum in rank order (mode 0) or each in place (mode 1)
+  for (int64_t ib = i0 + threadIdx.x; ib < i1; ib += kBatch * kThreadsX) {
+    const unsigned long long* q[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) q[u] = base + ib + u * kThreadsX;
+    auto valid = [&](int u, int) { return ib + u * kThreadsX < i1; };
+    collect<W, kBatch>(q, max_elems, valid, e, ok, err, v);
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      if (!valid(u, 0)) continue;
+      const int64_t i = ib + u * kThreadsX;
+      if (mode == 0) {
+        float acc = v[u][0];
+#pragma unroll
+        for (int r = 1; r < W; ++r) acc += v[u][r];
+        out[i] = acc;
+      } else {
+        float* o = out + (i / npr) * world * npr + i % npr;
+#pragma unroll
+        for (int r = 0; r < W; ++r) o[(int64_t)r * npr] = v[u][r];
+      }
     }
   }
   __syncthreads();
@@ -307,6 +361,17 @@ int rrr_comm_connect(rrr_comm* c, const void* handles) {
   return RRR_OK;
 }
 
+// RRR_COMM_TWO_TRIP: 1 = every all-reduce of two or more ranks takes two trips, 0 = none
+// does; unset = large ones from 4 ranks (comm_launch). Read once per process (tests run the
+// two-trip form on two GPUs with it).
+static int two_trip_setting() {
+  static const int v = [] {
+    const char* s = std::getenv("RRR_COMM_TWO_TRIP");
+    return s ? std::atoi(s) : -1;
+  }();
+  return v;
+}
+
 static int comm_launch(rrr_comm* c, const float* in, float* out, int64_t n, int mode, int64_t npr,
                        void* stream, const char* what) {
   if (!c) return set_error(nullptr, RRR_ERR_INVALID_ARG, "null communicator");
@@ -320,7 +385,9 @@ static int comm_launch(rrr_comm* c, const float* in, float* out, int64_t n, int 
   // Large all-reduces from 4 ranks up take two trips (mode 2): each rank then writes about
   // 2n tagged words instead of world * n, which pays once the saved bytes outweigh the
   // second NVLink trip (n * (world - 2) * 8 bytes >= 2 MB, e.g. 64 tokens x 3072 at 8 ranks)
-  if (mode == 0 && c->world >= 4 && n * (c->world - 2) * 8 >= (int64_t)(2 << 20)) {
+  const int forced = two_trip_setting();
+  if (mode == 0 && c->world >= 2 &&
+      (forced == 1 || (forced != 0 && c->world >= 4 && n * (c->world - 2) * 8 >= (int64_t)(2 << 20)))) {
     mode = 2;
     npr = (n + c->world - 1) / c->world;
   }
@@ -331,9 +398,19 @@ static int comm_launch(rrr_comm* c, const float* in, float* out, int64_t n, int 
   chunk = (chunk + 3) / 4 * 4;
   const int ctas = kMaxCtas;
   const LaunchEnv env = make_env(c->ctx, stream);
-  cudaError_t e = rrr_launch_pdl(exchange_kernel, dim3(ctas), dim3(kThreadsX), 0, env.stream, env.pdl,
-                                 c->peers, in, out, n, chunk, c->rank, c->world, c->max_elems,
-                                 c->counters, mode, npr, env.d_err);
+  cudaError_t e;
+  switch (c->world) {
+#define RRR_EXCHANGE(W)                                                                          \
+  case W:                                                                                        \
+    e = rrr_launch_pdl(exchange_kernel<W>, dim3(ctas), dim3(kThreadsX), 0, env.stream, env.pdl,  \
+                       c->peers, in, out, n, chunk, c->rank, c->max_elems, c->counters, mode, npr, \
+                       env.d_err);                                                               \
+    break;
+    RRR_EXCHANGE(1) RRR_EXCHANGE(2) RRR_EXCHANGE(3) RRR_EXCHANGE(4)
+    RRR_EXCHANGE(5) RRR_EXCHANGE(6) RRR_EXCHANGE(7) RRR_EXCHANGE(8)
+#undef RRR_EXCHANGE
+    default: e = cudaErrorInvalidValue;
+  }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(c->ctx, e, what);
   return RRR_OK;

@@ -288,11 +288,12 @@ def test_tp_fused_exchange_bits_equal_unfused(world, max_seq):
 
 
 # ------------------------------------------------------------------ exchange kernels
-def _exchange_rank(rank, world, port, q):
-    import ctypes
+def _exchange_rank(rank, world, port, q, two_trip):
     import datetime
     import torch
     import torch.distributed as dist
+    if two_trip is not None:
+        os.environ["RRR_COMM_TWO_TRIP"] = two_trip
     rrr = importlib.import_module("recursive-routing-racer-rs_b200")
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -333,12 +334,13 @@ def _exchange_rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [4, 8])
-def test_comm_allreduce_two_trips_bits(world):
+@pytest.mark.parametrize("world,two_trip", [(2, None), (2, "1"), (4, None), (8, None)])
+def test_comm_allreduce_two_trips_bits(world, two_trip):
     """The peer-memory all-reduce at 64 tokens x 3072 (two trips from 4 ranks: each rank's
     slice summed by its owner in rank order, the sums sent back) gives every rank the bits
     of the rank-order f32 sum, as the one-trip form does for small exchanges, across calls
-    of different sizes and an all-gather in between."""
+    of different sizes and an all-gather in between. At 2 ranks once as built (one trip
+    throughout) and once with RRR_COMM_TWO_TRIP=1 (two trips for every all-reduce)."""
     import torch
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -346,7 +348,7 @@ def test_comm_allreduce_two_trips_bits(world):
     mpc = mp.get_context("spawn")
     q = mpc.Queue()
     port = _free_port()
-    procs = [mpc.Process(target=_exchange_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [mpc.Process(target=_exchange_rank, args=(r, world, port, q, two_trip)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
