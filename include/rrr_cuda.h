@@ -454,7 +454,8 @@ int rrr_phi4_destroy(rrr_phi4* m);
  * receiver waiting on the words themselves; no NCCL), capturable in CUDA graphs:
  *   all-reduce: x[i] = sum over ranks in rank order (identical bits on every rank; from
  *     4 ranks, exchanges of n * (world - 2) * 8 >= 2 MB bytes take two trips: each slice
- *     summed by its owner rank, the sums sent back),
+ *     summed by its owner rank, the sums sent back; the environment variable
+ *     RRR_COMM_TWO_TRIP=1 / 0 forces two trips for every all-reduce / for none),
  *   all-gather: out[r*n + i] = rank r's part[i] (part may be out + rank*n).
  * Every rank must issue the same sequence of calls with the same n <= max_elems. A wait
  * that exceeds about a second records an error in the context's device flag. */
