@@ -72,3 +72,64 @@ def test_each_awaited_word_written_once(world, n, form):
             for i in range(n):
                 owner = i // npr
                 assert (owner == r) != (got[(r, i)] == 1), (r, i)
+
+
+# ---------------------------------------------------------------- epochs across calls
+MAX_CTAS = 64  # kMaxCtas in csrc/comm_p2p.cu
+
+
+def _chunk(span):
+    """Elements per CTA (comm_launch): about 2 KB per rank, at most MAX_CTAS CTAs."""
+    c = max(512, (span + MAX_CTAS - 1) // MAX_CTAS)
+    return (c + 3) // 4 * 4
+
+
+def _cta_of(kind, n, world):
+    """Element index -> CTA of one call: the one-trip forms map by index, the two-trip
+    form by position inside the slice."""
+    if kind == "two_trips":
+        npr = (n + world - 1) // world
+        c = _chunk(npr)
+        return lambda i: (i % npr) // c
+    c = _chunk(n)
+    return lambda i: i // c
+
+
+def _sets_per_call(calls, world, all_ctas):
+    """For each call, element index -> slot set (epoch parity) its words use, with every
+    call running all MAX_CTAS CTAs (all_ctas) or only the CTAs that hold data."""
+    counters = [0] * MAX_CTAS
+    out = []
+    for kind, n in calls:
+        cta = _cta_of(kind, n, world)
+        used = {cta(i) for i in range(n)}
+        epoch = {c: counters[c] + 1 for c in range(MAX_CTAS)}
+        out.append({i: epoch[cta(i)] & 1 for i in range(n)})
+        for c in range(MAX_CTAS):
+            if all_ctas or c in used:
+                counters[c] += 1
+    return out
+
+
+# the batched decode step's exchanges at 8 ranks: all-reduces of 64 x 3072 (two trips), a
+# one-trip exchange of 3072, the logits all-gather rows (64 x 25008 per rank)
+STEP = [("two_trips", 64 * 3072), ("two_trips", 64 * 3072), ("one_trip", 3072),
+        ("one_trip", 64 * 25008), ("two_trips", 64 * 3072), ("one_trip", 3072)]
+
+
+def _alternates(sets):
+    for a, b in zip(sets, sets[1:]):
+        for i in a.keys() & b.keys():
+            if a[i] == b[i]:
+                return False
+    return True
+
+
+def test_consecutive_calls_use_different_slot_sets():
+    """A rank may be one call ahead of another, so consecutive calls must write every
+    word they share into different slot sets (the reader of the older call would see the
+    newer epoch and wait until its limit). Running all CTAs in every call advances every
+    CTA's epoch together, which keeps that however calls of different sizes map elements
+    to CTAs; running only the CTAs that hold data does not."""
+    assert _alternates(_sets_per_call(STEP, 8, all_ctas=True))
+    assert not _alternates(_sets_per_call(STEP, 8, all_ctas=False))
